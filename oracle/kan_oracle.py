@@ -1,0 +1,503 @@
+"""CPU oracle for the fused KAN forward path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py`` (its ``cpu_baseline`` leg and the
+``--impl reference`` arm) may import this module, and only as the checker or as the timed CPU
+baseline.  The product (``metal_kans`` + ``libkan_cuda.so``) never calls it.
+
+It restates, in NumPy, the arithmetic of the reference (Shuril/metal-kans, ``metal_kans`` v0.6.0):
+
+* basis kernels of ``metal_kans/kernels/fused_kan.metal`` (fp32 kernels and their fp16 twins),
+  with the rounding points of each kernel mirrored;
+* the projection ``Y = bias + silu(x) W_base^T + Phi W^T`` that the bridge runs as two MPS GEMMs
+  (``metal_kans/kernels/metal_kan_bridge.mm:443-530``).  The MPS accumulation order is not
+  published, so this oracle accumulates in float64 and rounds once to the output dtype;
+* the host C++ quantisers/dequantisers of the bridge (``metal_kan_bridge.mm:4177-4302``,
+  ``:4634-4682``, ``:4735-4788``) and the GPU dequantisers (``fused_kan.metal:2392-2441``),
+  bit-exactly, plus the NumPy fallbacks of ``metal_kans/quantization.py`` (``semantics="numpy"``).
+
+Pinning: the quantisers are pinned bit-exactly against the reference's own NumPy code paths run
+in this container (``tests/golden/make_goldens.py``).  The layer classes of the reference were
+driven end to end by a NumPy stand-in for its Metal bridge (``oracle/fake_bridge.py``) to produce
+the golden layer outputs; the Metal basis kernels and MPS GEMM themselves cannot run off macOS,
+so the basis/projection arithmetic is a restatement, not a re-execution ("parity partially
+pinned").
+
+Dtype conventions: ``"f32"`` mirrors the fp32 kernels (basis math evaluated exactly, in float64);
+``"f16"`` mirrors the ``*_fp16`` kernels (half arithmetic where the reference uses half,
+fp32 math + half store where it stores half); ``"bf16"`` (new, no reference counterpart) rounds x
+to bf16, evaluates the basis exactly and rounds it to bf16.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+try:  # bf16 rounding for the bf16 mode
+    import ml_dtypes
+
+    BF16 = np.dtype(ml_dtypes.bfloat16)
+except Exception:  # pragma: no cover
+    ml_dtypes = None
+    BF16 = None
+
+F16 = np.dtype(np.float16)
+F32 = np.dtype(np.float32)
+
+ACT_DTYPES = {"f32": F32, "f16": F16}
+if BF16 is not None:
+    ACT_DTYPES["bf16"] = BF16
+
+
+def act_dtype(mode: str) -> np.dtype:
+    return ACT_DTYPES[mode]
+
+
+def _h(a):
+    """Round to IEEE half (round-to-nearest-even)."""
+    return np.asarray(a).astype(np.float16)
+
+
+def _round_mode(a64: np.ndarray, mode: str) -> np.ndarray:
+    """Round exact (float64) basis values to the operand dtype of ``mode``."""
+    if mode == "f32":
+        return a64
+    if mode == "f16":
+        return a64.astype(np.float32).astype(np.float16).astype(np.float64)
+    return a64.astype(np.float32).astype(BF16).astype(np.float64)
+
+
+def to_mode(x, mode: str) -> np.ndarray:
+    """Round an array to the activation dtype of ``mode`` (x is rounded before any math)."""
+    return np.asarray(x, dtype=np.float32).astype(act_dtype(mode))
+
+
+# --------------------------------------------------------------------------------------------
+# Input maps (new pre-ops: tanh for the ChebyKAN config, LayerNorm for the FastKAN config)
+# --------------------------------------------------------------------------------------------
+
+def layernorm(x: np.ndarray, eps: float = 1e-5) -> np.ndarray:
+    """Row LayerNorm without affine parameters, statistics in float64 (population variance).
+
+    No reference counterpart: the FastKAN benchmark config asks for an input LayerNorm that
+    the reference lacks.  Returned in float64; callers round to the activation dtype.
+    """
+    x64 = np.asarray(x, dtype=np.float64)
+    mu = x64.mean(axis=-1, keepdims=True)
+    var = ((x64 - mu) ** 2).mean(axis=-1, keepdims=True)
+    return (x64 - mu) / np.sqrt(var + eps)
+
+
+def apply_input_map(x_act: np.ndarray, input_map: str, mode: str) -> np.ndarray:
+    """Apply the pre-op to the activation-dtype input; result is rounded back to the act dtype
+    (the kernel hands the mapped value to the basis in the activation dtype)."""
+    if input_map in ("none", "clamp", None):
+        return x_act
+    if input_map == "tanh":
+        y = np.tanh(x_act.astype(np.float64))
+    elif input_map == "layernorm":
+        y = layernorm(x_act)
+    else:
+        raise ValueError(input_map)
+    return y.astype(np.float32).astype(act_dtype(mode)) if mode != "f32" else y.astype(np.float32)
+
+
+# --------------------------------------------------------------------------------------------
+# Base branch: SiLU on the raw input
+# --------------------------------------------------------------------------------------------
+
+def silu(x_act: np.ndarray, mode: str) -> np.ndarray:
+    """SiLU column values, float64.
+
+    fp32: ``x / (1 + exp2(-log2e x))`` (``fused_kan.metal:116-138``) -> exact math.
+    fp16: ``x / (1.0h + exp(-x))`` in half arithmetic (``fused_kan.metal:1373-1397``):
+          three half roundings (exp, add, divide).
+    bf16: exact math rounded to bf16.
+    """
+    if mode == "f16":
+        xh = x_act.astype(np.float16)
+        e = _h(np.exp(-xh.astype(np.float64)))
+        d = _h(np.float64(1.0) + e.astype(np.float64))
+        return _h(xh.astype(np.float64) / d.astype(np.float64)).astype(np.float64)
+    x64 = x_act.astype(np.float64)
+    return _round_mode(x64 / (1.0 + np.exp(-x64)), mode)
+
+
+# --------------------------------------------------------------------------------------------
+# Bases.  Each returns Phi[B, D_in*K] (float64, already rounded to the operand dtype), column
+# i*K + k, which is the column order of the reference weight matrices (cheby_kan.py:40).
+# --------------------------------------------------------------------------------------------
+
+def cheby_basis(x_act: np.ndarray, K: int, mode: str) -> np.ndarray:
+    """Chebyshev T_0..T_{K-1} of clamp(x, -1, 1).
+
+    ``fused_kan.metal:205-238`` (fp32: recurrence 2x T1 - T0) and ``:1399-1426`` (fp16: fp32
+    recurrence with fma, result stored as half).  ``K`` counts terms (the reference's
+    ``degree``).  fp32 mode evaluates the recurrence exactly in float64.
+    """
+    xc = np.clip(x_act.astype(np.float64), -1.0, 1.0)
+    B, D = xc.shape
+    out = np.empty((B, D, K), np.float64)
+    if mode == "f16":
+        # fp32 recurrence t2 = fma(2x, t1, -t0): the float64 evaluation of a*b+c is exact for
+        # fp32 inputs up to the final rounding, which is then done to fp32.
+        x32 = xc.astype(np.float32)
+        t0 = np.ones_like(x32)
+        t1 = x32
+        out[..., 0] = 1.0
+        if K > 1:
+            out[..., 1] = t1
+        x2 = (np.float32(2.0) * x32).astype(np.float64)
+        for k in range(2, K):
+            t2 = (x2 * t1.astype(np.float64) - t0.astype(np.float64)).astype(np.float32)
+            out[..., k] = t2
+            t0, t1 = t1, t2
+        return out.reshape(B, D * K).astype(np.float16).astype(np.float64)
+    t0 = np.ones_like(xc)
+    t1 = xc
+    out[..., 0] = 1.0
+    if K > 1:
+        out[..., 1] = xc
+    for k in range(2, K):
+        t2 = 2.0 * xc * t1 - t0
+        out[..., k] = t2
+        t0, t1 = t1, t2
+    return _round_mode(out.reshape(B, D * K), mode)
+
+
+def rbf_basis(x_act: np.ndarray, grid: np.ndarray, inv_den: float, mode: str) -> np.ndarray:
+    """Gaussian RBF exp(-(x - c_k)^2 * inv_den).
+
+    fp32: ``fused_kan.metal:140-166`` (exp2 of -log2e * d^2 * inv_d) -> exact math.
+    fp16: ``fused_kan.metal:1428-1450`` -- half arithmetic: diff = x - grid[k] (half),
+    -diff*diff (half), * half(inv_den) (half), exp in half (value rounded to half).
+    """
+    B, D = x_act.shape
+    K = grid.shape[0]
+    if mode == "f16":
+        xh = x_act.astype(np.float16).astype(np.float64)[:, :, None]
+        gh = np.asarray(grid).astype(np.float16).astype(np.float64)[None, None, :]
+        inv_h = np.float64(np.float16(inv_den))
+        diff = _h(xh - gh).astype(np.float64)
+        sq = _h(-diff * diff).astype(np.float64)
+        t = _h(sq * inv_h).astype(np.float64)
+        return _h(np.exp(t)).astype(np.float64).reshape(B, D * K)
+    x64 = x_act.astype(np.float64)[:, :, None]
+    g64 = np.asarray(grid, dtype=np.float32).astype(np.float64)[None, None, :]
+    d = x64 - g64
+    inv32 = np.float64(np.float32(inv_den))
+    return _round_mode(np.exp(-(d * d) * inv32).reshape(B, D * K), mode)
+
+
+def bspline_basis(x_act: np.ndarray, grid_size: int, grid_min: float, inv_h: float,
+                  mode: str) -> np.ndarray:
+    """Closed-form uniform cubic B-spline, ``num_bases = G + 3`` per feature.
+
+    ``fused_kan.metal:240-276`` (fp32) / ``:1476-1512`` (fp16: same fp32 math, half store):
+    pos = (x - min) * inv_h (fp32), span = clamp(floor(pos), 0, G-1), u = clamp(pos - span, 0, 1),
+    the four cubic weights land on columns span..span+3.  Outside [min, max] the clamp evaluates
+    the edge polynomial at u in {0, 1}.
+    """
+    B, D = x_act.shape
+    G = int(grid_size)
+    nb = G + 3
+    x32 = x_act.astype(np.float32)
+    pos = ((x32 - np.float32(grid_min)) * np.float32(inv_h)).astype(np.float32)
+    span = np.clip(np.floor(pos), 0, G - 1).astype(np.int64)
+    u = np.clip(pos.astype(np.float64) - span, 0.0, 1.0)
+    om = 1.0 - u
+    b0 = om ** 3 / 6.0
+    b1 = (3.0 * u ** 3 - 6.0 * u ** 2 + 4.0) / 6.0
+    b2 = (-3.0 * u ** 3 + 3.0 * u ** 2 + 3.0 * u + 1.0) / 6.0
+    b3 = u ** 3 / 6.0
+    out = np.zeros((B, D, nb), np.float64)
+    bi, di = np.meshgrid(np.arange(B), np.arange(D), indexing="ij")
+    for j, bj in enumerate((b0, b1, b2, b3)):
+        out[bi, di, span + j] = bj
+    return _round_mode(out.reshape(B, D * nb), mode)
+
+
+def wavelet_basis(x_act: np.ndarray, translation: np.ndarray, inv_scale: np.ndarray,
+                  wavelet_type: int, mode: str) -> np.ndarray:
+    """Continuous wavelets psi((x - t) * inv_s) per (feature, wavelet).
+
+    fp32 (``fused_kan.metal:168-203``): z = (x - t) * inv_s; e = exp(-z^2/2);
+    mexican hat (1 - z^2) e, morlet cos(5 z) e, dog -z e.
+    fp16 (``fused_kan.metal:1514-1548``): every step in half arithmetic, and the Morlet
+    frequency is 1.75 instead of 5 (a quirk of the reference's half kernel, mirrored).
+    """
+    B, D = x_act.shape
+    W = translation.shape[1]
+    if mode == "f16":
+        xh = x_act.astype(np.float16).astype(np.float64)[:, :, None]
+        tr = np.asarray(translation).astype(np.float16).astype(np.float64)[None]
+        sc = np.asarray(inv_scale).astype(np.float16).astype(np.float64)[None]
+        z = _h(_h(xh - tr).astype(np.float64) * sc).astype(np.float64)
+        # exp(-0.5h * z * z): ((-0.5 * z) * z) left to right, then exp, all in half
+        a = _h(_h(-0.5 * z).astype(np.float64) * z).astype(np.float64)
+        e = _h(np.exp(a)).astype(np.float64)
+        if wavelet_type == 0:
+            zz = _h(z * z).astype(np.float64)
+            psi = _h(_h(1.0 - zz).astype(np.float64) * e)
+        elif wavelet_type == 1:
+            c = _h(np.cos(_h(1.75 * z).astype(np.float64))).astype(np.float64)
+            psi = _h(c * e)
+        else:
+            psi = _h(_h(-z).astype(np.float64) * e)
+        return psi.astype(np.float64).reshape(B, D * W)
+    x64 = x_act.astype(np.float64)[:, :, None]
+    tr = np.asarray(translation, np.float32).astype(np.float64)[None]
+    sc = np.asarray(inv_scale, np.float32).astype(np.float64)[None]
+    z = (x64 - tr) * sc
+    e = np.exp(-0.5 * z * z)
+    if wavelet_type == 0:
+        psi = (1.0 - z * z) * e
+    elif wavelet_type == 1:
+        psi = np.cos(5.0 * z) * e
+    else:
+        psi = -z * e
+    return _round_mode(psi.reshape(B, D * W), mode)
+
+
+# --------------------------------------------------------------------------------------------
+# Projection
+# --------------------------------------------------------------------------------------------
+
+def _w64(w, mode):
+    """Weights as float64 after rounding to the operand dtype of ``mode``."""
+    w = np.asarray(w)
+    if mode == "f32":
+        return w.astype(np.float32).astype(np.float64)
+    return w.astype(np.float32).astype(act_dtype(mode)).astype(np.float64)
+
+
+def project(phi64: np.ndarray, W, x_base64, W_base, bias, mode: str,
+            out_round: bool = True) -> np.ndarray:
+    """Y = bias + silu(x) W_base^T + Phi W^T, accumulated in float64 and rounded once.
+
+    Stand-in for the two MPS GEMMs of ``metal_kan_bridge.mm:489-523`` (accumulation order and
+    precision of MPS are not published).
+    """
+    y = phi64 @ _w64(W, mode).T
+    if x_base64 is not None:
+        y = y + x_base64 @ _w64(W_base, mode).T
+    if bias is not None:
+        y = y + _w64(bias, mode)[None, :]
+    if not out_round:
+        return y
+    return y.astype(np.float32).astype(act_dtype(mode)) if mode != "f32" else y.astype(np.float32)
+
+
+def kan_layer(x, basis: str, mode: str, W, W_base=None, bias=None, *, K=None, grid=None,
+              inv_den=None, grid_size=None, grid_min=None, inv_h=None, translation=None,
+              inv_scale=None, wavelet_type=0, input_map="none", out_round=True):
+    """One KAN layer forward (reference call stack A of the bridge, any basis).
+
+    ``x`` is rounded to the activation dtype first (the reference casts x to the weight dtype,
+    ``cheby_kan.py:97-101``).  The input map (tanh / layernorm) feeds the basis; SiLU of the
+    base branch sees the same mapped value.
+    """
+    xa = to_mode(x, mode) if mode != "f32" else np.asarray(x, np.float32)
+    xm = apply_input_map(xa, input_map, mode)
+    if basis == "cheby":
+        phi = cheby_basis(xm, K, mode)
+    elif basis == "rbf":
+        phi = rbf_basis(xm, np.asarray(grid), inv_den, mode)
+    elif basis == "bspline":
+        phi = bspline_basis(xm, grid_size, grid_min, inv_h, mode)
+    elif basis == "wavelet":
+        phi = wavelet_basis(xm, translation, inv_scale, wavelet_type, mode)
+    else:
+        raise ValueError(basis)
+    xb = silu(xm, mode) if W_base is not None else None
+    return project(phi, W, xb, W_base, bias, mode, out_round=out_round)
+
+
+def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """hidden = g * sigmoid(clamp(g, -20, 20)) * u (``fused_kan.metal:2284-2296``), float64."""
+    g = np.asarray(gate, np.float64)
+    u = np.asarray(up, np.float64)
+    sig = 1.0 / (1.0 + np.exp(-np.clip(g, -20.0, 20.0)))
+    return g * sig * u
+
+
+# --------------------------------------------------------------------------------------------
+# Quantisers (reference bridge C++ semantics by default; "numpy" mirrors quantization.py)
+# --------------------------------------------------------------------------------------------
+
+def _pad_rows(w: np.ndarray, gs: int) -> np.ndarray:
+    """Pad each row with zeros to a multiple of the group size (quantization.py:24-29)."""
+    w = np.asarray(w, np.float32)
+    pad = (gs - (w.shape[1] % gs)) % gs
+    if pad:
+        w = np.pad(w, ((0, 0), (0, pad)))
+    return np.ascontiguousarray(w, np.float32)
+
+
+def quantize_affine(w: np.ndarray, bits: int, gs: int, semantics: str = "bridge"):
+    """INT8/INT4 block-affine quantiser on a [D_out, K_dim] matrix.
+
+    Returns ``(qweight, scales, biases, padded_in)`` in the reference layout: ``qweight`` is
+    [num_groups, gs] (INT8) or [num_groups, gs/2] (INT4, byte = q[2i] | q[2i+1] << 4); scales and
+    biases are [num_groups, 1] float32; groups are consecutive ``gs`` elements of the row-padded
+    matrix.
+
+    ``semantics="bridge"`` follows ``metal_kan_bridge.mm:4177-4211`` / ``:4234-4275`` evaluated
+    with one IEEE fp32 rounding per source operation: s = max(max-min, 1e-7f) / (2^b-1),
+    q = (int)((w - min) * (1/s) + 0.5f) clamped.  ``"numpy"`` follows the fallback of
+    ``quantization.py:73-97``: q = round_half_even((w - min) / s).
+    """
+    padded = _pad_rows(w, gs)
+    g = padded.reshape(-1, gs)
+    mn = g.min(axis=1, keepdims=True)
+    mx = g.max(axis=1, keepdims=True)
+    rng = np.maximum((mx - mn).astype(np.float32), np.float32(1e-7))
+    maxq = (1 << bits) - 1
+    s = (rng / np.float32(maxq)).astype(np.float32)
+    if semantics == "bridge":
+        inv = (np.float32(1.0) / s).astype(np.float32)
+        v = (((g - mn).astype(np.float32) * inv).astype(np.float32) + np.float32(0.5)).astype(np.float32)
+        q = v.astype(np.int32)
+    else:
+        q = np.round(((g - mn).astype(np.float32) / s).astype(np.float32)).astype(np.int32)
+    q = np.clip(q, 0, maxq)
+    if bits == 8:
+        qw = q.astype(np.uint8)
+    elif bits == 4:
+        qw = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+    else:
+        raise ValueError(bits)
+    return qw, s.astype(np.float32), mn.astype(np.float32), padded.shape[1]
+
+
+def dequantize_affine(qweight: np.ndarray, scales: np.ndarray, biases: np.ndarray, bits: int,
+                      gs: int) -> np.ndarray:
+    """q * s + b as a separate fp32 multiply and add per element (``metal_kan_bridge.mm:4213``,
+    ``:4278``; ``quantization.py:136-146``).  Returns [num_groups, gs] float32."""
+    if bits == 8:
+        q = qweight.astype(np.float32)
+    else:
+        q = np.empty((qweight.shape[0], gs), np.float32)
+        q[:, 0::2] = qweight & 0x0F
+        q[:, 1::2] = (qweight >> 4) & 0x0F
+    s = np.asarray(scales, np.float32).reshape(-1, 1)
+    b = np.asarray(biases, np.float32).reshape(-1, 1)
+    return ((q * s).astype(np.float32) + b).astype(np.float32)
+
+
+def dequantize_affine_matrix(qweight, scales, biases, bits, gs, shape, padded_in):
+    """Dequantise back to the [D_out, K_dim] matrix (padding columns dropped)."""
+    full = dequantize_affine(qweight, scales, biases, bits, gs).reshape(-1, padded_in)
+    return np.ascontiguousarray(full[: shape[0], : shape[1]])
+
+
+def _pack2(codes: np.ndarray) -> np.ndarray:
+    """Pack 2-bit codes [D_out, K_dim] into uint32 words: element k at bits 2*(k%16) of word k/16."""
+    D, Kd = codes.shape
+    words = (Kd + 15) // 16
+    c = np.zeros((D, words * 16), np.uint32)
+    c[:, :Kd] = codes
+    c = c.reshape(D, words, 16)
+    shifts = (np.arange(16, dtype=np.uint32) * 2)[None, None, :]
+    return np.bitwise_or.reduce(c << shifts, axis=2).astype(np.uint32)
+
+
+def unpack2(packed: np.ndarray, K_dim: int) -> np.ndarray:
+    """Inverse of :func:`_pack2`."""
+    D, words = packed.shape
+    shifts = (np.arange(16, dtype=np.uint32) * 2)[None, None, :]
+    c = (packed[:, :, None] >> shifts) & 0x3
+    return c.reshape(D, words * 16)[:, :K_dim].astype(np.uint32)
+
+
+def _group_view(w: np.ndarray, gs: int):
+    """Per-row groups with ragged last group: returns (padded [D, G, gs], valid mask, counts)."""
+    D, Kd = w.shape
+    G = (Kd + gs - 1) // gs
+    pad = np.zeros((D, G * gs), np.float32)
+    pad[:, :Kd] = w
+    mask = np.zeros((G * gs,), bool)
+    mask[:Kd] = True
+    counts = np.array([min(gs, Kd - gi * gs) for gi in range(G)], np.int64)
+    return pad.reshape(D, G, gs), mask.reshape(G, gs), counts
+
+
+def quantize_ternary(w: np.ndarray, gs: int, semantics: str = "bridge"):
+    """Ternary quantiser: codes 0:-1, 1:0, 2:+1 with per-(row, group) scale = mean|w|.
+
+    ``"bridge"``: ``metal_kan_bridge.mm:4634-4682`` -- sum |w| sequentially in double, scale =
+    (float)(sum/count) (1e-4f if zero), val = w * (1/scale).  ``"numpy"``:
+    ``quantization.py:231-246`` -- float32 ``np.mean``, val = w / scale.
+    Returns (w_packed [D_out, ceil(K_dim/16)] uint32, scales [D_out, ceil(K_dim/gs)] float32).
+    """
+    w = np.ascontiguousarray(w, np.float32)
+    D, Kd = w.shape
+    gv, mask, counts = _group_view(w, gs)
+    if semantics == "bridge":
+        a = np.abs(gv.astype(np.float64)) * mask[None]
+        ssum = np.add.accumulate(a, axis=2)[:, :, -1]
+        sc = np.where(ssum > 0.0, (ssum / counts[None, :]), 1e-4).astype(np.float32)
+        sc = np.where(ssum > 0.0, sc, np.float32(1e-4)).astype(np.float32)
+        inv = (np.float32(1.0) / sc).astype(np.float32)
+        val = (gv * inv[:, :, None]).astype(np.float32)
+    else:
+        sc = np.empty((D, gv.shape[1]), np.float32)
+        for gi in range(gv.shape[1]):
+            sl = np.abs(gv[:, gi, : counts[gi]])
+            m = np.mean(sl, axis=1)  # float32 pairwise mean, as np.mean(np.abs(slice_w))
+            sc[:, gi] = np.where(m > 0, m, np.float32(1e-4))
+        val = (gv / sc[:, :, None]).astype(np.float32)
+    codes = np.where(val < -0.5, 0, np.where(val > 0.5, 2, 1)).astype(np.uint32)
+    codes = codes.reshape(D, -1)[:, :Kd]
+    return _pack2(codes), sc.astype(np.float32)
+
+
+def quantize_int2(w: np.ndarray, gs: int, codebook=None, semantics: str = "bridge"):
+    """2-bit codebook quantiser: per-(row, group) scale = max|w|, code = first argmin
+    |w/scale - codebook[c]| (``metal_kan_bridge.mm:4735-4788``; numpy fallback
+    ``quantization.py:336-352`` divides instead of multiplying by the reciprocal)."""
+    if codebook is None:
+        codebook = np.array([-1.0, -0.33333, 0.33333, 1.0], np.float32)
+    cb = np.asarray(codebook, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    D, Kd = w.shape
+    gv, mask, counts = _group_view(w, gs)
+    mx = np.max(np.abs(gv) * mask[None], axis=2)
+    sc = np.where(mx > 0, mx, np.float32(1e-4)).astype(np.float32)
+    if semantics == "bridge":
+        inv = (np.float32(1.0) / sc).astype(np.float32)
+        val = (gv * inv[:, :, None]).astype(np.float32)
+    else:
+        val = (gv / sc[:, :, None]).astype(np.float32)
+    dist = np.abs(val[..., None] - cb[None, None, None, :]).astype(np.float32)
+    codes = np.argmin(dist, axis=-1).astype(np.uint32).reshape(D, -1)[:, :Kd]
+    return _pack2(codes), sc.astype(np.float32)
+
+
+def dequantize_ternary(packed: np.ndarray, scales: np.ndarray, K_dim: int, gs: int) -> np.ndarray:
+    """(code - 1) * scale, code 3 -> 0 (``fused_kan.metal:2392-2416``), float32 [D_out, K_dim]."""
+    codes = unpack2(packed, K_dim)
+    wv = np.where(codes == 3, 0.0, codes.astype(np.float32) - 1.0).astype(np.float32)
+    gidx = np.arange(K_dim) // gs
+    return (wv * np.asarray(scales, np.float32)[:, gidx]).astype(np.float32)
+
+
+def dequantize_int2(packed: np.ndarray, scales: np.ndarray, codebook: np.ndarray, K_dim: int,
+                    gs: int) -> np.ndarray:
+    """codebook[code] * scale (``fused_kan.metal:2418-2441``), float32 [D_out, K_dim]."""
+    codes = unpack2(packed, K_dim)
+    cb = np.asarray(codebook, np.float32)
+    gidx = np.arange(K_dim) // gs
+    return (cb[codes] * np.asarray(scales, np.float32)[:, gidx]).astype(np.float32)
+
+
+# --------------------------------------------------------------------------------------------
+# Error metric
+# --------------------------------------------------------------------------------------------
+
+def max_rel_err(y, y_ref) -> float:
+    """max |y - y_ref| / max |y_ref| over the whole output tensor."""
+    y = np.asarray(y, np.float64)
+    r = np.asarray(y_ref, np.float64)
+    den = np.max(np.abs(r))
+    if den == 0:
+        return float(np.max(np.abs(y)))
+    return float(np.max(np.abs(y - r)) / den)

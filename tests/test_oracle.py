@@ -1,0 +1,177 @@
+"""CPU: the oracle against the golden fixtures made from the reference's own Python code."""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import REPO, group, load_npz
+from oracle import kan_oracle as O
+
+LAYERS = load_npz("layers_small.npz")
+QUANT = load_npz("quant_reference_numpy.npz")
+BLOCKS = load_npz("blocks_small.npz")
+
+
+def _cases():
+    return sorted({k.split("/")[0] for k in LAYERS})
+
+
+def oracle_layer_from_golden(rec, mode):
+    """Call the oracle with the parameters a reference layer golden recorded."""
+    hb = int(rec["meta_has_base"])
+    hbi = int(rec["meta_has_bias"])
+    kw = {}
+    if "w_cheby" in rec:
+        basis, W, K = "cheby", rec["w_cheby"], int(rec["meta_degree"])
+    elif "w_rbf" in rec:
+        basis, W, K = "rbf", rec["w_rbf"], int(rec["meta_num_centers"])
+        kw = dict(grid=rec["grid"], inv_den=float(rec["meta_inv_denominator"]))
+    elif "w_spline" in rec:
+        G = int(rec["meta_grid_size"])
+        basis, W, K = "bspline", rec["w_spline"], G + 3
+        kw = dict(grid_size=G, grid_min=float(rec["grid"][0]), inv_h=float(rec["grid"][1]))
+    else:
+        basis, W, K = "wavelet", rec["w_wav"], int(rec["meta_num_wavelets"])
+        kw = dict(translation=rec["translation"], inv_scale=rec["inv_scale"],
+                  wavelet_type=int(rec["meta_wavelet_type"]))
+    return O.kan_layer(rec["x"], basis, mode, W, rec["w_base"] if hb else None,
+                       rec["bias"] if hbi else None, K=K, **kw)
+
+
+@pytest.mark.parametrize("case", _cases())
+def test_layer_goldens_reproduce(case):
+    rec = group(LAYERS, case)
+    mode = case.rsplit("_", 1)[1]
+    y = oracle_layer_from_golden(rec, mode)
+    assert y.dtype == rec["y"].dtype
+    np.testing.assert_array_equal(y, rec["y"])
+
+
+def test_fp16_vs_fp32_reference_tolerance():
+    """The reference's own pin: fp16 forward within atol 1e-2 of fp32 (test_metal_kans.py:257)."""
+    for case in _cases():
+        # Morlet is excluded: the reference's half kernel uses cos(1.75 z), its fp32 kernel
+        # cos(5 z) (fused_kan.metal:1541 vs :184), and its own fp16 test only covers Mexican hat.
+        if not case.endswith("_f32") or "morlet" in case:
+            continue
+        r32 = group(LAYERS, case)
+        r16 = group(LAYERS, case[:-4] + "_f16")
+        np.testing.assert_allclose(r16["y"].astype(np.float32), r32["y"], atol=1e-2)
+
+
+def test_c1_golden():
+    z = load_npz("c1_cheby_f32.npz")
+    y = O.kan_layer(z["x"], "cheby", "f32", z["w_cheby"], K=9, input_map="tanh")
+    assert O.max_rel_err(y, z["y"]) < 1e-6
+
+
+def _c_oracle():
+    so = os.path.join(REPO, "oracle", "_build", "libquant_oracle.so")
+    if not os.path.exists(so):
+        subprocess.run(["make", "-C", os.path.join(REPO, "oracle")], check=True,
+                       capture_output=True)
+    return ctypes.CDLL(so)
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_affine_numpy_semantics_bit_exact(bits):
+    for tag in ("n01_32x64_g32", "ragged_12x100_g64", "const_4x64_g64"):
+        r = group(QUANT, f"aff{bits}_{tag}")
+        gs = int(r["gs"])
+        qw, s, b, pin = O.quantize_affine(r["w"], bits, gs, semantics="numpy")
+        np.testing.assert_array_equal(qw, r["qweight"])
+        np.testing.assert_array_equal(s, r["scales"])
+        np.testing.assert_array_equal(b, r["biases"])
+        deq = O.dequantize_affine_matrix(r["qweight"], r["scales"], r["biases"], bits, gs,
+                                         r["w"].shape, pin)
+        np.testing.assert_array_equal(deq, r["deq"])
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_affine_bridge_semantics_vs_c_oracle(bits):
+    lib = _c_oracle()
+    rng = np.random.default_rng(bits)
+    for shape, gs in (((64, 576), 64), ((33, 100), 32), ((5, 128), 128)):
+        w = rng.normal(0, 0.02, shape).astype(np.float32)
+        qw, s, b, pin = O.quantize_affine(w, bits, gs, "bridge")
+        padded = O._pad_rows(w, gs)
+        G = padded.size // gs
+        cq = np.empty_like(qw)
+        cs = np.empty((G,), np.float32)
+        cb = np.empty((G,), np.float32)
+        assert lib.oracle_quantize_affine(_p(padded), _p(cq), _p(cs), _p(cb), G, gs, bits) == 0
+        np.testing.assert_array_equal(cq, qw)
+        np.testing.assert_array_equal(cs, s.ravel())
+        np.testing.assert_array_equal(cb, b.ravel())
+        out = np.empty((G, gs), np.float32)
+        assert lib.oracle_dequantize_affine(_p(cq), _p(cs), _p(cb), _p(out), G, gs, bits) == 0
+        np.testing.assert_array_equal(out, O.dequantize_affine(qw, s, b, bits, gs))
+        # bridge vs numpy rounding differ only where (w-min)/s sits on a rounding boundary
+        qn, _, _, _ = O.quantize_affine(w, bits, gs, "numpy")
+        assert np.mean(qn != qw) < 1e-3
+
+
+def test_ternary_int2_numpy_semantics_bit_exact():
+    for tag in ("n_8x72_g32", "n_6x100_g64", "zeros_2x40_g16"):
+        r = group(QUANT, f"tern_{tag}")
+        gs = int(r["gs"])
+        p, s = O.quantize_ternary(r["w"], gs, "numpy")
+        np.testing.assert_array_equal(p, r["packed"])
+        np.testing.assert_array_equal(s, r["scales"])
+        np.testing.assert_array_equal(O.dequantize_ternary(r["packed"], r["scales"],
+                                                           r["w"].shape[1], gs), r["deq"])
+        r = group(QUANT, f"int2_{tag}")
+        p, s = O.quantize_int2(r["w"], gs, r["codebook"], "numpy")
+        np.testing.assert_array_equal(p, r["packed"])
+        np.testing.assert_array_equal(s, r["scales"])
+        np.testing.assert_array_equal(O.dequantize_int2(r["packed"], r["scales"], r["codebook"],
+                                                        r["w"].shape[1], gs), r["deq"])
+
+
+def test_ternary_int2_bridge_semantics_vs_c_oracle():
+    lib = _c_oracle()
+    rng = np.random.default_rng(3)
+    cbk = np.array([-1.0, -0.33333, 0.33333, 1.0], np.float32)
+    for shape, gs in (((16, 576), 64), ((7, 100), 32), ((3, 37), 16)):
+        w = rng.normal(0, 0.03, shape).astype(np.float32)
+        D, Kd = shape
+        words, G = (Kd + 15) // 16, (Kd + gs - 1) // gs
+        p, s = O.quantize_ternary(w, gs, "bridge")
+        cp = np.empty((D, words), np.uint32)
+        cs = np.empty((D, G), np.float32)
+        assert lib.oracle_quantize_ternary(_p(w), _p(cp), _p(cs), D, Kd, gs) == 0
+        np.testing.assert_array_equal(cp, p)
+        np.testing.assert_array_equal(cs, s)
+        out = np.empty((D, Kd), np.float32)
+        assert lib.oracle_dequantize_2bit(_p(cp), _p(cs), None, _p(out), D, Kd, gs) == 0
+        np.testing.assert_array_equal(out, O.dequantize_ternary(p, s, Kd, gs))
+        p, s = O.quantize_int2(w, gs, cbk, "bridge")
+        assert lib.oracle_quantize_int2(_p(w), _p(cp), _p(cs), _p(cbk), D, Kd, gs) == 0
+        np.testing.assert_array_equal(cp, p)
+        np.testing.assert_array_equal(cs, s)
+        assert lib.oracle_dequantize_2bit(_p(cp), _p(cs), _p(cbk), _p(out), D, Kd, gs) == 0
+        np.testing.assert_array_equal(out, O.dequantize_int2(p, s, cbk, Kd, gs))
+
+
+def test_pack_roundtrip():
+    rng = np.random.default_rng(0)
+    codes = rng.integers(0, 4, (5, 53)).astype(np.uint32)
+    np.testing.assert_array_equal(O.unpack2(O._pack2(codes), 53), codes)
+
+
+def test_blocks_gated_int4_dequant_matches_reference():
+    """to_int4 in the reference stores dequantised weights; the oracle reproduces them."""
+    for nm in ("gate_kan", "up_kan", "down_kan"):
+        for attr in ("w_cheby", "w_base"):
+            pre = f"gated_int4/{nm}.{attr}"
+            deq = BLOCKS[pre + ".deq"]
+            pin = BLOCKS[pre + ".qweight"].shape[0] * 64 // deq.shape[0]
+            got = O.dequantize_affine_matrix(BLOCKS[pre + ".qweight"], BLOCKS[pre + ".scales"],
+                                             BLOCKS[pre + ".biases"], 4, 64, deq.shape, pin)
+            np.testing.assert_array_equal(got, deq)
