@@ -1,0 +1,261 @@
+/*
+ * kan_cuda.h -- C ABI of libkan_cuda.so, the B200 (sm_100a) KAN inference engine.
+ *
+ * Two tiers:
+ *
+ *  1. Reference-compatible entry points.  Same names, argument order and meaning as the
+ *     `extern "C"` functions of the reference bridge (Shuril/metal-kans,
+ *     metal_kans/kernels/metal_kan_bridge.mm), which its ctypes loader binds in
+ *     metal_kans/device.py:64-474.  All pointers are HOST pointers (C-contiguous, owned by the
+ *     caller); fp16 arrays are passed as uint16_t.  Every operand is staged to the device, the
+ *     result is copied back, and the call returns 0 on success or a negative status.  Unlike the
+ *     reference, failures are never silent: a non-zero status comes with kan_last_error().
+ *
+ *  2. Device-resident entry points (new, prefix kan_).  Pointers are DEVICE pointers; work is
+ *     enqueued on the given cudaStream_t (passed as void*, NULL = the library's stream of the
+ *     current device) and the call returns without synchronising.
+ *
+ * Status codes are the KAN_ERR_* values below.  Nothing here falls back to a CPU path: without a
+ * CUDA device every compute entry point returns KAN_ERR_NO_DEVICE.
+ */
+#ifndef KAN_CUDA_H_
+#define KAN_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------------------ */
+/* status                                                                                      */
+/* ------------------------------------------------------------------------------------------ */
+#define KAN_OK 0
+#define KAN_ERR_ARG (-1)           /* bad pointer / size / enum                                 */
+#define KAN_ERR_CUDA (-2)          /* a CUDA runtime/driver call failed                         */
+#define KAN_ERR_UNSUPPORTED (-3)   /* valid request with no kernel for it                       */
+#define KAN_ERR_NO_DEVICE (-4)     /* no CUDA device visible                                    */
+#define KAN_ERR_DEVICE_TIMEOUT (-5)/* a kernel's bounded wait expired (kan_device_error())      */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* kan_last_error(void);
+/* ABI version (major*100 + minor). */
+int kan_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* tier 1: reference-compatible, host pointers                                                */
+/* ------------------------------------------------------------------------------------------ */
+
+/* metal_kan_bridge.mm:289 metal_kan_init(const char* shader_path): the path is ignored (there is
+ * no runtime shader compilation); initialises the current CUDA device. */
+int metal_kan_init(const char* shader_path);
+/* metal_kan_bridge.mm:275 / :280 -- async mode: forwards enqueue and return; metal_kan_sync()
+ * waits and completes the pending host copies. */
+int metal_kan_set_async(int enabled);
+int metal_kan_sync(void);
+
+/* metal_kan_bridge.mm:443 */
+int metal_kan_cheby_forward(const float* X, const float* W_cheby, const float* W_base,
+                            const float* bias, float* Y, int B, int D_in, int D_out, int K,
+                            int has_base, int has_bias);
+/* metal_kan_bridge.mm:1890 */
+int metal_kan_cheby_forward_fp16(const uint16_t* X, const uint16_t* W_cheby,
+                                 const uint16_t* W_base, const uint16_t* bias, uint16_t* Y, int B,
+                                 int D_in, int D_out, int K, int has_base, int has_bias);
+/* metal_kan_bridge.mm:532 */
+int metal_kan_fastkan_forward(const float* X, const float* W_rbf, const float* W_base,
+                              const float* grid, const float* bias, float* Y, int B, int D_in,
+                              int D_out, int num_centers, float inv_denominator, int has_base,
+                              int has_bias);
+/* metal_kan_bridge.mm:1973 (grid is fp16 here, like the reference) */
+int metal_kan_fastkan_forward_fp16(const uint16_t* X, const uint16_t* W_rbf,
+                                   const uint16_t* W_base, const uint16_t* grid,
+                                   const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                   int num_centers, float inv_denominator, int has_base,
+                                   int has_bias);
+/* metal_kan_bridge.mm:1069 (grid = {grid_min, inv_h}, float32; spline_order is ignored: the
+ * reference evaluates closed-form uniform cubics whatever the order) */
+int metal_kan_bspline_forward(const float* X, const float* W_spline, const float* W_base,
+                              const float* grid, const float* bias, float* Y, int B, int D_in,
+                              int D_out, int grid_size, int spline_order, int has_base,
+                              int has_bias);
+/* metal_kan_bridge.mm:2062 (grid stays float32, like the reference) */
+int metal_kan_bspline_forward_fp16(const uint16_t* X, const uint16_t* W_spline,
+                                   const uint16_t* W_base, const float* grid,
+                                   const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                   int grid_size, int spline_order, int has_base, int has_bias);
+/* metal_kan_bridge.mm:722 (wavelet_type 0 mexican hat, 1 morlet, 2 dog) */
+int metal_kan_wavkan_forward(const float* X, const float* W_wav, const float* W_base,
+                             const float* translation, const float* inv_scale, const float* bias,
+                             float* Y, int B, int D_in, int D_out, int num_wavelets,
+                             int wavelet_type, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2448 */
+int metal_kan_wavkan_forward_fp16(const uint16_t* X, const uint16_t* W_wav,
+                                  const uint16_t* W_base, const uint16_t* translation,
+                                  const uint16_t* inv_scale, const uint16_t* bias, uint16_t* Y,
+                                  int B, int D_in, int D_out, int num_wavelets, int wavelet_type,
+                                  int has_base, int has_bias);
+/* metal_kan_bridge.mm:1168 -- unlike the reference (which hard-codes 4 terms), degrees[] is
+ * honoured per layer.  W_bases[l] / biases[l] may be NULL (no base / no bias for that layer). */
+int metal_kan_chain_pipeline_cheby(const float* X, float* Y, int B, int num_layers,
+                                   const int* layer_dims, const int* degrees,
+                                   const float** W_chebys, const float** W_bases,
+                                   const float** biases);
+/* metal_kan_bridge.mm:4846 -- out = g * sigmoid(clamp(g, -20, 20)) * u */
+int metal_kan_swiglu_forward(const float* gate, const float* up, float* out, int n_elems);
+
+/* Host quantisers (metal_kan_bridge.mm:4177, :4234, :4634, :4735) and dequantisers (:4213,
+ * :4278, :5073, :5109).  Bit-exact with the source text evaluated with one IEEE fp32 rounding per
+ * operation.  Layouts: INT8 q[groups][gs]; INT4 q[groups][gs/2] (lo nibble = even element);
+ * 2-bit P[D_out][ceil(K_dim/16)] (element k at bits 2*(k%16) of word k/16), scales
+ * [D_out][ceil(K_dim/gs)]. */
+int metal_kan_quantize_int8(const float* weights, uint8_t* qweight, float* scales, float* biases,
+                            int num_groups, int group_size);
+int metal_kan_quantize_int4(const float* weights, uint8_t* qweight, float* scales, float* biases,
+                            int num_groups, int group_size);
+int metal_kan_dequantize_int8(const uint8_t* qweight, const float* scales, const float* biases,
+                              float* weights, int num_groups, int group_size);
+int metal_kan_dequantize_int4(const uint8_t* qweight, const float* scales, const float* biases,
+                              float* weights, int num_groups, int group_size);
+int metal_kan_quantize_ternary(const float* W, uint32_t* W_packed, float* scales, int D_out,
+                               int K_dim, int group_size);
+int metal_kan_quantize_int2(const float* W, uint32_t* W_packed, float* scales,
+                            const float* codebook, int D_out, int K_dim, int group_size);
+/* These two run on the GPU, like the reference's dequantize_*_fast kernels. */
+int metal_kan_dequantize_ternary(const uint32_t* packed, const float* scales, float* out,
+                                 int D_out, int K_dim, int group_size);
+int metal_kan_dequantize_int2(const uint32_t* packed, const float* scales, const float* codebook,
+                              float* out, int D_out, int K_dim, int group_size);
+
+/* metal_kan_bridge.mm:4684 / :4790 -- packed-weight ChebyKAN forward (no base branch), fp32.
+ * degree = number of terms. */
+int metal_kan_forward_ternary_cheby(const float* X, const uint32_t* W_packed, const float* scales,
+                                    const float* bias, float* Y, int B, int D_in, int D_out,
+                                    int degree, int group_size, int has_bias);
+int metal_kan_forward_int2_cheby(const float* X, const uint32_t* W_packed, const float* scales,
+                                 const float* codebook, const float* bias, float* Y, int B,
+                                 int D_in, int D_out, int degree, int group_size, int has_bias);
+
+/* metal_kan_bridge.mm:1250-1371 -- mean milliseconds per full host-pointer forward (stage +
+ * kernel + copy back), after `warmup` untimed calls; negative on error. */
+double benchmark_metal_cheby(const float* X, const float* W_cheby, const float* W_base,
+                             const float* bias, float* Y, int B, int D_in, int D_out, int K,
+                             int has_base, int has_bias, int warmup, int iters);
+double benchmark_metal_fastkan(const float* X, const float* W_rbf, const float* W_base,
+                               const float* grid, const float* bias, float* Y, int B, int D_in,
+                               int D_out, int num_centers, float inv_denominator, int has_base,
+                               int has_bias, int warmup, int iters);
+double benchmark_metal_bspline(const float* X, const float* W_spline, const float* W_base,
+                               const float* grid, const float* bias, float* Y, int B, int D_in,
+                               int D_out, int grid_size, int spline_order, int has_base,
+                               int has_bias, int warmup, int iters);
+double benchmark_metal_wavkan(const float* X, const float* W_wav, const float* W_base,
+                              const float* translation, const float* inv_scale, const float* bias,
+                              float* Y, int B, int D_in, int D_out, int num_wavelets,
+                              int wavelet_type, int has_base, int has_bias, int warmup, int iters);
+
+/* ------------------------------------------------------------------------------------------ */
+/* tier 2: device-resident engine (new)                                                       */
+/* ------------------------------------------------------------------------------------------ */
+
+enum kan_dtype { KAN_F32 = 0, KAN_F16 = 1, KAN_BF16 = 2 };
+enum kan_basis { KAN_CHEBY = 0, KAN_RBF = 1, KAN_BSPLINE = 2, KAN_WAVELET = 3 };
+enum kan_input_map { KAN_MAP_NONE = 0, KAN_MAP_TANH = 1, KAN_MAP_LAYERNORM = 2 };
+enum kan_wformat {
+  KAN_W_DENSE = 0,   /* act-dtype matrix [rows][cols]                                          */
+  KAN_W_INT8 = 1,    /* u8 [rows*padded_cols/gs][gs], fp32 scales/biases per group             */
+  KAN_W_INT4 = 2,    /* u8 [rows*padded_cols/gs][gs/2]                                          */
+  KAN_W_TERNARY = 3, /* u32 [rows][ceil(cols/16)], fp32 scales [rows][ceil(cols/gs)]           */
+  KAN_W_INT2 = 4     /* as ternary + fp32 codebook[4]                                          */
+};
+/* Kernel selection for kan_forward (KAN_PATH_AUTO picks by shape and batch). */
+enum kan_path { KAN_PATH_AUTO = 0, KAN_PATH_SIMT = 1, KAN_PATH_TC = 2, KAN_PATH_GEMV = 3 };
+
+/* One weight matrix with `rows` = D_out and `cols` = D_in*K (basis) or D_in (base branch). */
+typedef struct kan_weight {
+  int32_t format;       /* enum kan_wformat */
+  int32_t group_size;   /* quantised formats */
+  int32_t padded_cols;  /* INT8/INT4: cols rounded up to a multiple of group_size */
+  int32_t reserved;
+  const void* data;     /* device pointer */
+  const float* scales;  /* device pointer or NULL */
+  const float* biases;  /* device pointer or NULL (INT8/INT4 group minimum) */
+  const float* codebook;/* device pointer or NULL (INT2) */
+  const void* dense;    /* optional: the same matrix already dequantised to the act dtype
+                         * (device pointer).  Packed formats run the tensor-core path from it;
+                         * the small-batch and SIMT paths decode the packed data. */
+} kan_weight;
+
+/* One KAN layer: y[b, j] = bias[j] + sum_i silu(m(x))[b,i] Wb[j,i]
+ *                              + sum_i sum_k phi_k(m(x)[b,i]) W[j, i*K + k]
+ * with m the input map.  All pointers are device pointers.  Basis parameters (grid,
+ * translation, inv_scale) are float32 whatever the activation dtype; the fp16 mode rounds them
+ * to half exactly where the reference's half kernels use half values. */
+typedef struct kan_layer {
+  int32_t basis;        /* enum kan_basis */
+  int32_t act_dtype;    /* enum kan_dtype: X, Y, bias and dense weights */
+  int32_t D_in, D_out;
+  int32_t K;            /* basis terms per input feature (BSpline: grid_size + 3) */
+  int32_t has_base, has_bias;
+  int32_t input_map;    /* enum kan_input_map */
+  int32_t wavelet_type; /* 0 mexican hat, 1 morlet, 2 dog */
+  int32_t grid_size;    /* BSpline G */
+  float inv_den;        /* RBF: exp(-(x-c)^2 * inv_den) */
+  float grid_min, inv_h;/* BSpline */
+  float ln_eps;         /* LayerNorm epsilon */
+  const float* grid;    /* RBF centres [K] */
+  const float* translation; /* wavelet [D_in][K] */
+  const float* inv_scale;   /* wavelet [D_in][K] */
+  const void* bias;     /* [D_out], act dtype */
+  kan_weight w;         /* basis weights [D_out][D_in*K] */
+  kan_weight wb;        /* base weights [D_out][D_in] */
+} kan_layer;
+
+/* Enqueue one layer forward: X [B][D_in] -> Y [B][D_out] (act dtype). */
+int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* stream);
+/* Same with an explicit kernel path (tests, benchmarks). */
+int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int path,
+                     void* stream);
+
+/* GatedKAN block: H = silu(gate(X)) * up(X) (act dtype, [B][D_ffn]); Y = down(H).  H is caller
+ * memory ([B][gate.D_out] elements of the act dtype). */
+int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
+                      const void* X, void* H, void* Y, int B, void* stream);
+
+/* Dequantise any weight format to a dense matrix of `out_dtype` ([rows][cols]); the fp32 value
+ * is bit-identical to the reference dequantiser, then rounded (RNE) for f16/bf16 outputs. */
+int kan_dequantize(const kan_weight* w, int rows, int cols, void* out, int out_dtype,
+                   void* stream);
+/* Elementwise: out = g * sigmoid(clamp(g,-20,20)) * u, dtype act_dtype, n elements. */
+int kan_swiglu(const void* gate, const void* up, void* out, long long n, int act_dtype,
+               void* stream);
+/* Dtype conversion of n elements (any of KAN_F32/F16/BF16 to any). */
+int kan_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
+                void* stream);
+
+/* Device memory / stream helpers so that callers without a CUDA runtime binding (ctypes users)
+ * can manage buffers.  kind: 1 = host->device, 2 = device->host, 3 = device->device. */
+int kan_device_count(int* count);
+int kan_set_device(int device);
+int kan_get_device(int* device);
+int kan_malloc(void** ptr, size_t bytes);
+int kan_free(void* ptr);
+int kan_host_alloc(void** ptr, size_t bytes); /* pinned host memory */
+int kan_host_free(void* ptr);
+int kan_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream);
+int kan_memset(void* dst, int value, size_t bytes, void* stream);
+int kan_stream_synchronize(void* stream);
+void* kan_default_stream(void);
+
+/* Device-side error word: non-zero when a kernel's bounded wait expired (the kernel then skipped
+ * its remaining work and released its resources).  Reading clears it. */
+int kan_device_error(int* code);
+
+/* Number of kernels this library launched since load (evidence counter for benchmarks). */
+long long kan_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KAN_CUDA_H_ */

@@ -1,0 +1,955 @@
+// kan_abi.cpp -- the C ABI of libkan_cuda.so (declared in include/kan_cuda.h).
+//
+// Host runtime of the engine: per-device state (stream, staging buffers, scratch), kernel
+// dispatch for kan_forward, the reference-compatible host-pointer entry points (the symbols the
+// reference's ctypes loader binds, metal_kans/device.py:64-474), the host quantisers and the
+// memory helpers.  No CPU compute fallback exists: every forward runs a CUDA kernel or fails.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kan_cuda.h"
+#include "kan_launch.h"
+
+namespace kan {
+
+// ------------------------------------------------------------------------------------------
+// errors
+// ------------------------------------------------------------------------------------------
+static thread_local std::string t_err;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+#define KAN_CUDA_TRY(expr)                                                                 \
+  do {                                                                                     \
+    cudaError_t e_ = (expr);                                                               \
+    if (e_ != cudaSuccess)                                                                 \
+      return fail(KAN_ERR_CUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_),   \
+                  __FILE__, __LINE__);                                                     \
+  } while (0)
+
+static std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(); }
+
+// ------------------------------------------------------------------------------------------
+// per-device state
+// ------------------------------------------------------------------------------------------
+constexpr int MAX_DEVICES = 16;
+enum Slot { S_X, S_W, S_WB, S_BIAS, S_Y, S_GRID, S_TRANS, S_ISC, S_SC, S_BI, S_CB, S_T0, S_T1,
+            NUM_SLOTS };
+
+struct PendingCopy {
+  void* pinned;
+  void* user;
+  size_t bytes;
+};
+
+struct DeviceState {
+  bool init = false;
+  cudaStream_t stream = nullptr;
+  int* err_word = nullptr;
+  void* slot_ptr[NUM_SLOTS] = {};
+  size_t slot_cap[NUM_SLOTS] = {};
+  std::vector<PendingCopy> pending;     // async-mode results waiting for metal_kan_sync()
+  std::vector<std::pair<void*, size_t>> pinned_free;  // reusable pinned buffers
+};
+
+static DeviceState g_dev[MAX_DEVICES];
+static std::mutex g_mu;
+static thread_local int t_async = 0;
+
+static int current_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+      return fail(KAN_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+    return fail(KAN_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= MAX_DEVICES) return fail(KAN_ERR_ARG, "device index %d too large", dev);
+  DeviceState& d = g_dev[dev];
+  if (!d.init) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!d.init) {
+      KAN_CUDA_TRY(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+      d.err_word = device_error_ptr();
+      if (!d.err_word) return fail(KAN_ERR_CUDA, "device error word unavailable");
+      d.init = true;
+    }
+  }
+  *out = &d;
+  return KAN_OK;
+}
+
+static int slot(DeviceState* d, int s, size_t bytes, void** out) {
+  if (bytes == 0) bytes = 16;
+  if (d->slot_cap[s] < bytes) {
+    if (d->slot_ptr[s]) {
+      cudaStreamSynchronize(d->stream);
+      cudaFree(d->slot_ptr[s]);
+      d->slot_ptr[s] = nullptr;
+      d->slot_cap[s] = 0;
+    }
+    size_t cap = std::max<size_t>(bytes, 4096);
+    KAN_CUDA_TRY(cudaMalloc(&d->slot_ptr[s], cap));
+    d->slot_cap[s] = cap;
+  }
+  *out = d->slot_ptr[s];
+  return KAN_OK;
+}
+
+static int stage_in(DeviceState* d, int s, const void* host, size_t bytes, void** dev) {
+  int rc = slot(d, s, bytes, dev);
+  if (rc) return rc;
+  if (host && bytes) KAN_CUDA_TRY(cudaMemcpyAsync(*dev, host, bytes, cudaMemcpyHostToDevice, d->stream));
+  return KAN_OK;
+}
+
+static int check_device_error(DeviceState* d) {
+  int v = 0;
+  KAN_CUDA_TRY(cudaMemcpy(&v, d->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    int z = 0;
+    cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice);
+    return fail(KAN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
+  }
+  return KAN_OK;
+}
+
+// Copy the result back: synchronously, or (async mode) into pinned memory completed by sync().
+static int stage_out(DeviceState* d, void* host, const void* dev, size_t bytes) {
+  if (!t_async) {
+    KAN_CUDA_TRY(cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, d->stream));
+    KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+    return check_device_error(d);
+  }
+  void* pin = nullptr;
+  for (size_t i = 0; i < d->pinned_free.size(); ++i) {
+    if (d->pinned_free[i].second >= bytes) {
+      pin = d->pinned_free[i].first;
+      d->pinned_free.erase(d->pinned_free.begin() + i);
+      break;
+    }
+  }
+  if (!pin) KAN_CUDA_TRY(cudaHostAlloc(&pin, std::max<size_t>(bytes, 4096), cudaHostAllocDefault));
+  KAN_CUDA_TRY(cudaMemcpyAsync(pin, dev, bytes, cudaMemcpyDeviceToHost, d->stream));
+  d->pending.push_back({pin, host, std::max<size_t>(bytes, 4096)});
+  d->pending.back().bytes = bytes;
+  return KAN_OK;
+}
+
+static int sync_pending(DeviceState* d) {
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  for (auto& p : d->pending) {
+    std::memcpy(p.user, p.pinned, p.bytes);
+    d->pinned_free.push_back({p.pinned, std::max<size_t>(p.bytes, 4096)});
+  }
+  d->pending.clear();
+  return check_device_error(d);
+}
+
+// ------------------------------------------------------------------------------------------
+// validation + dispatch
+// ------------------------------------------------------------------------------------------
+static size_t dtype_size(int dt) { return dt == KAN_F32 ? 4 : 2; }
+
+static int validate_weight(const kan_weight& w, const char* name, int act_dtype) {
+  switch (w.format) {
+    case KAN_W_DENSE:
+      if (!w.data) return fail(KAN_ERR_ARG, "%s: dense weight pointer is NULL", name);
+      return KAN_OK;
+    case KAN_W_INT8:
+    case KAN_W_INT4:
+      if (!w.data || !w.scales || !w.biases || w.group_size <= 0 || w.padded_cols <= 0 ||
+          (w.format == KAN_W_INT4 && (w.group_size & 1)))
+        return fail(KAN_ERR_ARG, "%s: incomplete INT8/INT4 weight", name);
+      return KAN_OK;
+    case KAN_W_TERNARY:
+    case KAN_W_INT2:
+      if (!w.data || !w.scales || w.group_size <= 0 ||
+          (w.format == KAN_W_INT2 && !w.codebook))
+        return fail(KAN_ERR_ARG, "%s: incomplete 2-bit weight", name);
+      return KAN_OK;
+    default:
+      return fail(KAN_ERR_ARG, "%s: unknown weight format %d", name, w.format);
+  }
+  (void)act_dtype;
+}
+
+static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceState* d,
+                     LayerArgs* a) {
+  if (!L) return fail(KAN_ERR_ARG, "layer descriptor is NULL");
+  if (B < 0) return fail(KAN_ERR_ARG, "B = %d", B);
+  if (L->D_in <= 0 || L->D_out <= 0 || L->K <= 0)
+    return fail(KAN_ERR_ARG, "bad layer dims D_in=%d D_out=%d K=%d", L->D_in, L->D_out, L->K);
+  if (L->K > 64) return fail(KAN_ERR_UNSUPPORTED, "K=%d terms per feature (max 64)", L->K);
+  if (L->act_dtype < KAN_F32 || L->act_dtype > KAN_BF16)
+    return fail(KAN_ERR_ARG, "act_dtype %d", L->act_dtype);
+  if (L->basis < KAN_CHEBY || L->basis > KAN_WAVELET) return fail(KAN_ERR_ARG, "basis %d", L->basis);
+  if (B > 0 && (!X || !Y)) return fail(KAN_ERR_ARG, "X or Y is NULL");
+  if (L->basis == KAN_RBF && !L->grid) return fail(KAN_ERR_ARG, "RBF layer without grid");
+  if (L->basis == KAN_WAVELET && (!L->translation || !L->inv_scale))
+    return fail(KAN_ERR_ARG, "wavelet layer without translation/inv_scale");
+  if (L->basis == KAN_BSPLINE && (L->grid_size <= 0 || L->K != L->grid_size + 3))
+    return fail(KAN_ERR_ARG, "BSpline layer needs K = grid_size + 3 (K=%d G=%d)", L->K,
+                L->grid_size);
+  if (L->has_bias && !L->bias) return fail(KAN_ERR_ARG, "has_bias without bias pointer");
+  int rc = validate_weight(L->w, "w", L->act_dtype);
+  if (rc) return rc;
+  if (L->has_base) {
+    rc = validate_weight(L->wb, "wb", L->act_dtype);
+    if (rc) return rc;
+  }
+  std::memset(a, 0, sizeof(*a));
+  a->basis = L->basis;
+  a->act_dtype = L->act_dtype;
+  a->B = B;
+  a->D_in = L->D_in;
+  a->D_out = L->D_out;
+  a->K = L->K;
+  a->has_base = L->has_base ? 1 : 0;
+  a->has_bias = L->has_bias ? 1 : 0;
+  a->input_map = L->input_map;
+  a->wavelet_type = L->wavelet_type;
+  a->grid_size = L->grid_size;
+  a->inv_den = L->inv_den;
+  a->grid_min = L->grid_min;
+  a->inv_h = L->inv_h;
+  a->ln_eps = L->ln_eps > 0.f ? L->ln_eps : 1e-5f;
+  a->grid = L->grid;
+  a->translation = L->translation;
+  a->inv_scale = L->inv_scale;
+  a->X = X;
+  a->Y = Y;
+  a->bias = L->bias;
+  a->w = L->w;
+  a->wb = L->wb;
+  a->err = d->err_word;
+  return KAN_OK;
+}
+
+static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int path,
+                       cudaStream_t s, DeviceState* d) {
+  LayerArgs a;
+  int rc = make_args(L, X, Y, B, d, &a);
+  if (rc) return rc;
+  if (B == 0) return KAN_OK;
+  cudaError_t e;
+  if (path == KAN_PATH_AUTO) {
+    path = (L->act_dtype != KAN_F32 && tc_supported(a, L->act_dtype)) ? KAN_PATH_TC
+                                                                        : KAN_PATH_SIMT;
+  }
+  if (path == KAN_PATH_TC) {
+    if (!tc_supported(a, L->act_dtype))
+      return fail(KAN_ERR_UNSUPPORTED,
+                  "tensor-core path needs f16/bf16, K<=64, D_in*K %% 8 == 0 (and D_in %% 8 == 0 "
+                  "with a base branch), 16-byte aligned dense weights");
+    e = launch_tc(a, L->act_dtype, s);
+  } else if (path == KAN_PATH_SIMT || path == KAN_PATH_GEMV) {
+    e = launch_simt(a, L->act_dtype, s);
+  } else {
+    return fail(KAN_ERR_ARG, "unknown path %d", path);
+  }
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+static cudaStream_t pick_stream(void* s, DeviceState* d) {
+  return s ? (cudaStream_t)s : d->stream;
+}
+
+}  // namespace kan
+
+using namespace kan;
+
+// ==========================================================================================
+// tier 2: device-resident engine
+// ==========================================================================================
+extern "C" {
+
+const char* kan_last_error(void) { return t_err.c_str(); }
+int kan_abi_version(void) { return 100; }
+long long kan_launch_count(void) { return launch_count(); }
+
+int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int path,
+                     void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  return run_forward(layer, X, Y, B, path, pick_stream(stream, d), d);
+}
+
+int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* stream) {
+  return kan_forward_path(layer, X, Y, B, KAN_PATH_AUTO, stream);
+}
+
+int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
+                      const void* X, void* H, void* Y, int B, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!gate || !up || !down || !H) return fail(KAN_ERR_ARG, "gated: NULL argument");
+  if (gate->D_out != up->D_out || down->D_in != gate->D_out || gate->D_in != up->D_in ||
+      gate->act_dtype != up->act_dtype || down->act_dtype != gate->act_dtype)
+    return fail(KAN_ERR_ARG, "gated: inconsistent gate/up/down shapes or dtypes");
+  cudaStream_t s = pick_stream(stream, d);
+  const size_t esz = dtype_size(gate->act_dtype);
+  const size_t n = (size_t)B * gate->D_out;
+  void *g, *u;
+  rc = slot(d, S_T0, n * esz, &g);
+  if (rc) return rc;
+  rc = slot(d, S_T1, n * esz, &u);
+  if (rc) return rc;
+  if ((rc = run_forward(gate, X, g, B, KAN_PATH_AUTO, s, d))) return rc;
+  if ((rc = run_forward(up, X, u, B, KAN_PATH_AUTO, s, d))) return rc;
+  cudaError_t e = launch_swiglu(g, u, H, (long long)n, gate->act_dtype, s);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu launch: %s", cudaGetErrorString(e));
+  return run_forward(down, H, Y, B, KAN_PATH_AUTO, s, d);
+}
+
+int kan_dequantize(const kan_weight* w, int rows, int cols, void* out, int out_dtype,
+                   void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!w || !out || rows <= 0 || cols <= 0) return fail(KAN_ERR_ARG, "dequantize: bad args");
+  if ((rc = validate_weight(*w, "w", out_dtype))) return rc;
+  if (w->format == KAN_W_DENSE) return fail(KAN_ERR_ARG, "dequantize: weight is already dense");
+  cudaError_t e = launch_dequantize(*w, rows, cols, out, out_dtype, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "dequantize launch: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_swiglu(const void* gate, const void* up, void* out, long long n, int act_dtype,
+               void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (!gate || !up || !out))) return fail(KAN_ERR_ARG, "swiglu: bad args");
+  if (n == 0) return KAN_OK;
+  cudaError_t e = launch_swiglu(gate, up, out, n, act_dtype, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu launch: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
+                void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (!src || !dst))) return fail(KAN_ERR_ARG, "convert: bad args");
+  if (n == 0) return KAN_OK;
+  cudaError_t e = launch_convert(src, src_dtype, dst, dst_dtype, n, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "convert launch: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_device_count(int* count) {
+  if (!count) return fail(KAN_ERR_ARG, "NULL");
+  cudaError_t e = cudaGetDeviceCount(count);
+  if (e != cudaSuccess) {
+    *count = 0;
+    return fail(KAN_ERR_NO_DEVICE, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+  }
+  return KAN_OK;
+}
+int kan_set_device(int device) {
+  KAN_CUDA_TRY(cudaSetDevice(device));
+  return KAN_OK;
+}
+int kan_get_device(int* device) {
+  if (!device) return fail(KAN_ERR_ARG, "NULL");
+  KAN_CUDA_TRY(cudaGetDevice(device));
+  return KAN_OK;
+}
+int kan_malloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(KAN_ERR_ARG, "NULL");
+  KAN_CUDA_TRY(cudaMalloc(ptr, bytes ? bytes : 16));
+  return KAN_OK;
+}
+int kan_free(void* ptr) {
+  if (ptr) KAN_CUDA_TRY(cudaFree(ptr));
+  return KAN_OK;
+}
+int kan_host_alloc(void** ptr, size_t bytes) {
+  if (!ptr) return fail(KAN_ERR_ARG, "NULL");
+  KAN_CUDA_TRY(cudaHostAlloc(ptr, bytes ? bytes : 16, cudaHostAllocDefault));
+  return KAN_OK;
+}
+int kan_host_free(void* ptr) {
+  if (ptr) KAN_CUDA_TRY(cudaFreeHost(ptr));
+  return KAN_OK;
+}
+int kan_memcpy(void* dst, const void* src, size_t bytes, int kind, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (bytes == 0) return KAN_OK;
+  if (!dst || !src) return fail(KAN_ERR_ARG, "memcpy: NULL pointer");
+  cudaMemcpyKind k = kind == 1 ? cudaMemcpyHostToDevice
+                     : kind == 2 ? cudaMemcpyDeviceToHost
+                                 : cudaMemcpyDeviceToDevice;
+  KAN_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, k, pick_stream(stream, d)));
+  return KAN_OK;
+}
+int kan_memset(void* dst, int value, size_t bytes, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (bytes == 0) return KAN_OK;
+  KAN_CUDA_TRY(cudaMemsetAsync(dst, value, bytes, pick_stream(stream, d)));
+  return KAN_OK;
+}
+int kan_stream_synchronize(void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  KAN_CUDA_TRY(cudaStreamSynchronize(pick_stream(stream, d)));
+  return KAN_OK;
+}
+void* kan_default_stream(void) {
+  DeviceState* d;
+  if (current_state(&d)) return nullptr;
+  return (void*)d->stream;
+}
+int kan_device_error(int* code) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  int v = 0;
+  KAN_CUDA_TRY(cudaMemcpy(&v, d->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    int z = 0;
+    KAN_CUDA_TRY(cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  if (code) *code = v;
+  return KAN_OK;
+}
+
+// ==========================================================================================
+// tier 1: reference-compatible host-pointer entry points
+// ==========================================================================================
+
+int metal_kan_init(const char* shader_path) {
+  (void)shader_path;
+  DeviceState* d;
+  return current_state(&d);
+}
+
+int metal_kan_set_async(int enabled) {
+  if (!enabled && t_async) {
+    t_async = 0;
+    return metal_kan_sync();
+  }
+  t_async = enabled ? 1 : 0;
+  return KAN_OK;
+}
+
+int metal_kan_sync(void) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  return sync_pending(d);
+}
+
+}  // extern "C"
+
+namespace kan {
+
+// Stage a host-pointer layer call, run it, copy Y back.
+struct HostLayer {
+  kan_layer L;
+  const void* X;
+  void* Y;
+  int B;
+  // host sources for the dense operands
+  const void* hW = nullptr;
+  const void* hWb = nullptr;
+  const void* hBias = nullptr;
+  std::vector<float> grid, trans, isc;  // basis parameters, already fp32
+};
+
+static int run_host_layer(HostLayer& h) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  kan_layer& L = h.L;
+  if (h.B < 0 || L.D_in <= 0 || L.D_out <= 0) return fail(KAN_ERR_ARG, "bad sizes");
+  if (h.B > 0 && (!h.X || !h.Y || !h.hW)) return fail(KAN_ERR_ARG, "NULL X/Y/W");
+  if (L.has_base && !h.hWb) return fail(KAN_ERR_ARG, "has_base with NULL W_base");
+  if (L.has_bias && !h.hBias) return fail(KAN_ERR_ARG, "has_bias with NULL bias");
+  if (h.B == 0) return KAN_OK;
+  const size_t es = dtype_size(L.act_dtype);
+  void *dX, *dY, *dW, *dWb = nullptr, *dB = nullptr, *dG = nullptr, *dT = nullptr, *dS = nullptr;
+  if ((rc = stage_in(d, S_X, h.X, (size_t)h.B * L.D_in * es, &dX))) return rc;
+  if ((rc = stage_in(d, S_W, h.hW, (size_t)L.D_out * L.D_in * L.K * es, &dW))) return rc;
+  if (L.has_base && (rc = stage_in(d, S_WB, h.hWb, (size_t)L.D_out * L.D_in * es, &dWb))) return rc;
+  if (L.has_bias && (rc = stage_in(d, S_BIAS, h.hBias, (size_t)L.D_out * es, &dB))) return rc;
+  if (!h.grid.empty() && (rc = stage_in(d, S_GRID, h.grid.data(), h.grid.size() * 4, &dG))) return rc;
+  if (!h.trans.empty() && (rc = stage_in(d, S_TRANS, h.trans.data(), h.trans.size() * 4, &dT))) return rc;
+  if (!h.isc.empty() && (rc = stage_in(d, S_ISC, h.isc.data(), h.isc.size() * 4, &dS))) return rc;
+  if ((rc = slot(d, S_Y, (size_t)h.B * L.D_out * es, &dY))) return rc;
+  L.w.format = KAN_W_DENSE;
+  L.w.data = dW;
+  L.wb.format = KAN_W_DENSE;
+  L.wb.data = dWb;
+  L.bias = dB;
+  L.grid = (const float*)dG;
+  L.translation = (const float*)dT;
+  L.inv_scale = (const float*)dS;
+  if ((rc = run_forward(&L, dX, dY, h.B, KAN_PATH_AUTO, d->stream, d))) return rc;
+  return stage_out(d, h.Y, dY, (size_t)h.B * L.D_out * es);
+}
+
+static kan_layer base_layer(int basis, int dt, int D_in, int D_out, int K, int hb, int hbi) {
+  kan_layer L;
+  std::memset(&L, 0, sizeof(L));
+  L.basis = basis;
+  L.act_dtype = dt;
+  L.D_in = D_in;
+  L.D_out = D_out;
+  L.K = K;
+  L.has_base = hb ? 1 : 0;
+  L.has_bias = hbi ? 1 : 0;
+  L.ln_eps = 1e-5f;
+  return L;
+}
+
+static std::vector<float> half_to_float(const uint16_t* p, size_t n) {
+  std::vector<float> v(n);
+  for (size_t i = 0; i < n; ++i) {
+    __half_raw r;
+    r.x = p[i];
+    v[i] = __half2float(__half(r));
+  }
+  return v;
+}
+
+}  // namespace kan
+
+namespace kan {
+// host-timed loop behind benchmark_metal_* (metal_kan_bridge.mm:1250-1371)
+template <class F>
+static double bench_loop(F&& fwd, int warmup, int iters) {
+  if (iters <= 0) {
+    fail(KAN_ERR_ARG, "iters must be > 0");
+    return -1.0;
+  }
+  for (int i = 0; i < warmup; ++i)
+    if (fwd()) return -1.0;
+  auto t0 = std::chrono::steady_clock::now();
+  for (int i = 0; i < iters; ++i)
+    if (fwd()) return -1.0;
+  auto t1 = std::chrono::steady_clock::now();
+  return std::chrono::duration<double, std::milli>(t1 - t0).count() / iters;
+}
+
+}  // namespace kan
+
+extern "C" {
+
+int metal_kan_cheby_forward(const float* X, const float* W, const float* Wb, const float* bias,
+                            float* Y, int B, int D_in, int D_out, int K, int hb, int hbi) {
+  HostLayer h{base_layer(KAN_CHEBY, KAN_F32, D_in, D_out, K, hb, hbi), X, Y, B, W, Wb, bias};
+  return run_host_layer(h);
+}
+
+int metal_kan_cheby_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                 const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                 int K, int hb, int hbi) {
+  HostLayer h{base_layer(KAN_CHEBY, KAN_F16, D_in, D_out, K, hb, hbi), X, Y, B, W, Wb, bias};
+  return run_host_layer(h);
+}
+
+int metal_kan_fastkan_forward(const float* X, const float* W, const float* Wb, const float* grid,
+                              const float* bias, float* Y, int B, int D_in, int D_out, int K,
+                              float inv_den, int hb, int hbi) {
+  if (!grid || K <= 0) return fail(KAN_ERR_ARG, "fastkan: NULL grid");
+  HostLayer h{base_layer(KAN_RBF, KAN_F32, D_in, D_out, K, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.inv_den = inv_den;
+  h.grid.assign(grid, grid + K);
+  return run_host_layer(h);
+}
+
+int metal_kan_fastkan_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                   const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                   int D_in, int D_out, int K, float inv_den, int hb, int hbi) {
+  if (!grid || K <= 0) return fail(KAN_ERR_ARG, "fastkan: NULL grid");
+  HostLayer h{base_layer(KAN_RBF, KAN_F16, D_in, D_out, K, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.inv_den = inv_den;
+  h.grid = half_to_float(grid, K);
+  return run_host_layer(h);
+}
+
+static int bspline_common(int dt, const void* X, const void* W, const void* Wb,
+                          const float* grid, const void* bias, void* Y, int B, int D_in,
+                          int D_out, int G, int hb, int hbi) {
+  if (!grid || G <= 0) return fail(KAN_ERR_ARG, "bspline: NULL grid or grid_size <= 0");
+  HostLayer h{base_layer(KAN_BSPLINE, dt, D_in, D_out, G + 3, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.grid_size = G;
+  h.L.grid_min = grid[0];
+  h.L.inv_h = grid[1];
+  return run_host_layer(h);
+}
+
+int metal_kan_bspline_forward(const float* X, const float* W, const float* Wb, const float* grid,
+                              const float* bias, float* Y, int B, int D_in, int D_out, int G,
+                              int spline_order, int hb, int hbi) {
+  (void)spline_order;
+  return bspline_common(KAN_F32, X, W, Wb, grid, bias, Y, B, D_in, D_out, G, hb, hbi);
+}
+
+int metal_kan_bspline_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                   const float* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                   int D_in, int D_out, int G, int spline_order, int hb,
+                                   int hbi) {
+  (void)spline_order;
+  return bspline_common(KAN_F16, X, W, Wb, grid, bias, Y, B, D_in, D_out, G, hb, hbi);
+}
+
+int metal_kan_wavkan_forward(const float* X, const float* W, const float* Wb, const float* trans,
+                             const float* isc, const float* bias, float* Y, int B, int D_in,
+                             int D_out, int nw, int wtype, int hb, int hbi) {
+  if (!trans || !isc || nw <= 0) return fail(KAN_ERR_ARG, "wavkan: NULL translation/scale");
+  HostLayer h{base_layer(KAN_WAVELET, KAN_F32, D_in, D_out, nw, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.wavelet_type = wtype;
+  h.trans.assign(trans, trans + (size_t)D_in * nw);
+  h.isc.assign(isc, isc + (size_t)D_in * nw);
+  return run_host_layer(h);
+}
+
+int metal_kan_wavkan_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                  const uint16_t* trans, const uint16_t* isc,
+                                  const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                  int nw, int wtype, int hb, int hbi) {
+  if (!trans || !isc || nw <= 0) return fail(KAN_ERR_ARG, "wavkan: NULL translation/scale");
+  HostLayer h{base_layer(KAN_WAVELET, KAN_F16, D_in, D_out, nw, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.wavelet_type = wtype;
+  h.trans = half_to_float(trans, (size_t)D_in * nw);
+  h.isc = half_to_float(isc, (size_t)D_in * nw);
+  return run_host_layer(h);
+}
+
+int metal_kan_chain_pipeline_cheby(const float* X, float* Y, int B, int num_layers,
+                                   const int* dims, const int* degrees, const float** W,
+                                   const float** Wb, const float** bias) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!X || !Y || !dims || !degrees || !W || num_layers <= 0 || B < 0)
+    return fail(KAN_ERR_ARG, "chain: bad arguments");
+  if (B == 0) return KAN_OK;
+  int max_dim = 0;
+  for (int l = 0; l <= num_layers; ++l) {
+    if (dims[l] <= 0) return fail(KAN_ERR_ARG, "chain: dims[%d] = %d", l, dims[l]);
+    max_dim = std::max(max_dim, dims[l]);
+  }
+  // ping-pong activations stay on the device between layers
+  void *act[2], *dW, *dWb, *dB;
+  if ((rc = slot(d, S_T0, (size_t)B * max_dim * 4, &act[0]))) return rc;
+  if ((rc = slot(d, S_T1, (size_t)B * max_dim * 4, &act[1]))) return rc;
+  KAN_CUDA_TRY(cudaMemcpyAsync(act[0], X, (size_t)B * dims[0] * 4, cudaMemcpyHostToDevice, d->stream));
+  int cur = 0;
+  for (int l = 0; l < num_layers; ++l) {
+    const int din = dims[l], dout = dims[l + 1], K = degrees[l];
+    if (K <= 0 || !W[l]) return fail(KAN_ERR_ARG, "chain: layer %d weights/degree", l);
+    const int hb = (Wb && Wb[l]) ? 1 : 0, hbi = (bias && bias[l]) ? 1 : 0;
+    // weights of every layer are staged into distinct slots only one layer at a time, so the
+    // copy for layer l must wait until layer l-1 has consumed the slot: same stream, in order.
+    if ((rc = stage_in(d, S_W, W[l], (size_t)dout * din * K * 4, &dW))) return rc;
+    dWb = nullptr;
+    dB = nullptr;
+    if (hb && (rc = stage_in(d, S_WB, Wb[l], (size_t)dout * din * 4, &dWb))) return rc;
+    if (hbi && (rc = stage_in(d, S_BIAS, bias[l], (size_t)dout * 4, &dB))) return rc;
+    kan_layer L = base_layer(KAN_CHEBY, KAN_F32, din, dout, K, hb, hbi);
+    L.w.format = KAN_W_DENSE;
+    L.w.data = dW;
+    L.wb.format = KAN_W_DENSE;
+    L.wb.data = dWb;
+    L.bias = dB;
+    if ((rc = run_forward(&L, act[cur], act[cur ^ 1], B, KAN_PATH_AUTO, d->stream, d))) return rc;
+    cur ^= 1;
+  }
+  return stage_out(d, Y, act[cur], (size_t)B * dims[num_layers] * 4);
+}
+
+int metal_kan_swiglu_forward(const float* gate, const float* up, float* out, int n) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!gate || !up || !out || n <= 0) return fail(KAN_ERR_ARG, "swiglu: bad arguments");
+  void *g, *u, *o;
+  if ((rc = stage_in(d, S_X, gate, (size_t)n * 4, &g))) return rc;
+  if ((rc = stage_in(d, S_W, up, (size_t)n * 4, &u))) return rc;
+  if ((rc = slot(d, S_Y, (size_t)n * 4, &o))) return rc;
+  cudaError_t e = launch_swiglu(g, u, o, n, KAN_F32, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu: %s", cudaGetErrorString(e));
+  return stage_out(d, out, o, (size_t)n * 4);
+}
+
+// ---------------------------------------------------------------- host quantisers
+// Source-level IEEE fp32 semantics of metal_kan_bridge.mm:4177-4302 / :4634-4682 / :4735-4788:
+// each operation rounds once (this file is compiled with -ffp-contract=off).
+
+int metal_kan_quantize_int8(const float* w, uint8_t* q, float* s, float* b, int groups, int gs) {
+  if (!w || !q || !s || !b || groups <= 0 || gs <= 0)
+    return fail(KAN_ERR_ARG, "quantize_int8: bad arguments");
+  for (int g = 0; g < groups; ++g) {
+    const float* grp = w + (size_t)g * gs;
+    float mn = grp[0], mx = grp[0];
+    for (int i = 1; i < gs; ++i) {
+      mn = grp[i] < mn ? grp[i] : mn;
+      mx = grp[i] > mx ? grp[i] : mx;
+    }
+    float range = std::max(mx - mn, 1e-7f);
+    float scale = range / 255.0f;
+    s[g] = scale;
+    b[g] = mn;
+    float inv = 1.0f / scale;
+    for (int i = 0; i < gs; ++i) {
+      float v = (grp[i] - mn) * inv + 0.5f;
+      int qi = (int)v;
+      q[(size_t)g * gs + i] = (uint8_t)(qi < 0 ? 0 : qi > 255 ? 255 : qi);
+    }
+  }
+  return KAN_OK;
+}
+
+int metal_kan_quantize_int4(const float* w, uint8_t* q, float* s, float* b, int groups, int gs) {
+  if (!w || !q || !s || !b || groups <= 0 || gs <= 0 || (gs & 1))
+    return fail(KAN_ERR_ARG, "quantize_int4: bad arguments");
+  const int half = gs / 2;
+  for (int g = 0; g < groups; ++g) {
+    const float* grp = w + (size_t)g * gs;
+    float mn = grp[0], mx = grp[0];
+    for (int i = 1; i < gs; ++i) {
+      mn = grp[i] < mn ? grp[i] : mn;
+      mx = grp[i] > mx ? grp[i] : mx;
+    }
+    float range = std::max(mx - mn, 1e-7f);
+    float scale = range / 15.0f;
+    s[g] = scale;
+    b[g] = mn;
+    float inv = 1.0f / scale;
+    for (int i = 0; i < half; ++i) {
+      int q0 = (int)((grp[2 * i] - mn) * inv + 0.5f);
+      int q1 = (int)((grp[2 * i + 1] - mn) * inv + 0.5f);
+      q0 = q0 < 0 ? 0 : q0 > 15 ? 15 : q0;
+      q1 = q1 < 0 ? 0 : q1 > 15 ? 15 : q1;
+      q[(size_t)g * half + i] = (uint8_t)(q0 | (q1 << 4));
+    }
+  }
+  return KAN_OK;
+}
+
+int metal_kan_dequantize_int8(const uint8_t* q, const float* s, const float* b, float* out,
+                              int groups, int gs) {
+  if (!q || !s || !b || !out || groups <= 0 || gs <= 0)
+    return fail(KAN_ERR_ARG, "dequantize_int8: bad arguments");
+  for (int g = 0; g < groups; ++g)
+    for (int i = 0; i < gs; ++i) {
+      float m = (float)q[(size_t)g * gs + i] * s[g];
+      out[(size_t)g * gs + i] = m + b[g];
+    }
+  return KAN_OK;
+}
+
+int metal_kan_dequantize_int4(const uint8_t* q, const float* s, const float* b, float* out,
+                              int groups, int gs) {
+  if (!q || !s || !b || !out || groups <= 0 || gs <= 0 || (gs & 1))
+    return fail(KAN_ERR_ARG, "dequantize_int4: bad arguments");
+  const int half = gs / 2;
+  for (int g = 0; g < groups; ++g)
+    for (int i = 0; i < half; ++i) {
+      uint8_t byte = q[(size_t)g * half + i];
+      float m0 = (float)(byte & 0xF) * s[g];
+      float m1 = (float)((byte >> 4) & 0xF) * s[g];
+      out[(size_t)g * gs + 2 * i] = m0 + b[g];
+      out[(size_t)g * gs + 2 * i + 1] = m1 + b[g];
+    }
+  return KAN_OK;
+}
+
+int metal_kan_quantize_ternary(const float* W, uint32_t* P, float* s, int D_out, int K_dim,
+                               int gs) {
+  if (!W || !P || !s || D_out <= 0 || K_dim <= 0 || gs <= 0)
+    return fail(KAN_ERR_ARG, "quantize_ternary: bad arguments");
+  const int words = (K_dim + 15) / 16, G = (K_dim + gs - 1) / gs;
+  std::memset(P, 0, (size_t)D_out * words * sizeof(uint32_t));
+  for (int j = 0; j < D_out; ++j) {
+    const float* row = W + (size_t)j * K_dim;
+    for (int g = 0; g < G; ++g) {
+      const int st = g * gs, en = std::min(st + gs, K_dim), cnt = en - st;
+      double sum = 0.0;
+      for (int k = st; k < en; ++k) sum += std::fabs((double)row[k]);
+      float sc = (cnt > 0 && sum > 0.0) ? (float)(sum / cnt) : 1e-4f;
+      s[(size_t)j * G + g] = sc;
+      float inv = 1.0f / sc;
+      for (int k = st; k < en; ++k) {
+        float v = row[k] * inv;
+        uint32_t c = v < -0.5f ? 0u : (v > 0.5f ? 2u : 1u);
+        P[(size_t)j * words + k / 16] |= c << ((k % 16) * 2);
+      }
+    }
+  }
+  return KAN_OK;
+}
+
+int metal_kan_quantize_int2(const float* W, uint32_t* P, float* s, const float* cb, int D_out,
+                            int K_dim, int gs) {
+  if (!W || !P || !s || !cb || D_out <= 0 || K_dim <= 0 || gs <= 0)
+    return fail(KAN_ERR_ARG, "quantize_int2: bad arguments");
+  const int words = (K_dim + 15) / 16, G = (K_dim + gs - 1) / gs;
+  std::memset(P, 0, (size_t)D_out * words * sizeof(uint32_t));
+  for (int j = 0; j < D_out; ++j) {
+    const float* row = W + (size_t)j * K_dim;
+    for (int g = 0; g < G; ++g) {
+      const int st = g * gs, en = std::min(st + gs, K_dim);
+      float mx = 0.0f;
+      for (int k = st; k < en; ++k) mx = std::max(mx, std::fabs(row[k]));
+      float sc = mx > 0.0f ? mx : 1e-4f;
+      s[(size_t)j * G + g] = sc;
+      float inv = 1.0f / sc;
+      for (int k = st; k < en; ++k) {
+        float v = row[k] * inv;
+        int best = 0;
+        float bd = std::fabs(v - cb[0]);
+        for (int c = 1; c < 4; ++c) {
+          float dd = std::fabs(v - cb[c]);
+          if (dd < bd) {
+            bd = dd;
+            best = c;
+          }
+        }
+        P[(size_t)j * words + k / 16] |= (uint32_t)best << ((k % 16) * 2);
+      }
+    }
+  }
+  return KAN_OK;
+}
+
+static int dequant_2bit_host(int fmt, const uint32_t* P, const float* s, const float* cb,
+                             float* out, int D_out, int K_dim, int gs) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!P || !s || !out || D_out <= 0 || K_dim <= 0 || gs <= 0 || (fmt == KAN_W_INT2 && !cb))
+    return fail(KAN_ERR_ARG, "dequantize (2-bit): bad arguments");
+  const int words = (K_dim + 15) / 16, G = (K_dim + gs - 1) / gs;
+  void *dP, *dS, *dC = nullptr, *dO;
+  if ((rc = stage_in(d, S_W, P, (size_t)D_out * words * 4, &dP))) return rc;
+  if ((rc = stage_in(d, S_SC, s, (size_t)D_out * G * 4, &dS))) return rc;
+  if (cb && (rc = stage_in(d, S_CB, cb, 16, &dC))) return rc;
+  if ((rc = slot(d, S_Y, (size_t)D_out * K_dim * 4, &dO))) return rc;
+  kan_weight w;
+  std::memset(&w, 0, sizeof(w));
+  w.format = fmt;
+  w.group_size = gs;
+  w.data = dP;
+  w.scales = (const float*)dS;
+  w.codebook = (const float*)dC;
+  cudaError_t e = launch_dequantize(w, D_out, K_dim, dO, KAN_F32, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "dequantize: %s", cudaGetErrorString(e));
+  return stage_out(d, out, dO, (size_t)D_out * K_dim * 4);
+}
+
+int metal_kan_dequantize_ternary(const uint32_t* P, const float* s, float* out, int D_out,
+                                 int K_dim, int gs) {
+  return dequant_2bit_host(KAN_W_TERNARY, P, s, nullptr, out, D_out, K_dim, gs);
+}
+
+int metal_kan_dequantize_int2(const uint32_t* P, const float* s, const float* cb, float* out,
+                              int D_out, int K_dim, int gs) {
+  return dequant_2bit_host(KAN_W_INT2, P, s, cb, out, D_out, K_dim, gs);
+}
+
+static int packed_cheby_host(int fmt, const float* X, const uint32_t* P, const float* s,
+                             const float* cb, const float* bias, float* Y, int B, int D_in,
+                             int D_out, int deg, int gs, int hbi) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!X || !P || !s || !Y || B <= 0 || D_in <= 0 || D_out <= 0 || deg <= 0 || gs <= 0 ||
+      (fmt == KAN_W_INT2 && !cb) || (hbi && !bias))
+    return fail(KAN_ERR_ARG, "packed cheby forward: bad arguments");
+  const int K_dim = D_in * deg, words = (K_dim + 15) / 16, G = (K_dim + gs - 1) / gs;
+  void *dX, *dP, *dS, *dC = nullptr, *dB = nullptr, *dY;
+  if ((rc = stage_in(d, S_X, X, (size_t)B * D_in * 4, &dX))) return rc;
+  if ((rc = stage_in(d, S_W, P, (size_t)D_out * words * 4, &dP))) return rc;
+  if ((rc = stage_in(d, S_SC, s, (size_t)D_out * G * 4, &dS))) return rc;
+  if (cb && (rc = stage_in(d, S_CB, cb, 16, &dC))) return rc;
+  if (hbi && (rc = stage_in(d, S_BIAS, bias, (size_t)D_out * 4, &dB))) return rc;
+  if ((rc = slot(d, S_Y, (size_t)B * D_out * 4, &dY))) return rc;
+  kan_layer L = base_layer(KAN_CHEBY, KAN_F32, D_in, D_out, deg, 0, hbi);
+  L.w.format = fmt;
+  L.w.group_size = gs;
+  L.w.data = dP;
+  L.w.scales = (const float*)dS;
+  L.w.codebook = (const float*)dC;
+  L.bias = dB;
+  if ((rc = run_forward(&L, dX, dY, B, KAN_PATH_AUTO, d->stream, d))) return rc;
+  return stage_out(d, Y, dY, (size_t)B * D_out * 4);
+}
+
+int metal_kan_forward_ternary_cheby(const float* X, const uint32_t* P, const float* s,
+                                    const float* bias, float* Y, int B, int D_in, int D_out,
+                                    int degree, int gs, int hbi) {
+  return packed_cheby_host(KAN_W_TERNARY, X, P, s, nullptr, bias, Y, B, D_in, D_out, degree, gs,
+                           hbi);
+}
+
+int metal_kan_forward_int2_cheby(const float* X, const uint32_t* P, const float* s,
+                                 const float* cb, const float* bias, float* Y, int B, int D_in,
+                                 int D_out, int degree, int gs, int hbi) {
+  return packed_cheby_host(KAN_W_INT2, X, P, s, cb, bias, Y, B, D_in, D_out, degree, gs, hbi);
+}
+
+double benchmark_metal_cheby(const float* X, const float* W, const float* Wb, const float* bias,
+                             float* Y, int B, int D_in, int D_out, int K, int hb, int hbi,
+                             int warmup, int iters) {
+  return bench_loop([&] { return metal_kan_cheby_forward(X, W, Wb, bias, Y, B, D_in, D_out, K, hb, hbi); },
+                    warmup, iters);
+}
+double benchmark_metal_fastkan(const float* X, const float* W, const float* Wb, const float* grid,
+                               const float* bias, float* Y, int B, int D_in, int D_out, int K,
+                               float inv_den, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_fastkan_forward(X, W, Wb, grid, bias, Y, B, D_in, D_out, K, inv_den, hb, hbi);
+  }, warmup, iters);
+}
+double benchmark_metal_bspline(const float* X, const float* W, const float* Wb, const float* grid,
+                               const float* bias, float* Y, int B, int D_in, int D_out, int G,
+                               int order, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_bspline_forward(X, W, Wb, grid, bias, Y, B, D_in, D_out, G, order, hb, hbi);
+  }, warmup, iters);
+}
+double benchmark_metal_wavkan(const float* X, const float* W, const float* Wb, const float* tr,
+                              const float* isc, const float* bias, float* Y, int B, int D_in,
+                              int D_out, int nw, int wt, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_wavkan_forward(X, W, Wb, tr, isc, bias, Y, B, D_in, D_out, nw, wt, hb, hbi);
+  }, warmup, iters);
+}
+
+}  // extern "C"

@@ -1,0 +1,263 @@
+// kan_device.cuh -- device-side building blocks shared by every KAN kernel.
+//
+// * activation-dtype traits (f32 / f16 / bf16),
+// * the per-feature basis generators with the rounding points of the reference kernels
+//   (Shuril/metal-kans metal_kans/kernels/fused_kan.metal, cited per generator),
+// * weight decode (dense and the four packed formats of metal_kans/quantization.py),
+// * the input maps (reference clamp, tanh, LayerNorm) and the device error word.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/kan_cuda.h"
+#include "kan_args.h"
+
+namespace kan {
+
+// Generation modes: the arithmetic a basis value is produced with.
+//   MODE_F32  - fp32 math (the reference's fp32 kernels)
+//   MODE_F16  - the reference's *_fp16 kernels: half arithmetic where they use half, fp32 math
+//               with a half store where they store half
+//   MODE_BF16 - fp32 math, value rounded to bf16 (new; the reference has no bf16)
+enum { MODE_F32 = 0, MODE_F16 = 1, MODE_BF16 = 2 };
+
+template <int MODE> struct Act;
+template <> struct Act<MODE_F32> {
+  using T = float;
+  static __device__ __forceinline__ float to_f(T v) { return v; }
+  static __device__ __forceinline__ T from_f(float v) { return v; }
+  static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <> struct Act<MODE_F16> {
+  using T = __half;
+  static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
+  static __device__ __forceinline__ T from_f(float v) { return __float2half_rn(v); }
+  static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+};
+template <> struct Act<MODE_BF16> {
+  using T = __nv_bfloat16;
+  static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ T from_f(float v) { return __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+};
+
+
+// ------------------------------------------------------------------------------------------
+// device error word (bounded waits)
+// ------------------------------------------------------------------------------------------
+enum { DEVERR_TIMEOUT_FULL_A = 1, DEVERR_TIMEOUT_FULL_B = 2, DEVERR_TIMEOUT_EMPTY = 3,
+       DEVERR_TIMEOUT_ACCUM = 4 };
+
+__device__ __forceinline__ void raise_device_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+// ------------------------------------------------------------------------------------------
+// input maps
+// ------------------------------------------------------------------------------------------
+// The mapped value is handed to the basis in the activation dtype (rounded once).
+template <int MODE>
+__device__ __forceinline__ float map_input(float x, int input_map, float mean, float rstd) {
+  if (input_map == KAN_MAP_TANH) return Act<MODE>::round(tanhf(x));
+  if (input_map == KAN_MAP_LAYERNORM) return Act<MODE>::round((x - mean) * rstd);
+  return x;
+}
+
+// ------------------------------------------------------------------------------------------
+// SiLU of the base branch (applied to the mapped input)
+// ------------------------------------------------------------------------------------------
+// fp32: x / (1 + exp(-x))                         fused_kan.metal:116-138
+// fp16: x / (1.0h + exp(-x)), three half roundings fused_kan.metal:1373-1397
+template <int MODE>
+__device__ __forceinline__ float silu_value(float x) {
+  if (MODE == MODE_F16) {
+    __half e = __float2half_rn(__expf(-x));
+    __half d = __hadd(__float2half_rn(1.0f), e);
+    return __half2float(__hdiv(__float2half_rn(x), d));
+  }
+  return Act<MODE>::round(x / (1.0f + __expf(-x)));
+}
+
+// ------------------------------------------------------------------------------------------
+// basis generators: one object per (row, feature); term(k) is called for k = 0, 1, 2, ... in
+// order (the Chebyshev recurrence relies on it).
+// ------------------------------------------------------------------------------------------
+
+// Chebyshev T_k(clamp(x, -1, 1)), K terms.  fp32: recurrence 2x T1 - T0 (fused_kan.metal:
+// 205-238); fp16: fp32 recurrence fma(2x, T1, -T0) stored as half (:1399-1426).
+template <int MODE>
+struct ChebyGen {
+  float x2, t0, t1;
+  int k;
+  __device__ __forceinline__ void init(float xm, int /*feature*/, const LayerArgs& /*a*/) {
+    float xc = fminf(fmaxf(xm, -1.0f), 1.0f);
+    x2 = 2.0f * xc;
+    t0 = 1.0f;
+    t1 = xc;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    float v;
+    if (k == 0) v = t0;
+    else if (k == 1) v = t1;
+    else {
+      float t2 = fmaf(x2, t1, -t0);
+      t0 = t1;
+      t1 = t2;
+      v = t2;
+    }
+    ++k;
+    return Act<MODE>::round(v);
+  }
+};
+
+// Gaussian RBF exp(-(x - c_k)^2 * inv_den).  fp32: fused_kan.metal:140-166; fp16 (:1428-1450):
+// diff, -diff*diff and *inv_den in half arithmetic, exp of the half argument stored as half.
+template <int MODE>
+struct RbfGen {
+  float x;
+  const float* grid;
+  float inv_den;
+  int k;
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+    x = xm;
+    grid = a.grid;
+    inv_den = a.inv_den;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    float c = __ldg(grid + k);
+    ++k;
+    if (MODE == MODE_F16) {
+      __half diff = __hsub(__float2half_rn(x), __float2half_rn(c));
+      __half sq = __hmul(__hneg(diff), diff);
+      __half t = __hmul(sq, __float2half_rn(inv_den));
+      return __half2float(__float2half_rn(__expf(__half2float(t))));
+    }
+    float d = x - c;
+    return Act<MODE>::round(__expf(-(d * d) * inv_den));
+  }
+};
+
+// Closed-form uniform cubic B-spline, G+3 bases (fused_kan.metal:240-276; fp16 :1476-1512 uses the
+// same fp32 math and stores half).  span = clamp(floor(pos), 0, G-1), u = clamp(pos-span, 0, 1).
+template <int MODE>
+struct BsplineGen {
+  float b0, b1, b2, b3;
+  int span, k;
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+    float pos = (xm - a.grid_min) * a.inv_h;
+    float fl = floorf(pos);
+    int s = (int)fminf(fmaxf(fl, 0.0f), (float)(a.grid_size - 1));
+    float u = fminf(fmaxf(pos - (float)s, 0.0f), 1.0f);
+    float om = 1.0f - u;
+    const float inv6 = 1.0f / 6.0f;
+    float u2 = u * u, u3 = u2 * u;
+    b0 = Act<MODE>::round(om * om * om * inv6);
+    b1 = Act<MODE>::round((3.0f * u3 - 6.0f * u2 + 4.0f) * inv6);
+    b2 = Act<MODE>::round((-3.0f * u3 + 3.0f * u2 + 3.0f * u + 1.0f) * inv6);
+    b3 = Act<MODE>::round(u3 * inv6);
+    span = s;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    int d = k - span;
+    ++k;
+    float v = 0.0f;
+    v = (d == 0) ? b0 : v;
+    v = (d == 1) ? b1 : v;
+    v = (d == 2) ? b2 : v;
+    v = (d == 3) ? b3 : v;
+    return v;
+  }
+};
+
+// Wavelets psi((x - t) * inv_s).  fp32 (fused_kan.metal:168-203): mexican hat (1-z^2) e^{-z^2/2},
+// morlet cos(5z) e^{-z^2/2}, dog -z e^{-z^2/2}.  fp16 (:1514-1548): every step in half, and the
+// Morlet frequency is 1.75 (the reference's half kernel differs from its fp32 one; mirrored).
+template <int MODE>
+struct WaveletGen {
+  float x;
+  const float* tr;
+  const float* sc;
+  int wtype, k;
+  __device__ __forceinline__ void init(float xm, int feature, const LayerArgs& a) {
+    x = xm;
+    tr = a.translation + (size_t)feature * a.K;
+    sc = a.inv_scale + (size_t)feature * a.K;
+    wtype = a.wavelet_type;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    float t = __ldg(tr + k), s = __ldg(sc + k);
+    ++k;
+    if (MODE == MODE_F16) {
+      __half z = __hmul(__hsub(__float2half_rn(x), __float2half_rn(t)), __float2half_rn(s));
+      __half ar = __hmul(__hmul(__float2half_rn(-0.5f), z), z);
+      __half e = __float2half_rn(__expf(__half2float(ar)));
+      __half psi;
+      if (wtype == 0) psi = __hmul(__hsub(__float2half_rn(1.0f), __hmul(z, z)), e);
+      else if (wtype == 1)
+        psi = __hmul(__float2half_rn(cosf(__half2float(__hmul(__float2half_rn(1.75f), z)))), e);
+      else psi = __hmul(__hneg(z), e);
+      return __half2float(psi);
+    }
+    float z = (x - t) * s;
+    float e = __expf(-0.5f * z * z);
+    float psi;
+    if (wtype == 0) psi = (1.0f - z * z) * e;
+    else if (wtype == 1) psi = cosf(5.0f * z) * e;
+    else psi = -z * e;
+    return Act<MODE>::round(psi);
+  }
+};
+
+template <int BASIS, int MODE> struct GenFor;
+template <int MODE> struct GenFor<KAN_CHEBY, MODE> { using type = ChebyGen<MODE>; };
+template <int MODE> struct GenFor<KAN_RBF, MODE> { using type = RbfGen<MODE>; };
+template <int MODE> struct GenFor<KAN_BSPLINE, MODE> { using type = BsplineGen<MODE>; };
+template <int MODE> struct GenFor<KAN_WAVELET, MODE> { using type = WaveletGen<MODE>; };
+
+// ------------------------------------------------------------------------------------------
+// weight decode: element (row, col) of a kan_weight as the exact fp32 value the reference's
+// dequantiser produces (separate fp32 multiply and add; metal_kan_bridge.mm:4213-4232,
+// :4278-4302, fused_kan.metal:2392-2441).  Dense weights are converted from the act dtype.
+// ------------------------------------------------------------------------------------------
+template <int MODE>
+__device__ __forceinline__ float weight_value(const kan_weight& w, int row, int col, int cols) {
+  switch (w.format) {
+    case KAN_W_DENSE: {
+      const typename Act<MODE>::T* p = (const typename Act<MODE>::T*)w.data;
+      return Act<MODE>::to_f(p[(size_t)row * cols + col]);
+    }
+    case KAN_W_INT8:
+    case KAN_W_INT4: {
+      size_t e = (size_t)row * w.padded_cols + col;
+      size_t g = e / (unsigned)w.group_size;
+      int q;
+      if (w.format == KAN_W_INT8) q = ((const uint8_t*)w.data)[e];
+      else {
+        uint8_t byte = ((const uint8_t*)w.data)[e >> 1];
+        q = (e & 1) ? (byte >> 4) : (byte & 0xF);
+      }
+      return __fadd_rn(__fmul_rn((float)q, __ldg(w.scales + g)), __ldg(w.biases + g));
+    }
+    default: {  // 2-bit formats
+      int words = (cols + 15) >> 4;
+      int groups = (cols + w.group_size - 1) / w.group_size;
+      uint32_t word = ((const uint32_t*)w.data)[(size_t)row * words + (col >> 4)];
+      uint32_t code = (word >> ((col & 15) * 2)) & 3u;
+      float s = __ldg(w.scales + (size_t)row * groups + col / w.group_size);
+      float v;
+      if (w.format == KAN_W_TERNARY) v = (code == 3u) ? 0.0f : (float)code - 1.0f;
+      else v = __ldg(w.codebook + code);
+      return __fmul_rn(v, s);
+    }
+  }
+}
+
+}  // namespace kan

@@ -1,0 +1,31 @@
+// kan_launch.h -- host-side launchers of the device kernels (implemented in the .cu files) and
+// the launch counter reported by kan_launch_count().
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "kan_args.h"
+
+namespace kan {
+
+inline int BasisOf(const LayerArgs& a) { return a.basis; }
+
+void note_launch();
+long long launch_count();
+// Address of the device error word on the current device (kan_misc.cu).
+int* device_error_ptr();
+
+// kan_simt.cu
+cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s);
+// kan_tc.cu: returns cudaErrorNotSupported when the shape is outside the kernel's envelope
+cudaError_t launch_tc(const LayerArgs& a, int act_dtype, cudaStream_t s);
+bool tc_supported(const LayerArgs& a, int act_dtype);
+// kan_misc.cu
+cudaError_t launch_dequantize(const kan_weight& w, int rows, int cols, void* out, int out_dtype,
+                              cudaStream_t s);
+cudaError_t launch_swiglu(const void* g, const void* u, void* out, long long n, int dtype,
+                          cudaStream_t s);
+cudaError_t launch_convert(const void* src, int sdt, void* dst, int ddt, long long n,
+                           cudaStream_t s);
+
+}  // namespace kan

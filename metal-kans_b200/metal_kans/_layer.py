@@ -1,0 +1,157 @@
+"""Common machinery of the KAN layer classes: descriptor building and the device forward.
+
+A layer holds NumPy weights (the reference's API surface) mirrored on the device, builds a
+``kan_layer`` descriptor (include/kan_cuda.h) and runs ``kan_forward``.  Quantised layers (after
+``to_int8/to_int4/to_ternary/to_int2``) run their packed weights: decoded in the kernel (exact
+fp32 dequantised values), or, for the tensor-core path, from a dense act-dtype copy of the same
+values.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _engine as E
+from . import device as D
+
+_MAPS = {None: D.KAN_MAP_NONE, "none": D.KAN_MAP_NONE, "clamp": D.KAN_MAP_NONE,
+         "tanh": D.KAN_MAP_TANH, "layernorm": D.KAN_MAP_LAYERNORM}
+
+PACKED_SUFFIXES = ("_quantized", "_ternary", "_int2")
+
+
+class KANLayerBase(E.DeviceLayerMixin):
+    """Base of ChebyKAN / FastKAN / BSplineKAN / WavKAN."""
+
+    BASIS = D.KAN_CHEBY
+    MAIN = "w_cheby"
+    _WEIGHTS = ("w_base", "bias")
+
+    # ---- dtype handling (reference: .half() / .float(); new: .bfloat16()) ------------------
+    @property
+    def dtype(self) -> np.dtype:
+        return getattr(self, self.MAIN).dtype
+
+    def _cast(self, dt, extra=()):
+        setattr(self, self.MAIN, getattr(self, self.MAIN).astype(dt))
+        if self.has_base:
+            self.w_base = self.w_base.astype(dt)
+        if self.has_bias:
+            self.bias = self.bias.astype(dt)
+        for name in extra:
+            setattr(self, name, getattr(self, name).astype(dt))
+        return self
+
+    def half(self):
+        """Converts layer parameters to FP16 half precision."""
+        return self._cast(np.float16, self._HALF_EXTRA)
+
+    def float(self):
+        """Converts layer parameters to FP32 single precision."""
+        return self._cast(np.float32, self._HALF_EXTRA)
+
+    def bfloat16(self):
+        """Converts layer parameters to bf16 (new: the reference has no bf16 mode)."""
+        if E.BFLOAT16 is None:
+            raise RuntimeError("bf16 needs the ml_dtypes package")
+        return self._cast(E.BFLOAT16, ())
+
+    _HALF_EXTRA = ()
+
+    # ---- descriptor --------------------------------------------------------------------------
+    def _basis_params(self, L: D.KanLayer, keep: list) -> None:
+        """Fill the basis-specific fields of the descriptor (subclasses)."""
+
+    def _packed(self, name: str):
+        """The packed weight made by to_int*/quantize for ``name``, if still current."""
+        for suf in PACKED_SUFFIXES:
+            q = self.__dict__.get(f"_{name}{suf}")
+            if q is not None and getattr(q, "_source_version", None) == self._version(name):
+                return q
+        return None
+
+    def _weight_struct(self, name: str, act_np, keep: list) -> D.KanWeight:
+        w = D.KanWeight()
+        q = self._packed(name)
+        if q is None:
+            buf = self._dev(name, act_np)
+            keep.append(buf)
+            w.format = D.KAN_W_DENSE
+            w.data = buf.ptr
+            return w
+        q._fill_struct(w, keep)
+        if np.dtype(act_np) != np.float32:
+            dense = self._dev(name, act_np)  # dequantised values rounded to the act dtype
+            keep.append(dense)
+            w.dense = dense.ptr
+        return w
+
+    def _descriptor(self, keep: list) -> D.KanLayer:
+        act = self.dtype
+        L = D.KanLayer()
+        L.basis = self.BASIS
+        L.act_dtype = E.kan_dtype(act)
+        L.D_in = self.in_features
+        L.D_out = self.out_features
+        L.K = self._terms()
+        L.has_base = int(bool(self.has_base))
+        L.has_bias = int(bool(self.has_bias))
+        L.input_map = _MAPS[getattr(self, "input_map", "none")]
+        L.ln_eps = float(getattr(self, "ln_eps", 1e-5))
+        L.w = self._weight_struct(self.MAIN, act, keep)
+        if self.has_base:
+            L.wb = self._weight_struct("w_base", act, keep)
+        if self.has_bias:
+            b = self._dev("bias", act)
+            keep.append(b)
+            L.bias = b.ptr
+        self._basis_params(L, keep)
+        return L
+
+    # ---- forward -----------------------------------------------------------------------------
+    def forward_device(self, x_ptr: int, y_ptr: int, B: int, stream=None, path: int = 0) -> None:
+        """Enqueue this layer on device buffers (act dtype, [B, in] -> [B, out])."""
+        keep: list = []
+        L = self._descriptor(keep)
+        lib = E.lib()
+        if path:
+            lib.kan_forward_path(ctypes.byref(L), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr),
+                                 int(B), int(path), stream)
+        else:
+            lib.kan_forward(ctypes.byref(L), ctypes.c_void_p(x_ptr), ctypes.c_void_p(y_ptr),
+                            int(B), stream)
+        self._keepalive = keep  # buffers must outlive the queued kernel
+
+    def forward(self, x: np.ndarray, path: int = 0) -> np.ndarray:
+        """Fused CUDA forward: x [..., in_features] -> [..., out_features] in the layer dtype."""
+        act = self.dtype
+        x2, orig = E.as_activation(x, act, self.in_features)
+        B = x2.shape[0]
+        y = np.empty((B, self.out_features), dtype=act)
+        if B:
+            s = self._scratch()
+            dx = s.get("x", x2.nbytes).upload(x2)
+            dy = s.get("y", y.nbytes)
+            self.forward_device(dx.ptr, dy.ptr, B, None, path)
+            E.fetch(dy, y)
+        return E.restore_shape(y, orig, self.out_features)
+
+    __call__ = forward
+
+    def backward(self, *args, **kwargs):
+        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+
+    def train_step(self, *args, **kwargs):
+        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+
+    def _benchmark_fallback(self, x, warmup, iters):
+        import time
+
+        for _ in range(warmup):
+            self.forward(x)
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            self.forward(x)
+        return (time.perf_counter() - t0) * 1e3 / iters

@@ -1,0 +1,132 @@
+"""GatedKAN FFN block on the B200 engine.
+
+Drop-in for ``metal_kans/gated_kan.py:24-282``: three ChebyKAN layers (gate, up: d_model ->
+d_ffn; down: d_ffn -> d_model), ``hidden = SiLU(gate) * up`` with the SiLU argument clamped to
++-20 (``gated_kan.py:112-131``, ``fused_kan.metal:2284-2296``), (B, Seq, d) inputs flattened.
+The whole block runs on the device through ``kan_gated_forward``: activations never return to
+the host between the three layers (the reference syncs four times).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _engine as E
+from .cheby_kan import ChebyKAN
+from .quantization import to_int2, to_int4, to_int8, to_ternary
+
+
+class GatedKAN:
+    """Gated KAN block: gate = G(x), up = U(x), hidden = SiLU(gate) * up, out = Down(hidden)."""
+
+    def __init__(self, d_model: int, d_ffn: Optional[int] = None, degree: int = 4,
+                 has_base: bool = True, has_bias: bool = False, dtype=np.float32):
+        self.d_model = int(d_model)
+        self.d_ffn = int(d_ffn if d_ffn is not None else 2 * d_model)
+        self.degree = int(degree)
+        self.has_base = bool(has_base)
+        self.has_bias = bool(has_bias)
+        self.dtype = np.dtype(dtype)
+        self.gate_kan = ChebyKAN(self.d_model, self.d_ffn, degree=self.degree,
+                                 bias=self.has_bias, use_base=self.has_base)
+        self.up_kan = ChebyKAN(self.d_model, self.d_ffn, degree=self.degree,
+                               bias=self.has_bias, use_base=self.has_base)
+        self.down_kan = ChebyKAN(self.d_ffn, self.d_model, degree=self.degree,
+                                 bias=self.has_bias, use_base=self.has_base)
+        if self.dtype == np.float16:
+            self.half()
+        elif E.BFLOAT16 is not None and self.dtype == E.BFLOAT16:
+            self.bfloat16()
+        self._scratch = E._Scratch()
+
+    def _layers(self):
+        return (self.gate_kan, self.up_kan, self.down_kan)
+
+    def half(self) -> "GatedKAN":
+        for l in self._layers():
+            l.half()
+        self.dtype = np.dtype(np.float16)
+        return self
+
+    def float(self) -> "GatedKAN":
+        for l in self._layers():
+            l.float()
+        self.dtype = np.dtype(np.float32)
+        return self
+
+    def bfloat16(self) -> "GatedKAN":
+        """New: bf16 compute (the reference has no bf16)."""
+        for l in self._layers():
+            l.bfloat16()
+        self.dtype = E.BFLOAT16
+        return self
+
+    def forward_device(self, x_ptr: int, h_ptr: int, y_ptr: int, B: int, stream=None) -> None:
+        """Enqueue the block on device buffers: x [B, d_model] -> hidden [B, d_ffn] -> y."""
+        keep: list = []
+        descs = [l._descriptor(keep) for l in self._layers()]
+        E.lib().kan_gated_forward(*(ctypes.byref(d) for d in descs), ctypes.c_void_p(x_ptr),
+                                  ctypes.c_void_p(h_ptr), ctypes.c_void_p(y_ptr), int(B), stream)
+        self._keepalive = keep
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        """Accepts x of shape (B, d_model) or (B, Seq, d_model)."""
+        act = self.gate_kan.dtype
+        if self.up_kan.dtype != act or self.down_kan.dtype != act:
+            raise TypeError("gate/up/down layers must share one dtype")
+        x2, orig = E.as_activation(x, act, self.d_model)
+        B = x2.shape[0]
+        y = np.empty((B, self.d_model), act)
+        if B:
+            esz = np.dtype(act).itemsize
+            dx = self._scratch.get("x", x2.nbytes).upload(x2)
+            dh = self._scratch.get("h", B * self.d_ffn * esz)
+            dy = self._scratch.get("y", y.nbytes)
+            self.forward_device(dx.ptr, dh.ptr, dy.ptr, B)
+            E.fetch(dy, y)
+        return E.restore_shape(y, orig, self.d_model)
+
+    __call__ = forward
+
+    def backward(self, *a, **k):
+        raise NotImplementedError("training (backward) is outside this inference engine")
+
+    def to_int8(self, group_size: int = 64) -> "GatedKAN":
+        for l in self._layers():
+            to_int8(l, group_size=group_size)
+        self.dtype = self.gate_kan.dtype
+        return self
+
+    def to_int4(self, group_size: int = 64) -> "GatedKAN":
+        for l in self._layers():
+            to_int4(l, group_size=group_size)
+        self.dtype = self.gate_kan.dtype
+        return self
+
+    def to_ternary(self, group_size: int = 32) -> "GatedKAN":
+        for l in self._layers():
+            to_ternary(l, group_size=group_size)
+        self.dtype = self.gate_kan.dtype
+        return self
+
+    def to_int2(self, group_size: int = 32) -> "GatedKAN":
+        for l in self._layers():
+            to_int2(l, group_size=group_size)
+        self.dtype = self.gate_kan.dtype
+        return self
+
+    def parameter_count(self) -> int:
+        count = 0
+        for kan in self._layers():
+            count += kan.w_cheby.size
+            if kan.has_base and kan.w_base is not None:
+                count += kan.w_base.size
+            if kan.has_bias and kan.bias is not None:
+                count += kan.bias.size
+        return count
+
+    def __repr__(self) -> str:
+        return (f"GatedKAN(d_model={self.d_model}, d_ffn={self.d_ffn}, degree={self.degree}, "
+                f"has_base={self.has_base}, params={self.parameter_count():,})")

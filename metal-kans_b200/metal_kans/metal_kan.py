@@ -1,0 +1,139 @@
+"""Sequential multi-layer KAN network on the B200 engine.
+
+Drop-in for ``metal_kans/metal_kan.py:28-288`` (forward side): ``MetalKAN(layers_hidden,
+basis_type, degree, bias, use_base, pipeline)``, ``.half()``, ``.float()``, ``async_stream``.
+Activations stay on the device between layers (ping-pong buffers); only the input and the final
+output cross PCIe.  ``pipeline=True`` on an fp32 Cheby net runs the reference's single-call chain
+entry point ``metal_kan_chain_pipeline_cheby``, which here honours each layer's degree (the
+reference hard-codes 4 terms, ``metal_kan_bridge.mm:1210``).
+Bases served by this engine: cheby, fastkan/rbf, bspline/spline/kan, wav/wavkan/wavelet.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Sequence
+
+import numpy as np
+
+from . import _engine as E
+from .bspline_kan import BSplineKAN
+from .cheby_kan import ChebyKAN
+from .fast_kan import FastKAN
+from .wav_kan import WavKAN
+
+MetalChebyKAN = ChebyKAN
+MetalFastKAN = FastKAN
+
+
+class MetalKAN:
+    """Multi-layer KAN network executed layer by layer on the GPU."""
+
+    def __init__(self, layers_hidden: Sequence[int], basis_type: str = "cheby", degree: int = 4,
+                 bias: bool = True, use_base: bool = True, pipeline: bool = False):
+        self.layers_hidden = list(layers_hidden)
+        self.basis_type = basis_type.lower()
+        self.degree = degree
+        self.bias = bias
+        self.use_base = use_base
+        self.pipeline = pipeline and (self.basis_type in ("cheby", "chebyshev"))
+        self.layers = []
+        for i in range(len(layers_hidden) - 1):
+            in_f, out_f = layers_hidden[i], layers_hidden[i + 1]
+            b = self.basis_type
+            if b in ("cheby", "chebyshev"):
+                layer = ChebyKAN(in_f, out_f, degree=degree, bias=bias, use_base=use_base)
+            elif b in ("fastkan", "rbf"):
+                layer = FastKAN(in_f, out_f, num_centers=degree, bias=bias, use_base=use_base)
+            elif b in ("wav", "wavkan", "wavelet"):
+                layer = WavKAN(in_f, out_f, num_wavelets=degree, bias=bias, use_base=use_base)
+            elif b in ("bspline", "spline", "kan"):
+                layer = BSplineKAN(in_f, out_f, grid_size=degree, bias=bias, use_base=use_base)
+            else:
+                raise ValueError(f"Unknown or unsupported basis_type for this engine: {basis_type}")
+            self.layers.append(layer)
+        self._scratch = E._Scratch()
+
+    @property
+    def dtype(self) -> np.dtype:
+        return self.layers[0].dtype if self.layers else np.dtype(np.float32)
+
+    def half(self) -> "MetalKAN":
+        for l in self.layers:
+            l.half()
+        return self
+
+    def float(self) -> "MetalKAN":
+        for l in self.layers:
+            l.float()
+        return self
+
+    def bfloat16(self) -> "MetalKAN":
+        for l in self.layers:
+            l.bfloat16()
+        return self
+
+    def async_stream(self, batches) -> List[np.ndarray]:
+        """Runs several batches back to back and synchronises once (metal_kan.py:105-119)."""
+        from .device import set_async, sync
+
+        results = []
+        set_async(True)
+        try:
+            for b in batches:
+                results.append(self.forward(b))
+        finally:
+            sync()
+            set_async(False)
+        return results
+
+    def forward_device(self, x_ptr: int, y_ptr: int, B: int, stream=None) -> None:
+        """Enqueue the whole stack on device buffers (every layer must share one dtype)."""
+        esz = self.dtype.itemsize
+        width = max(self.layers_hidden)
+        bufs = [self._scratch.get("a0", B * width * esz), self._scratch.get("a1", B * width * esz)]
+        cur = x_ptr
+        for li, layer in enumerate(self.layers):
+            nxt = y_ptr if li == len(self.layers) - 1 else bufs[li % 2].ptr
+            layer.forward_device(cur, nxt, B, stream)
+            cur = nxt
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        act = self.dtype
+        if any(l.dtype != act for l in self.layers):
+            for l in self.layers:  # mixed dtypes: each layer casts, like the reference
+                x = l(x)
+            return x
+        x2, orig = E.as_activation(x, act, self.layers_hidden[0])
+        B = x2.shape[0]
+        out_dim = self.layers_hidden[-1]
+        if self.pipeline and len(self.layers) > 1 and act == np.float32:
+            return E.restore_shape(self._forward_pipelined_cheby(x2), orig, out_dim)
+        y = np.empty((B, out_dim), act)
+        if B:
+            dx = self._scratch.get("x", x2.nbytes).upload(x2)
+            dy = self._scratch.get("y", y.nbytes)
+            self.forward_device(dx.ptr, dy.ptr, B)
+            E.fetch(dy, y)
+        return E.restore_shape(y, orig, out_dim)
+
+    def _forward_pipelined_cheby(self, x2: np.ndarray) -> np.ndarray:
+        B = x2.shape[0]
+        n = len(self.layers)
+        y = np.empty((B, self.layers_hidden[-1]), np.float32)
+        dims = (ctypes.c_int * (n + 1))(*self.layers_hidden)
+        degs = (ctypes.c_int * n)(*[l.degree for l in self.layers])
+        ws = (ctypes.c_void_p * n)(*[l.w_cheby.ctypes.data for l in self.layers])
+        wbs = (ctypes.c_void_p * n)(*[l.w_base.ctypes.data if l.has_base else None for l in self.layers])
+        bs = (ctypes.c_void_p * n)(*[l.bias.ctypes.data if l.has_bias else None for l in self.layers])
+        E.lib().metal_kan_chain_pipeline_cheby(x2.ctypes.data, y.ctypes.data, B, n, dims, degs,
+                                               ws, wbs, bs)
+        return y
+
+    def __call__(self, x: np.ndarray) -> np.ndarray:
+        return self.forward(x)
+
+    def backward(self, *a, **k):
+        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+
+    def __repr__(self) -> str:
+        return f"MetalKAN(layers={self.layers_hidden}, basis={self.basis_type!r})"

@@ -1,0 +1,61 @@
+"""Helpers shared by the GPU tests: build engine layers and oracle calls from the same inputs."""
+import numpy as np
+
+from oracle import kan_oracle as O
+
+TOL = {"f32": 1e-5, "f16": 2e-3, "bf16": 2e-3}  # max|y - y_ref| / max|y_ref| (BASELINE tolerance)
+
+
+def np_dtype(mode):
+    return O.act_dtype(mode)
+
+
+def set_mode(layer, mode):
+    if mode == "f16":
+        layer.half()
+    elif mode == "bf16":
+        layer.bfloat16()
+    return layer
+
+
+def oracle_for_layer(layer, x, mode, basis):
+    """Oracle output for an engine layer object (reads its current weights)."""
+    import metal_kans as mk  # noqa: F401
+
+    W = np.asarray(getattr(layer, layer.MAIN)).astype(np.float32)
+    wb = np.asarray(layer.w_base).astype(np.float32) if layer.has_base else None
+    b = np.asarray(layer.bias).astype(np.float32) if layer.has_bias else None
+    kw = {}
+    if basis == "rbf":
+        kw = dict(grid=np.asarray(layer.grid).astype(np.float32), inv_den=layer.inv_denominator)
+    elif basis == "bspline":
+        kw = dict(grid_size=layer.grid_size, grid_min=float(layer.grid[0]), inv_h=float(layer.grid[1]))
+    elif basis == "wavelet":
+        kw = dict(translation=np.asarray(layer.translation).astype(np.float32),
+                  inv_scale=np.asarray(layer._inv_scale).astype(np.float32),
+                  wavelet_type=layer.wavelet_type)
+    return O.kan_layer(x, basis, mode, W, wb, b, K=layer._terms(),
+                       input_map=getattr(layer, "input_map", "none"), **kw)
+
+
+def make_layer(basis, d_in, d_out, K, *, bias=True, use_base=True, input_map="none", seed=0,
+               wavelet_type="mexican_hat"):
+    import metal_kans as mk
+
+    np.random.seed(seed)
+    if basis == "cheby":
+        return mk.ChebyKAN(d_in, d_out, degree=K, bias=bias, use_base=use_base, input_map=input_map)
+    if basis == "rbf":
+        return mk.FastKAN(d_in, d_out, num_centers=K, bias=bias, use_base=use_base,
+                          grid_range=(-2.0, 2.0), input_map=input_map)
+    if basis == "bspline":
+        return mk.BSplineKAN(d_in, d_out, grid_size=K - 3, bias=bias, use_base=use_base,
+                             input_map=input_map)
+    return mk.WavKAN(d_in, d_out, num_wavelets=K, bias=bias, use_base=use_base,
+                     wavelet_type=wavelet_type, input_map=input_map)
+
+
+def randomize_bias(layer, seed=1):
+    if layer.has_bias:
+        rng = np.random.default_rng(seed)
+        layer.bias = rng.normal(0, 0.1, layer.bias.shape).astype(layer.bias.dtype)
