@@ -182,9 +182,6 @@ typedef struct kan_weight {
   const float* scales;  /* device pointer or NULL */
   const float* biases;  /* device pointer or NULL (INT8/INT4 group minimum) */
   const float* codebook;/* device pointer or NULL (INT2) */
-  const void* dense;    /* optional: the same matrix already dequantised to the act dtype
-                         * (device pointer).  Packed formats run the tensor-core path from it;
-                         * the small-batch and SIMT paths decode the packed data. */
 } kan_weight;
 
 /* One KAN layer: y[b, j] = bias[j] + sum_i silu(m(x))[b,i] Wb[j,i]
@@ -210,7 +207,18 @@ typedef struct kan_layer {
   const void* bias;     /* [D_out], act dtype */
   kan_weight w;         /* basis weights [D_out][D_in*K] */
   kan_weight wb;        /* base weights [D_out][D_in] */
+  /* Optional: w and wb already packed by kan_tc_pack() into the tensor-core layout (device
+   * pointer, act dtype).  When NULL the tensor-core path packs into library scratch on every
+   * call; callers that keep weights resident should pack once and pass the buffer here. */
+  const void* tc_weights;
 } kan_layer;
+
+/* Tensor-core weight layout: 64-column blocks of whole input features -- F = 64 / KT features
+ * per block, KT = K + has_base terms per feature (the basis terms, then the base weight), zero
+ * padded -- rows = D_out, in the act dtype.  Packed weights are decoded (exact fp32 values) and
+ * rounded to the act dtype.  kan_tc_packed_bytes() gives the buffer size. */
+int kan_tc_packed_bytes(const kan_layer* layer, size_t* bytes);
+int kan_tc_pack(const kan_layer* layer, void* out, void* stream);
 
 /* Enqueue one layer forward: X [B][D_in] -> Y [B][D_out] (act dtype). */
 int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* stream);

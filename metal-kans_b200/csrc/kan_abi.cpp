@@ -63,6 +63,16 @@ struct PendingCopy {
   size_t bytes;
 };
 
+// Engine scratch of one stream: packed tensor-core weights (when the caller passes none), split-K
+// partial tiles and their arrival counters, GatedKAN gate/up activations.  Kept per stream so
+// that work queued on different streams never shares a buffer.
+enum ScratchId { SC_TCW, SC_PART, SC_CNT, SC_GATE, SC_UP, NUM_SCRATCH };
+struct Scratch {
+  cudaStream_t stream = nullptr;
+  void* ptr[NUM_SCRATCH] = {};
+  size_t cap[NUM_SCRATCH] = {};
+};
+
 struct DeviceState {
   bool init = false;
   cudaStream_t stream = nullptr;
@@ -71,6 +81,7 @@ struct DeviceState {
   size_t slot_cap[NUM_SLOTS] = {};
   std::vector<PendingCopy> pending;     // async-mode results waiting for metal_kan_sync()
   std::vector<std::pair<void*, size_t>> pinned_free;  // reusable pinned buffers
+  std::vector<Scratch*> scratch;        // one per stream that ran the engine
 };
 
 static DeviceState g_dev[MAX_DEVICES];
@@ -118,6 +129,42 @@ static int slot(DeviceState* d, int s, size_t bytes, void** out) {
   return KAN_OK;
 }
 
+static Scratch* scratch_for(DeviceState* d, cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (Scratch* sc : d->scratch)
+    if (sc->stream == s) return sc;
+  Scratch* sc = new Scratch();
+  sc->stream = s;
+  d->scratch.push_back(sc);
+  return sc;
+}
+
+// Grow-only scratch buffer `id` of stream s; new buffers are zeroed when `zero` is set.
+static int scratch_buf(DeviceState* d, cudaStream_t s, int id, size_t bytes, bool zero,
+                       void** out) {
+  Scratch* sc = scratch_for(d, s);
+  if (bytes == 0) bytes = 16;
+  if (sc->cap[id] < bytes) {
+    if (sc->ptr[id]) {
+      KAN_CUDA_TRY(cudaStreamSynchronize(s));
+      cudaFree(sc->ptr[id]);
+      sc->ptr[id] = nullptr;
+      sc->cap[id] = 0;
+    }
+    KAN_CUDA_TRY(cudaMalloc(&sc->ptr[id], bytes));
+    sc->cap[id] = bytes;
+    if (zero) KAN_CUDA_TRY(cudaMemsetAsync(sc->ptr[id], 0, bytes, s));
+  }
+  *out = sc->ptr[id];
+  return KAN_OK;
+}
+
+// After an aborted kernel the split-K counters may be left non-zero: clear them all.
+static void reset_counters(DeviceState* d) {
+  for (Scratch* sc : d->scratch)
+    if (sc->ptr[SC_CNT]) cudaMemset(sc->ptr[SC_CNT], 0, sc->cap[SC_CNT]);
+}
+
 static int stage_in(DeviceState* d, int s, const void* host, size_t bytes, void** dev) {
   int rc = slot(d, s, bytes, dev);
   if (rc) return rc;
@@ -131,6 +178,7 @@ static int check_device_error(DeviceState* d) {
   if (v) {
     int z = 0;
     cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice);
+    reset_counters(d);
     return fail(KAN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
   }
   return KAN_OK;
@@ -245,6 +293,32 @@ static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceSt
   a->w = L->w;
   a->wb = L->wb;
   a->err = d->err_word;
+  a->tc_weights = L->tc_weights;
+  return KAN_OK;
+}
+
+// Tensor-core launch: packs the weights into scratch when the caller did not, and provides the
+// split-K scratch the plan asks for.
+static int run_tc(LayerArgs& a, int act_dtype, cudaStream_t s, DeviceState* d) {
+  const TcPlan p = tc_plan(a);
+  int rc;
+  if (!a.tc_weights) {
+    const TcBlocking bl = tc_blocking(a.D_in, a.K, a.has_base);
+    void* buf;
+    if ((rc = scratch_buf(d, s, SC_TCW, (size_t)bl.NB * 64 * a.D_out * 2, false, &buf))) return rc;
+    cudaError_t e = launch_tc_pack(a, act_dtype, buf, s);
+    if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "weight pack: %s", cudaGetErrorString(e));
+    a.tc_weights = buf;
+  }
+  if (p.splits > 1) {
+    void *part, *cnt;
+    if ((rc = scratch_buf(d, s, SC_PART, p.partial_floats * 4, false, &part))) return rc;
+    if ((rc = scratch_buf(d, s, SC_CNT, p.counters * 4, true, &cnt))) return rc;
+    a.partials = (float*)part;
+    a.counters = (int*)cnt;
+  }
+  cudaError_t e = launch_tc(a, act_dtype, p, s);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "tensor-core launch: %s", cudaGetErrorString(e));
   return KAN_OK;
 }
 
@@ -262,9 +336,8 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
   if (path == KAN_PATH_TC) {
     if (!tc_supported(a, L->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED,
-                  "tensor-core path needs f16/bf16, K<=64, D_in*K %% 8 == 0 (and D_in %% 8 == 0 "
-                  "with a base branch), 16-byte aligned dense weights");
-    e = launch_tc(a, L->act_dtype, s);
+                  "tensor-core path needs an f16/bf16 layer with K + has_base <= 64");
+    return run_tc(a, L->act_dtype, s, d);
   } else if (path == KAN_PATH_SIMT || path == KAN_PATH_GEMV) {
     e = launch_simt(a, L->act_dtype, s);
   } else {
@@ -316,15 +389,40 @@ int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_laye
   const size_t esz = dtype_size(gate->act_dtype);
   const size_t n = (size_t)B * gate->D_out;
   void *g, *u;
-  rc = slot(d, S_T0, n * esz, &g);
-  if (rc) return rc;
-  rc = slot(d, S_T1, n * esz, &u);
-  if (rc) return rc;
+  if ((rc = scratch_buf(d, s, SC_GATE, n * esz, false, &g))) return rc;
+  if ((rc = scratch_buf(d, s, SC_UP, n * esz, false, &u))) return rc;
   if ((rc = run_forward(gate, X, g, B, KAN_PATH_AUTO, s, d))) return rc;
   if ((rc = run_forward(up, X, u, B, KAN_PATH_AUTO, s, d))) return rc;
   cudaError_t e = launch_swiglu(g, u, H, (long long)n, gate->act_dtype, s);
   if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu launch: %s", cudaGetErrorString(e));
   return run_forward(down, H, Y, B, KAN_PATH_AUTO, s, d);
+}
+
+int kan_tc_packed_bytes(const kan_layer* layer, size_t* bytes) {
+  if (!layer || !bytes) return fail(KAN_ERR_ARG, "NULL argument");
+  const int KT = layer->K + (layer->has_base ? 1 : 0);
+  if (layer->D_in <= 0 || layer->D_out <= 0 || layer->K <= 0 || KT > 64)
+    return fail(KAN_ERR_ARG, "tc layout needs D_in, D_out, K > 0 and K + has_base <= 64");
+  const TcBlocking bl = tc_blocking(layer->D_in, layer->K, layer->has_base);
+  *bytes = (size_t)bl.NB * 64 * layer->D_out * 2;
+  return KAN_OK;
+}
+
+int kan_tc_pack(const kan_layer* layer, void* out, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  size_t bytes;
+  if ((rc = kan_tc_packed_bytes(layer, &bytes))) return rc;
+  if (!out) return fail(KAN_ERR_ARG, "tc pack: NULL output");
+  if (layer->act_dtype != KAN_F16 && layer->act_dtype != KAN_BF16)
+    return fail(KAN_ERR_ARG, "tc pack: the tensor-core layout is f16/bf16");
+  LayerArgs a;
+  // X/Y are not used by the pack kernel; B = 0 skips their checks
+  if ((rc = make_args(layer, nullptr, nullptr, 0, d, &a))) return rc;
+  cudaError_t e = launch_tc_pack(a, layer->act_dtype, out, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "tc pack: %s", cudaGetErrorString(e));
+  return KAN_OK;
 }
 
 int kan_dequantize(const kan_weight* w, int rows, int cols, void* out, int out_dtype,

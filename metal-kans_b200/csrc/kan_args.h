@@ -18,6 +18,24 @@ struct LayerArgs {
   const void* bias;
   kan_weight w, wb;
   int* err;  // device error word (set when a bounded wait expires)
+  const void* tc_weights;  // tensor-core layout weights (kan_tc_pack), act dtype
+  // split-K scratch of the tensor-core path: fp32 partial tiles and per-tile arrival counters
+  // (counters start at zero and are reset by the CTA that completes a tile)
+  float* partials;
+  int* counters;
 };
+
+// Feature blocking of the tensor-core weight layout: F whole features of KT terms per 64-column
+// block (KT = K + has_base: the K basis terms, then the base-branch weight).
+struct TcBlocking {
+  int KT, F, NB;
+};
+inline TcBlocking tc_blocking(int D_in, int K, int has_base) {
+  TcBlocking b;
+  b.KT = K + (has_base ? 1 : 0);
+  b.F = b.KT > 0 ? 64 / b.KT : 0;
+  b.NB = b.F > 0 ? (D_in + b.F - 1) / b.F : 0;
+  return b;
+}
 
 }  // namespace kan

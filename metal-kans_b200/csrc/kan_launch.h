@@ -17,9 +17,17 @@ int* device_error_ptr();
 
 // kan_simt.cu
 cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s);
-// kan_tc.cu: returns cudaErrorNotSupported when the shape is outside the kernel's envelope
-cudaError_t launch_tc(const LayerArgs& a, int act_dtype, cudaStream_t s);
+// kan_tc.cu: the tensor-core path.  tc_plan() picks the tile width, the split-K factor and the
+// scratch the launch needs; launch_tc() needs a.tc_weights (the packed layout) and, when
+// splits > 1, a.partials (partial_floats floats) and a.counters (zeroed ints).
+struct TcPlan {
+  int BN, nb, mtiles, ntiles, splits;
+  size_t partial_floats, counters;
+};
 bool tc_supported(const LayerArgs& a, int act_dtype);
+TcPlan tc_plan(const LayerArgs& a);
+cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& plan, cudaStream_t s);
+cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s);
 // kan_misc.cu
 cudaError_t launch_dequantize(const kan_weight& w, int rows, int cols, void* out, int out_dtype,
                               cudaStream_t s);

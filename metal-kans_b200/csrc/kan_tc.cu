@@ -1,21 +1,28 @@
 // kan_tc.cu -- fused KAN layer on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
 //
-// Y[B, D_out] = bias + Phi(x) W^T + silu(x) Wb^T is one dense contraction over
-// K_total = D_in*K (+ D_in for the base branch).  One CTA computes a 128 x BN output tile:
+// Y[B, D_out] = bias + [Phi(x) | silu(x)] Wp^T is one dense contraction.  The weights are first
+// packed (kan_tc_pack / pack_kernel below) into a feature-blocked layout: each 64-column K block
+// holds F = 64 / KT whole input features of KT = K + has_base columns (the K basis terms of the
+// feature, then its base-branch weight), zero padded.  One CTA computes a 128 x BN output tile
+// over a range of K blocks:
 //
-//   warps 0-7  basis producers: evaluate the basis of their rows in registers (the generators of
-//              kan_device.cuh, reference rounding points) and write the 128 x 64 A tile of each
-//              pipeline stage straight into shared memory in the 128-byte-swizzled K-major layout
-//              the MMA reads -- Phi never exists in HBM (the reference writes it to a scratch
-//              buffer and runs MPS GEMMs on it, metal_kan_bridge.mm:503-523).  After the K loop
-//              the same warps are the epilogue: tcgen05.ld of the fp32 accumulator, + bias,
-//              round to the act dtype, store.
-//   warp 8     TMA producer: one cp.async.bulk.tensor.2d per stage for the BN x 64 weight tile
-//              (W for the basis blocks, W_base for the base blocks), out-of-range rows/columns
-//              zero-filled by the tensor map.
+//   warps 0-7  basis producers, two groups of four warps taking alternate pipeline stages; each
+//              thread owns one row of the 128 x 64 A tile: it loads the F inputs of its row,
+//              evaluates their K basis terms and SiLU in registers (the generators of
+//              kan_device.cuh, with the reference's rounding points), and writes the row straight
+//              into shared memory in the 128-byte-swizzled K-major layout the MMA reads.  Phi is
+//              never written to HBM (the reference stores it to a scratch buffer and runs MPS
+//              GEMMs on it, metal_kan_bridge.mm:503-523).  After the K loop these warps are the
+//              epilogue: tcgen05.ld of the fp32 accumulator, + bias, round, store.
+//   warp 8     TMA producer: one cp.async.bulk.tensor.2d per stage for the BN x 64 weight tile.
 //   warp 9     TMEM allocator and MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::f16
-//              (M=128, N=BN, K=16) per stage into a TMEM fp32 accumulator; tcgen05.commit frees
-//              the stage and finally signals the epilogue.
+//              (M=128, N=BN, K=16) per stage into the TMEM accumulator; tcgen05.commit frees the
+//              stage and finally signals the epilogue.
+//
+// Split-K (grid.z > 1) serves grids too small to fill the 148 SMs without recomputing the basis
+// for several N tiles: every split writes its fp32 partial tile to scratch, and the CTA that
+// completes a tile (per-tile arrival counter) sums the partials in split order -- deterministic --
+// adds the bias, stores Y and resets the counter.
 //
 // Every mbarrier wait is bounded (about one second of SM clocks); on expiry the kernel records
 // the error in the device error word, skips its remaining work and still releases TMEM.
@@ -29,13 +36,27 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 16-bit elements = one 128-byte swizzle row
+constexpr int STAGES = 4;              // even: producer group g owns stages g, g+2
 constexpr int A_STAGE_BYTES = BM * BK * 2;
+constexpr int B_STAGE_BYTES = 256 * BK * 2;  // sized for the widest tile (BN = 256)
 constexpr int NUM_PRODUCER_WARPS = 8;
 constexpr int PRODUCER_THREADS = NUM_PRODUCER_WARPS * 32;
 constexpr int TMA_WARP = 8;
 constexpr int MMA_WARP = 9;
 constexpr int THREADS = 320;
+constexpr uint32_t TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;  // ~1 s at the B200 boost clock
+
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
+constexpr int OFF_BAR = OFF_B + STAGES * B_STAGE_BYTES;
+constexpr int NUM_BARS = 3 * STAGES + 1;
+constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
+constexpr int OFF_FLAG = OFF_TMEM + 4;
+constexpr int OFF_LAST = OFF_FLAG + 4;
+constexpr int OFF_STATS = (OFF_LAST + 4 + 15) / 16 * 16;
+constexpr int SMEM_BYTES = OFF_STATS + 2 * BM * 4;
+constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
 
 // ---------------------------------------------------------------------------------------------
 // PTX wrappers
@@ -76,6 +97,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
@@ -136,7 +160,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor, kind::f16: D fp32, A/B f16 (0) or bf16 (1), both K-major, N>>3, M>>4.
-__host__ __device__ constexpr uint32_t instr_desc(int ab_fmt, int n, int m) {
+__device__ __forceinline__ uint32_t instr_desc(int ab_fmt, int n, int m) {
   return (1u << 4) | ((uint32_t)ab_fmt << 7) | ((uint32_t)ab_fmt << 10) |
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
@@ -152,59 +176,175 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-template <int BN, int STAGES>
-struct Layout {
-  static constexpr int B_STAGE_BYTES = BN * BK * 2;
-  static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
-  static constexpr int OFF_BAR = OFF_B + STAGES * B_STAGE_BYTES;
-  static constexpr int NUM_BARS = 3 * STAGES + 1;
-  static constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
-  static constexpr int OFF_FLAG = OFF_TMEM + 4;
-  static constexpr int OFF_STATS = (OFF_FLAG + 4 + 15) / 16 * 16;
-  static constexpr int BYTES = OFF_STATS + 2 * BM * 4;
-  static constexpr int ALLOC = BYTES + 1024;  // slack to align the base to 1024 B
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+// Swizzled address of 16-byte chunk `chunk` of row `r` inside an A stage.
+__device__ __forceinline__ uint32_t a_chunk_off(int r, int chunk) {
+  return (uint32_t)(r * 128 + ((chunk ^ (r & 7)) << 4));
+}
+
+// ---------------------------------------------------------------------------------------------
+// A-tile producers: one row of one 64-column block
+// ---------------------------------------------------------------------------------------------
+
+// Compile-time K: all 64 values live in registers and are stored as 8 swizzled 16-byte chunks.
+template <int BASIS, int MODE, int K, bool HB>
+struct RowProducer {
+  static constexpr int KT = K + (HB ? 1 : 0);
+  static constexpr int F = 64 / KT;
+  using T = typename Act<MODE>::T;
+  float g[K];  // RBF centres (registers)
+
+  __device__ __forceinline__ void setup(const LayerArgs& a) {
+    if (BASIS == KAN_RBF) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) g[k] = __ldg(a.grid + k);
+    }
+  }
+
+  __device__ __forceinline__ void produce(uint8_t* a_stage, int r, const T* xrow, bool valid,
+                                          int blk, const LayerArgs& a, float mean, float rstd) {
+    float v[64];
+    float xs[F];
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int i = blk * F + f;
+      xs[f] = (valid && i < a.D_in) ? Act<MODE>::to_f(xrow[i]) : 0.f;
+    }
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int i = blk * F + f;
+      const bool live = valid && i < a.D_in;
+      const float xm = map_input<MODE>(xs[f], a.input_map, mean, rstd);
+      if (BASIS == KAN_CHEBY) {
+        ChebyGen<MODE> gen;
+        gen.init(xm, i, a);
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[f * KT + k] = gen.next();
+      } else if (BASIS == KAN_RBF) {
+        if (MODE == MODE_F16) {
+          const __half xh = __float2half_rn(xm);
+          const __half ih = __float2half_rn(a.inv_den);
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            __half diff = __hsub(xh, __float2half_rn(g[k]));
+            __half t = __hmul(__hmul(__hneg(diff), diff), ih);
+            v[f * KT + k] = __half2float(__float2half_rn(__expf(__half2float(t))));
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            float d = xm - g[k];
+            v[f * KT + k] = Act<MODE>::round(__expf(-(d * d) * a.inv_den));
+          }
+        }
+      } else if (BASIS == KAN_BSPLINE) {
+        BsplineGen<MODE> gen;
+        gen.init(xm, i, a);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int d = k - gen.span;
+          float val = 0.f;
+          val = (d == 0) ? gen.b0 : val;
+          val = (d == 1) ? gen.b1 : val;
+          val = (d == 2) ? gen.b2 : val;
+          val = (d == 3) ? gen.b3 : val;
+          v[f * KT + k] = val;
+        }
+      } else {
+        WaveletGen<MODE> gen;
+        gen.init(xm, live ? i : 0, a);
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[f * KT + k] = gen.next();
+      }
+      if (HB) v[f * KT + K] = silu_value<MODE>(xm);
+      if (!live) {
+#pragma unroll
+        for (int k = 0; k < KT; ++k) v[f * KT + k] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int c = F * KT; c < 64; ++c) v[c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 pk;
+      pk.x = pack2<MODE>(v[8 * j + 0], v[8 * j + 1]);
+      pk.y = pack2<MODE>(v[8 * j + 2], v[8 * j + 3]);
+      pk.z = pack2<MODE>(v[8 * j + 4], v[8 * j + 5]);
+      pk.w = pack2<MODE>(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) = pk;
+    }
+  }
+};
+
+// Runtime K (any K + has_base <= 64): zero the row, then 2-byte stores of the computed terms.
+template <int BASIS, int MODE>
+struct RowProducerAnyK {
+  using T = typename Act<MODE>::T;
+  __device__ __forceinline__ void setup(const LayerArgs&) {}
+  __device__ __forceinline__ void produce(uint8_t* a_stage, int r, const T* xrow, bool valid,
+                                          int blk, const LayerArgs& a, float mean, float rstd) {
+    using Gen = typename GenFor<BASIS, MODE>::type;
+    const int KT = a.K + (a.has_base ? 1 : 0);
+    const int F = 64 / KT;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) = make_uint4(0, 0, 0, 0);
+    for (int f = 0; f < F; ++f) {
+      const int i = blk * F + f;
+      if (!valid || i >= a.D_in) break;
+      const float xm = map_input<MODE>(Act<MODE>::to_f(xrow[i]), a.input_map, mean, rstd);
+      Gen gen;
+      gen.init(xm, i, a);
+      for (int k = 0; k < KT; ++k) {
+        const float val = (k < a.K) ? gen.next() : silu_value<MODE>(xm);
+        const int c = f * KT + k;
+        T tv = Act<MODE>::from_f(val);
+        *reinterpret_cast<T*>(a_stage + a_chunk_off(r, c >> 3) + (c & 7) * 2) = tv;
+      }
+    }
+  }
 };
 
 // ---------------------------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------------------------
-template <int BASIS, int MODE, int BN, int STAGES>
+template <int BASIS, int MODE, class Producer>
 __global__ void __launch_bounds__(THREADS, 1)
-    kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                  const __grid_constant__ CUtensorMap tmap_wb, LayerArgs a, int n_kb_basis,
-                  int n_kb_base) {
-  using L = Layout<BN, STAGES>;
+    kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, LayerArgs a, int BN, int nb_total,
+                  int splits) {
   using T = typename Act<MODE>::T;
-  using Gen = typename GenFor<BASIS, MODE>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t bar_full_a = s_base + L::OFF_BAR;
+  const uint32_t bar_full_a = s_base + OFF_BAR;
   const uint32_t bar_full_b = bar_full_a + STAGES * 8;
   const uint32_t bar_empty = bar_full_b + STAGES * 8;
   const uint32_t bar_accum = bar_empty + STAGES * 8;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAG);
-  float* s_mean = reinterpret_cast<float*>(smem + L::OFF_STATS);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_FLAG);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_LAST);
+  float* s_mean = reinterpret_cast<float*>(smem + OFF_STATS);
   float* s_rstd = s_mean + BM;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int n_kb = n_kb_basis + n_kb_base;
+  const int z = blockIdx.z;
+  // this split's K blocks: [kb0, kb1)
+  const int kb0 = (int)((long long)nb_total * z / splits);
+  const int kb1 = (int)((long long)nb_total * (z + 1) / splits);
+  const int nj = kb1 - kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full_a + 8 * s, PRODUCER_THREADS);
+      mbar_init(bar_full_a + 8 * s, NUM_PRODUCER_WARPS / 2);
       mbar_init(bar_full_b + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_accum, 1);
     *abort_flag = 0;
+    *last_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == MMA_WARP) tmem_alloc(s_base + L::OFF_TMEM, L::TMEM_COLS);
+  if (warp == MMA_WARP) tmem_alloc(s_base + OFF_TMEM, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -212,7 +352,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp < NUM_PRODUCER_WARPS) {
     // ------------------------------------------------------------------ basis producers
-    const int q = warp & 3, h = warp >> 2;
+    const int q = warp & 3, grp = warp >> 2;
     const int r = q * 32 + lane;
     const int row = m0 + r;
     const bool valid = row < a.B;
@@ -245,77 +385,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           s_rstd[rr] = rstd;
         }
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(PRODUCER_THREADS) : "memory");
+      named_bar(1, PRODUCER_THREADS);
     }
     const float mean = (a.input_map == KAN_MAP_LAYERNORM) ? s_mean[r] : 0.f;
     const float rstd = (a.input_map == KAN_MAP_LAYERNORM) ? s_rstd[r] : 1.f;
-    const int Kdim = a.D_in * a.K;
+    Producer prod;
+    prod.setup(a);
 
-    bool ok = true;
-    for (int kb = 0; kb < n_kb && ok; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t it = (uint32_t)(kb / STAGES);
+    for (int j = grp; j < nj; j += 2) {
+      const int s = j % STAGES;
+      const uint32_t it = (uint32_t)(j / STAGES);
       if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
         *abort_flag = 1;
-        ok = false;
         break;
       }
-      if (*abort_flag) {
-        ok = false;
-        break;
-      }
-      float v[32];
-      if (kb < n_kb_basis) {
-        // warp-uniform walk over columns c_start .. c_start+31 of Phi (column = i*K + k)
-        const int c_start = kb * BK + h * 32;
-        int i = c_start / a.K;
-        int k = c_start - i * a.K;
-        Gen g;
-        bool live = valid && i < a.D_in;
-        {
-          float x = live ? Act<MODE>::to_f(xrow[i]) : 0.f;
-          g.init(map_input<MODE>(x, a.input_map, mean, rstd), i, a);
-          for (int t = 0; t < k; ++t) (void)g.next();
-        }
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = (live && c_start + c < Kdim) ? g.next() : 0.f;
-          if (++k == a.K) {
-            k = 0;
-            ++i;
-            live = valid && i < a.D_in;
-            float x = live ? Act<MODE>::to_f(xrow[i]) : 0.f;
-            g.init(map_input<MODE>(x, a.input_map, mean, rstd), i, a);
-          }
-        }
-      } else {
-        const int f_start = (kb - n_kb_basis) * BK + h * 32;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int f = f_start + c;
-          float val = 0.f;
-          if (valid && f < a.D_in) {
-            float x = Act<MODE>::to_f(xrow[f]);
-            val = silu_value<MODE>(map_input<MODE>(x, a.input_map, mean, rstd));
-          }
-          v[c] = val;
-        }
-      }
-      // 4 x 16-byte chunks into the swizzled K-major A tile (chunk ^= row % 8)
-      uint8_t* a_row = smem + L::OFF_A + s * A_STAGE_BYTES + r * 128;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int chunk = h * 4 + j;
-        uint4 pk;
-        pk.x = pack2<MODE>(v[8 * j + 0], v[8 * j + 1]);
-        pk.y = pack2<MODE>(v[8 * j + 2], v[8 * j + 3]);
-        pk.z = pack2<MODE>(v[8 * j + 4], v[8 * j + 5]);
-        pk.w = pack2<MODE>(v[8 * j + 6], v[8 * j + 7]);
-        *reinterpret_cast<uint4*>(a_row + ((chunk ^ (r & 7)) << 4)) = pk;
-      }
+      if (*abort_flag) break;
+      prod.produce(smem + OFF_A + s * A_STAGE_BYTES, r, xrow, valid, kb0 + j, a, mean, rstd);
       fence_proxy_async_smem();
-      mbar_arrive(bar_full_a + 8 * s);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
     }
 
     // ------------------------------------------------------------------ epilogue
@@ -324,80 +413,151 @@ __global__ void __launch_bounds__(THREADS, 1)
       *abort_flag = 1;
     }
     tc_fence_after();
-    if (!*abort_flag && n_kb > 0) {
-      T* Y = (T*)a.Y;
-      const T* bias = (const T*)a.bias;
-      const bool vec_ok = (a.D_out % 8) == 0;
-      constexpr int HALF = BN / 2;
-#pragma unroll 1
-      for (int cc = 0; cc < HALF; cc += 32) {
-        uint32_t acc[32];
-        const int col_in_tile = h * HALF + cc;
-        tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)col_in_tile, acc);
-        const int col0 = n0 + col_in_tile;
-        if (!valid || col0 >= a.D_out) continue;
-        float out[32];
+    // all epilogue threads must agree on the abort decision before the named barriers below
+    named_bar(3, PRODUCER_THREADS);
+    if (threadIdx.x == 0) *last_flag = *abort_flag ? 2 : 0;
+    named_bar(3, PRODUCER_THREADS);
+    const bool aborted = (*last_flag == 2);
+    named_bar(3, PRODUCER_THREADS);
+    if (threadIdx.x == 0) *last_flag = 0;
+    named_bar(3, PRODUCER_THREADS);
+    const int h = grp;  // column half of the tile
+    const int HALF = BN >> 1;
+    T* Y = (T*)a.Y;
+    const T* bias = (const T*)a.bias;
+    const bool vec_ok = (a.D_out % 8) == 0;
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    float* part = a.partials + (size_t)tile * splits * BM * BN;  // [split][row][col]
+
+    // Store (or accumulate into) Y one 32-column chunk at a time.
+    auto finish_chunk = [&](const float (&out)[32], int col0) {
+      T* yrow = Y + (size_t)row * a.D_out;
+      if (vec_ok && col0 + 32 <= a.D_out) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float b = 0.f;
-          if (a.has_bias && col0 + j < a.D_out) b = Act<MODE>::to_f(bias[col0 + j]);
-          out[j] = __uint_as_float(acc[j]) + b;
+        for (int jj = 0; jj < 4; ++jj) {
+          uint4 pk;
+          pk.x = pack2<MODE>(out[8 * jj + 0], out[8 * jj + 1]);
+          pk.y = pack2<MODE>(out[8 * jj + 2], out[8 * jj + 3]);
+          pk.z = pack2<MODE>(out[8 * jj + 4], out[8 * jj + 5]);
+          pk.w = pack2<MODE>(out[8 * jj + 6], out[8 * jj + 7]);
+          *reinterpret_cast<uint4*>(yrow + col0 + 8 * jj) = pk;
         }
-        T* yrow = Y + (size_t)row * a.D_out;
-        if (vec_ok && col0 + 32 <= a.D_out) {
+      } else {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 pk;
-            pk.x = pack2<MODE>(out[8 * j + 0], out[8 * j + 1]);
-            pk.y = pack2<MODE>(out[8 * j + 2], out[8 * j + 3]);
-            pk.z = pack2<MODE>(out[8 * j + 4], out[8 * j + 5]);
-            pk.w = pack2<MODE>(out[8 * j + 6], out[8 * j + 7]);
-            *reinterpret_cast<uint4*>(yrow + col0 + 8 * j) = pk;
+        for (int jj = 0; jj < 32; ++jj)
+          if (col0 + jj < a.D_out) yrow[col0 + jj] = Act<MODE>::from_f(out[jj]);
+      }
+    };
+    auto bias_of = [&](int col) -> float {
+      return (a.has_bias && col < a.D_out) ? Act<MODE>::to_f(bias[col]) : 0.f;
+    };
+
+    if (!aborted && nj > 0) {
+      if (splits == 1) {
+#pragma unroll 1
+        for (int cc = 0; cc < HALF; cc += 32) {
+          uint32_t acc[32];
+          const int ct = h * HALF + cc;
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
+          const int col0 = n0 + ct;
+          if (!valid || col0 >= a.D_out) continue;
+          float out[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) out[jj] = __uint_as_float(acc[jj]) + bias_of(col0 + jj);
+          finish_chunk(out, col0);
+        }
+      } else {
+        // phase 1: this split's partial tile -> scratch
+#pragma unroll 1
+        for (int cc = 0; cc < HALF; cc += 32) {
+          uint32_t acc[32];
+          const int ct = h * HALF + cc;
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
+          float4* dst = reinterpret_cast<float4*>(part + ((size_t)z * BM + r) * BN + ct);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj)
+            dst[jj] = make_float4(__uint_as_float(acc[4 * jj]), __uint_as_float(acc[4 * jj + 1]),
+                                  __uint_as_float(acc[4 * jj + 2]),
+                                  __uint_as_float(acc[4 * jj + 3]));
+        }
+        __threadfence();
+        named_bar(2, PRODUCER_THREADS);
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(a.counters + tile, 1);
+          *last_flag = (prev == splits - 1) ? 1 : 0;
+        }
+        named_bar(2, PRODUCER_THREADS);
+        if (*last_flag) {
+          __threadfence();
+          // phase 2 (last split to arrive): sum the partials in split order, bias, store
+#pragma unroll 1
+          for (int cc = 0; cc < HALF; cc += 32) {
+            uint32_t acc[32];
+            const int ct = h * HALF + cc;
+            tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
+            const int col0 = n0 + ct;
+            if (!valid || col0 >= a.D_out) continue;
+            float out[32];
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) out[jj] = 0.f;
+            for (int zz = 0; zz < splits; ++zz) {
+              if (zz == z) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) out[jj] += __uint_as_float(acc[jj]);
+              } else {
+                const float4* src =
+                    reinterpret_cast<const float4*>(part + ((size_t)zz * BM + r) * BN + ct);
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                  const float4 p4 = __ldcg(src + jj);
+                  out[4 * jj] += p4.x;
+                  out[4 * jj + 1] += p4.y;
+                  out[4 * jj + 2] += p4.z;
+                  out[4 * jj + 3] += p4.w;
+                }
+              }
+            }
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) out[jj] += bias_of(col0 + jj);
+            finish_chunk(out, col0);
           }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < a.D_out) yrow[col0 + j] = Act<MODE>::from_f(out[j]);
+          if (threadIdx.x == 0) a.counters[tile] = 0;  // ready for the next launch
         }
       }
     }
   } else if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ weight TMA
     if (lane == 0) {
+      const uint32_t bytes = (uint32_t)BN * BK * 2;
       int issued = 0;
-      for (int kb = 0; kb < n_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t it = (uint32_t)(kb / STAGES);
+      for (int j = 0; j < nj; ++j) {
+        const int s = j % STAGES;
+        const uint32_t it = (uint32_t)(j / STAGES);
         if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
-        const uint32_t dst = s_base + L::OFF_B + s * L::B_STAGE_BYTES;
-        mbar_arrive_expect_tx(bar_full_b + 8 * s, L::B_STAGE_BYTES);
-        if (kb < n_kb_basis) tma_load_2d(dst, &tmap_w, bar_full_b + 8 * s, kb * BK, n0);
-        else tma_load_2d(dst, &tmap_wb, bar_full_b + 8 * s, (kb - n_kb_basis) * BK, n0);
+        mbar_arrive_expect_tx(bar_full_b + 8 * s, bytes);
+        tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES, &tmap_w, bar_full_b + 8 * s,
+                    (kb0 + j) * BK, n0);
         ++issued;
       }
       // drain: wait (bounded) for the copies still landing in shared memory
-      for (int kb = issued - 1; kb >= 0 && kb >= issued - STAGES; --kb) {
-        const int s = kb % STAGES;
-        (void)mbar_wait(bar_full_b + 8 * s, (uint32_t)(kb / STAGES) & 1u);
-      }
+      for (int j = issued - 1; j >= 0 && j >= issued - STAGES; --j)
+        (void)mbar_wait(bar_full_b + 8 * (j % STAGES), (uint32_t)(j / STAGES) & 1u);
     }
   } else {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, BN, BM);
-      bool ok = true;
-      for (int kb = 0; kb < n_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t par = (uint32_t)(kb / STAGES) & 1u;
-        if (!mbar_wait(bar_full_a + 8 * s, par)) {
-          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
-          ok = false;
-        } else if (!mbar_wait(bar_full_b + 8 * s, par)) {
+      for (int j = 0; j < nj; ++j) {
+        const int s = j % STAGES;
+        const uint32_t par = (uint32_t)(j / STAGES) & 1u;
+        bool ok = mbar_wait(bar_full_a + 8 * s, par);
+        if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
+        if (ok && !mbar_wait(bar_full_b + 8 * s, par)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
           ok = false;
         }
@@ -406,13 +566,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = s_base + L::OFF_A + s * A_STAGE_BYTES;
-        const uint32_t b_addr = s_base + L::OFF_B + s * L::B_STAGE_BYTES;
+        const uint32_t a_addr = s_base + OFF_A + s * A_STAGE_BYTES;
+        const uint32_t b_addr = s_base + OFF_B + s * B_STAGE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
+        for (int kk = 0; kk < BK / 16; ++kk)
           mma_f16(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
-                  idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-        }
+                  idesc, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(bar_empty + 8 * s);
       }
       // signal the epilogue (also on abort, so that it does not wait out its own limit)
@@ -425,7 +584,31 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == MMA_WARP) {
     tc_fence_after();
-    tmem_dealloc(tmem_d, L::TMEM_COLS);
+    tmem_dealloc(tmem_d, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// weight packing into the feature-blocked tensor-core layout
+// ---------------------------------------------------------------------------------------------
+template <int MODE>
+__global__ void pack_kernel(LayerArgs a, typename Act<MODE>::T* out, int KT, int F, int NB) {
+  const long long cols = (long long)NB * BK;
+  const long long total = cols * a.D_out;
+  const int Kdim = a.D_in * a.K;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(e / cols);
+    const int c = (int)(e - (long long)o * cols);
+    const int b = c / BK, jj = c - b * BK;
+    const int f = jj / KT, t = jj - f * KT;
+    const int i = b * F + f;
+    float v = 0.f;
+    if (f < F && i < a.D_in) {
+      v = (t < a.K) ? weight_value<MODE>(a.w, o, i * a.K + t, Kdim)
+                    : weight_value<MODE>(a.wb, o, i, a.D_in);
+    }
+    out[e] = Act<MODE>::from_f(v);
   }
 }
 
@@ -452,12 +635,12 @@ static EncodeTiledFn get_encode() {
   return fn;
 }
 
-// 2-D tensor map over a row-major [rows][cols] 16-bit matrix, box = 64 columns x box_rows,
-// 128-byte swizzle, zero fill out of range.
-static bool make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int box_rows,
+// 2-D tensor map over the packed [rows][cols] 16-bit matrix, box = 64 columns x box_rows,
+// 128-byte swizzle, zero fill out of range (rows beyond D_out).
+static bool make_tmap(CUtensorMap* m, const void* base, int rows, long long cols, int box_rows,
                       int mode) {
   EncodeTiledFn enc = get_encode();
-  if (!enc) return false;
+  if (!enc || ((uintptr_t)base & 15)) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
@@ -470,84 +653,113 @@ static bool make_tmap(CUtensorMap* m, const void* base, int rows, int cols, int 
   return r == CUDA_SUCCESS;
 }
 
-static const void* tc_weight_ptr(const kan_weight& w) {
-  if (w.format == KAN_W_DENSE) return w.data;
-  return w.dense;
-}
-
-bool tc_supported(const LayerArgs& a, int act_dtype) {
-  if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
-  if (a.B <= 0 || a.D_in <= 0 || a.D_out <= 0 || a.K <= 0 || a.K > 64) return false;
-  const void* w = tc_weight_ptr(a.w);
-  if (!w || ((uintptr_t)w & 15)) return false;
-  if (((long long)a.D_in * a.K) % 8 != 0) return false;
-  if (a.has_base) {
-    const void* wb = tc_weight_ptr(a.wb);
-    if (!wb || ((uintptr_t)wb & 15) || (a.D_in % 8) != 0) return false;
-  }
-  if (!get_encode()) return false;
-  return true;
-}
-
-template <int BASIS, int MODE, int BN, int STAGES>
-static cudaError_t launch_cfg(const CUtensorMap& tw, const CUtensorMap& twb, const LayerArgs& a,
-                              int nkb, int nkb_base, cudaStream_t s) {
-  using L = Layout<BN, STAGES>;
-  auto kern = kan_tc_kernel<BASIS, MODE, BN, STAGES>;
-  static bool configured = false;  // per template instance
+template <int BASIS, int MODE, class Producer>
+static cudaError_t launch_kernel(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
+                                 int splits, dim3 grid, cudaStream_t s) {
+  auto kern = kan_tc_kernel<BASIS, MODE, Producer>;
+  static bool configured = false;  // one per template instance
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::ALLOC);
+                                         SMEM_ALLOC);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((a.D_out + BN - 1) / BN, (a.B + BM - 1) / BM);
-  kern<<<grid, THREADS, L::ALLOC, s>>>(tw, twb, a, nkb, nkb_base);
+  kern<<<grid, THREADS, SMEM_ALLOC, s>>>(tw, a, BN, nb, splits);
   return cudaGetLastError();
 }
 
+// Compile-time-K producers for the shapes the BASELINE configs and common layers use; any other
+// K runs the runtime-K producer.
 template <int BASIS, int MODE>
-static cudaError_t launch_basis(const LayerArgs& a, cudaStream_t s) {
-  const int Kdim = a.D_in * a.K;
-  const int nkb = (Kdim + BK - 1) / BK;
-  const int nkb_base = a.has_base ? (a.D_in + BK - 1) / BK : 0;
-  // Tile width: the widest N whose grid still covers the 148 SMs, else the smallest.
-  const int mt = (a.B + BM - 1) / BM;
-  int bn = 256;
-  if ((long long)mt * ((a.D_out + 255) / 256) < 148 || a.D_out <= 128) bn = 128;
-  if (bn == 128 && ((long long)mt * ((a.D_out + 127) / 128) < 148 || a.D_out <= 64)) bn = 64;
-  CUtensorMap tw, twb;
-  if (!make_tmap(&tw, tc_weight_ptr(a.w), a.D_out, Kdim, bn, MODE)) return cudaErrorInvalidValue;
-  if (a.has_base) {
-    if (!make_tmap(&twb, tc_weight_ptr(a.wb), a.D_out, a.D_in, bn, MODE))
-      return cudaErrorInvalidValue;
+static cudaError_t dispatch_k(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
+                              int splits, dim3 grid, cudaStream_t s) {
+#define KAN_TC_CASE(KK, HBV)                                                                 \
+  if (a.K == KK && (a.has_base != 0) == HBV)                                                 \
+    return launch_kernel<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, a, BN, nb, splits, \
+                                                                         grid, s);
+  if (BASIS == KAN_CHEBY) {
+    KAN_TC_CASE(4, true) KAN_TC_CASE(4, false) KAN_TC_CASE(5, true) KAN_TC_CASE(5, false)
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false) KAN_TC_CASE(9, true) KAN_TC_CASE(9, false)
+  } else if (BASIS == KAN_RBF) {
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
+  } else if (BASIS == KAN_BSPLINE) {
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   } else {
-    twb = tw;
+    KAN_TC_CASE(6, true) KAN_TC_CASE(6, false) KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   }
-  if (bn == 256) return launch_cfg<BASIS, MODE, 256, 4>(tw, twb, a, nkb, nkb_base, s);
-  if (bn == 128) return launch_cfg<BASIS, MODE, 128, 6>(tw, twb, a, nkb, nkb_base, s);
-  return launch_cfg<BASIS, MODE, 64, 8>(tw, twb, a, nkb, nkb_base, s);
+#undef KAN_TC_CASE
+  return launch_kernel<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, a, BN, nb, splits, grid, s);
 }
 
 template <int MODE>
-static cudaError_t launch_mode(const LayerArgs& a, cudaStream_t s) {
+static cudaError_t dispatch_basis(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
+                                  int splits, dim3 grid, cudaStream_t s) {
   switch (a.basis) {
-    case KAN_CHEBY: return launch_basis<KAN_CHEBY, MODE>(a, s);
-    case KAN_RBF: return launch_basis<KAN_RBF, MODE>(a, s);
-    case KAN_BSPLINE: return launch_basis<KAN_BSPLINE, MODE>(a, s);
-    default: return launch_basis<KAN_WAVELET, MODE>(a, s);
+    case KAN_CHEBY: return dispatch_k<KAN_CHEBY, MODE>(tw, a, BN, nb, splits, grid, s);
+    case KAN_RBF: return dispatch_k<KAN_RBF, MODE>(tw, a, BN, nb, splits, grid, s);
+    case KAN_BSPLINE: return dispatch_k<KAN_BSPLINE, MODE>(tw, a, BN, nb, splits, grid, s);
+    default: return dispatch_k<KAN_WAVELET, MODE>(tw, a, BN, nb, splits, grid, s);
   }
 }
 
 }  // namespace tc
 
-bool tc_supported(const LayerArgs& a, int act_dtype) { return tc::tc_supported(a, act_dtype); }
+bool tc_supported(const LayerArgs& a, int act_dtype) {
+  if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
+  if (a.B <= 0 || a.D_in <= 0 || a.D_out <= 0 || a.K <= 0) return false;
+  if (a.K + (a.has_base ? 1 : 0) > 64) return false;
+  return tc::get_encode() != nullptr;
+}
 
-cudaError_t launch_tc(const LayerArgs& a, int act_dtype, cudaStream_t s) {
-  if (!tc::tc_supported(a, act_dtype)) return cudaErrorNotSupported;
+TcPlan tc_plan(const LayerArgs& a) {
+  TcPlan p;
+  p.BN = a.D_out > 128 ? 256 : (a.D_out > 64 ? 128 : 64);
+  const TcBlocking bl = tc_blocking(a.D_in, a.K, a.has_base);
+  p.nb = bl.NB;
+  p.mtiles = (a.B + tc::BM - 1) / tc::BM;
+  p.ntiles = (a.D_out + p.BN - 1) / p.BN;
+  const long long tiles = (long long)p.mtiles * p.ntiles;
+  int splits = 1;
+  if (tiles < 120) {
+    splits = (int)(148 / tiles);
+    splits = splits > 8 ? 8 : splits;
+    const int max_by_k = p.nb / 4;  // keep >= 4 K blocks per split
+    splits = splits > max_by_k ? max_by_k : splits;
+    splits = splits < 1 ? 1 : splits;
+  }
+  p.splits = splits;
+  p.partial_floats = splits > 1 ? (size_t)tiles * splits * tc::BM * p.BN : 0;
+  p.counters = splits > 1 ? (size_t)tiles : 0;
+  return p;
+}
+
+cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& p, cudaStream_t s) {
+  if (!tc_supported(a, act_dtype) || !a.tc_weights) return cudaErrorNotSupported;
+  if (p.splits > 1 && (!a.partials || !a.counters)) return cudaErrorInvalidValue;
+  const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;
+  CUtensorMap tw;
+  if (!tc::make_tmap(&tw, a.tc_weights, a.D_out, (long long)p.nb * tc::BK, p.BN, mode))
+    return cudaErrorInvalidValue;
   note_launch();
-  if (act_dtype == KAN_F16) return tc::launch_mode<MODE_F16>(a, s);
-  return tc::launch_mode<MODE_BF16>(a, s);
+  dim3 grid(p.ntiles, p.mtiles, p.splits);
+  if (mode == MODE_F16) return tc::dispatch_basis<MODE_F16>(tw, a, p.BN, p.nb, p.splits, grid, s);
+  return tc::dispatch_basis<MODE_BF16>(tw, a, p.BN, p.nb, p.splits, grid, s);
+}
+
+cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s) {
+  const TcBlocking bl = tc_blocking(a.D_in, a.K, a.has_base);
+  if (bl.F <= 0) return cudaErrorInvalidValue;
+  note_launch();
+  const long long total = (long long)bl.NB * tc::BK * a.D_out;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
+  if (blocks < 1) blocks = 1;
+  if (act_dtype == KAN_F16)
+    tc::pack_kernel<MODE_F16><<<(int)blocks, 256, 0, s>>>(a, (__half*)out, bl.KT, bl.F, bl.NB);
+  else
+    tc::pack_kernel<MODE_BF16><<<(int)blocks, 256, 0, s>>>(a, (__nv_bfloat16*)out, bl.KT, bl.F,
+                                                          bl.NB);
+  return cudaGetLastError();
 }
 
 }  // namespace kan

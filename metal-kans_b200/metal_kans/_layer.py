@@ -82,11 +82,25 @@ class KANLayerBase(E.DeviceLayerMixin):
             w.data = buf.ptr
             return w
         q._fill_struct(w, keep)
-        if np.dtype(act_np) != np.float32:
-            dense = self._dev(name, act_np)  # dequantised values rounded to the act dtype
-            keep.append(dense)
-            w.dense = dense.ptr
         return w
+
+    def _tc_weights(self, L: D.KanLayer, keep: list) -> None:
+        """Attach the tensor-core weight layout (packed once per weight version)."""
+        if L.act_dtype == D.KAN_F32:
+            return
+        key = (self._version(self.MAIN), self._version("w_base"), L.act_dtype,
+               id(self._packed(self.MAIN)), id(self._packed("w_base")))
+        hit = self.__dict__.get("_tc_cache")
+        if hit is None or hit[0] != key:
+            n = ctypes.c_size_t(0)
+            lib = E.lib()
+            lib.kan_tc_packed_bytes(ctypes.byref(L), ctypes.byref(n))
+            buf = E.DeviceBuffer(n.value)
+            lib.kan_tc_pack(ctypes.byref(L), ctypes.c_void_p(buf.ptr), None)
+            hit = (key, buf)
+            object.__setattr__(self, "_tc_cache", hit)
+        keep.append(hit[1])
+        L.tc_weights = hit[1].ptr
 
     def _descriptor(self, keep: list) -> D.KanLayer:
         act = self.dtype
@@ -108,6 +122,7 @@ class KANLayerBase(E.DeviceLayerMixin):
             keep.append(b)
             L.bias = b.ptr
         self._basis_params(L, keep)
+        self._tc_weights(L, keep)
         return L
 
     # ---- forward -----------------------------------------------------------------------------

@@ -37,7 +37,7 @@ class KanWeight(ctypes.Structure):
 
     _fields_ = [("format", ctypes.c_int32), ("group_size", ctypes.c_int32),
                 ("padded_cols", ctypes.c_int32), ("reserved", ctypes.c_int32),
-                ("data", vp), ("scales", vp), ("biases", vp), ("codebook", vp), ("dense", vp)]
+                ("data", vp), ("scales", vp), ("biases", vp), ("codebook", vp)]
 
 
 class KanLayer(ctypes.Structure):
@@ -50,7 +50,8 @@ class KanLayer(ctypes.Structure):
                 ("grid_size", ctypes.c_int32), ("inv_den", ctypes.c_float),
                 ("grid_min", ctypes.c_float), ("inv_h", ctypes.c_float),
                 ("ln_eps", ctypes.c_float), ("grid", vp), ("translation", vp),
-                ("inv_scale", vp), ("bias", vp), ("w", KanWeight), ("wb", KanWeight)]
+                ("inv_scale", vp), ("bias", vp), ("w", KanWeight), ("wb", KanWeight),
+                ("tc_weights", vp)]
 
 
 # enum values of include/kan_cuda.h
@@ -97,6 +98,8 @@ SIGNATURES = [
     ("kan_forward", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, vp]),
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
+    ("kan_tc_packed_bytes", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(sz)]),
+    ("kan_tc_pack", i32, [ctypes.POINTER(KanLayer), vp, vp]),
     ("kan_dequantize", i32, [ctypes.POINTER(KanWeight), i32, i32, vp, i32, vp]),
     ("kan_swiglu", i32, [vp, vp, vp, i64, i32, vp]),
     ("kan_convert", i32, [vp, i32, vp, i32, i64, vp]),

@@ -490,6 +490,62 @@ def dequantize_int2(packed: np.ndarray, scales: np.ndarray, codebook: np.ndarray
 
 
 # --------------------------------------------------------------------------------------------
+# Timed CPU baseline ("the reference's CPU path")
+# --------------------------------------------------------------------------------------------
+
+def kan_layer_cpu_f32(x, basis: str, W, W_base=None, bias=None, *, K=None, grid=None,
+                      inv_den=None, grid_size=None, grid_min=None, inv_h=None, translation=None,
+                      inv_scale=None, wavelet_type=0, input_map="none"):
+    """float32 NumPy restatement of the reference's fp32 forward, for timing on host cores.
+
+    The reference has no CPU forward (its only backend is Metal); this is its fp32 pipeline --
+    basis kernel (``fused_kan.metal:116-276``) then ``Y = bias + X_silu W_b^T + Phi W^T`` as
+    float32 GEMMs standing in for MPS (``metal_kan_bridge.mm:489-523``) -- in float32 NumPy,
+    the GEMMs through NumPy's BLAS on all host threads.  Used by bench.py only.
+    """
+    x = np.asarray(x, np.float32)
+    if input_map == "tanh":
+        x = np.tanh(x)
+    elif input_map == "layernorm":
+        mu = x.mean(axis=1, keepdims=True)
+        var = ((x - mu) ** 2).mean(axis=1, keepdims=True)
+        x = (x - mu) / np.sqrt(var + np.float32(1e-5))
+    B, D = x.shape
+    if basis == "cheby":
+        xc = np.clip(x, -1.0, 1.0)
+        phi = np.empty((B, D, K), np.float32)
+        phi[..., 0] = 1.0
+        if K > 1:
+            phi[..., 1] = xc
+        for k in range(2, K):
+            phi[..., k] = 2.0 * xc * phi[..., k - 1] - phi[..., k - 2]
+    elif basis == "rbf":
+        d = x[:, :, None] - np.asarray(grid, np.float32)[None, None, :]
+        phi = np.exp(-(d * d) * np.float32(inv_den))
+    elif basis == "bspline":
+        pos = (x - np.float32(grid_min)) * np.float32(inv_h)
+        span = np.clip(np.floor(pos), 0, grid_size - 1).astype(np.int64)
+        u = np.clip(pos - span, 0.0, 1.0).astype(np.float32)
+        om = 1.0 - u
+        phi = np.zeros((B, D, grid_size + 3), np.float32)
+        bi, di = np.meshgrid(np.arange(B), np.arange(D), indexing="ij")
+        for j, bj in enumerate((om ** 3 / 6, (3 * u ** 3 - 6 * u ** 2 + 4) / 6,
+                                (-3 * u ** 3 + 3 * u ** 2 + 3 * u + 1) / 6, u ** 3 / 6)):
+            phi[bi, di, span + j] = bj
+    else:
+        z = (x[:, :, None] - translation[None]) * inv_scale[None]
+        e = np.exp(-0.5 * z * z)
+        phi = ((1 - z * z) * e if wavelet_type == 0 else
+               (np.cos(5 * z) * e if wavelet_type == 1 else -z * e)).astype(np.float32)
+    y = phi.reshape(B, -1) @ np.asarray(W, np.float32).T
+    if W_base is not None:
+        y += (x / (1.0 + np.exp(-x))) @ np.asarray(W_base, np.float32).T
+    if bias is not None:
+        y += np.asarray(bias, np.float32)[None, :]
+    return y
+
+
+# --------------------------------------------------------------------------------------------
 # Error metric
 # --------------------------------------------------------------------------------------------
 
@@ -501,3 +557,30 @@ def max_rel_err(y, y_ref) -> float:
     if den == 0:
         return float(np.max(np.abs(y)))
     return float(np.max(np.abs(y - r)) / den)
+
+
+_MANT_BITS = {"f32": 23, "f16": 10, "bf16": 7}
+
+
+def half_ulp(v, mode: str) -> np.ndarray:
+    """Half a unit in the last place of |v| in the output dtype of ``mode`` (normal range)."""
+    a = np.abs(np.asarray(v, np.float64))
+    e = np.floor(np.log2(np.maximum(a, 1e-30)))
+    return 0.5 * np.exp2(e - _MANT_BITS[mode])
+
+
+def max_rel_err_rounded(y, y_ref64, mode: str) -> float:
+    """Error of an output rounded to the dtype of ``mode`` against the UNROUNDED oracle value:
+    max over elements of (|y - ref| - half_ulp(ref))_+ / max |ref|.
+
+    The BASELINE tolerance (2e-3 for fp16/bf16 operands with fp32 accumulation, 1e-5 for fp32)
+    budgets the computation; the final rounding of the result to its own dtype is allowed on
+    top, half an ulp -- which alone can reach 2^-8 relative for bf16 (8 significant bits), so a
+    flat 2e-3 on rounded bf16 outputs would be unattainable by any implementation."""
+    y = np.asarray(y, np.float64)
+    r = np.asarray(y_ref64, np.float64)
+    den = np.max(np.abs(r))
+    excess = np.maximum(np.abs(y - r) - half_ulp(r, mode), 0.0)
+    if den == 0:
+        return float(np.max(excess))
+    return float(np.max(excess) / den)

@@ -146,11 +146,15 @@ def block_goldens(mk):
             l = getattr(blk, nm)
             rec[f"gated_{mode}/{nm}.w_cheby"] = l.w_cheby
             rec[f"gated_{mode}/{nm}.w_base"] = l.w_base
-    # INT4-quantised GatedKAN (to_int4 replaces weights by the dequantised fp32 arrays)
+    # INT4-quantised GatedKAN (to_int4 replaces weights by the dequantised fp32 arrays).
+    # Row lengths are multiples of the group size (like the BASELINE config-4 shapes): when they
+    # are not, the reference's QuantizedWeight.dequantize returns a non-contiguous slice of the
+    # padded matrix (quantization.py:123) whose raw pointer the layer forward then hands to the
+    # bridge, which reads the rows misaligned -- a reference defect the engine does not copy.
     np.random.seed(3)
-    blk = mk.GatedKAN(d_model=32, d_ffn=64, degree=5)
+    blk = mk.GatedKAN(d_model=64, d_ffn=128, degree=5)
     blk.to_int4(group_size=64)
-    x = np.random.normal(0, 1, (10, 32)).astype(np.float32)
+    x = np.random.normal(0, 1, (10, 64)).astype(np.float32)
     rec["gated_int4/x"] = x
     rec["gated_int4/y"] = blk(x)
     for nm in ("gate_kan", "up_kan", "down_kan"):

@@ -18,7 +18,7 @@ def set_mode(layer, mode):
     return layer
 
 
-def oracle_for_layer(layer, x, mode, basis):
+def oracle_for_layer(layer, x, mode, basis, out_round=True):
     """Oracle output for an engine layer object (reads its current weights)."""
     import metal_kans as mk  # noqa: F401
 
@@ -35,7 +35,13 @@ def oracle_for_layer(layer, x, mode, basis):
                   inv_scale=np.asarray(layer._inv_scale).astype(np.float32),
                   wavelet_type=layer.wavelet_type)
     return O.kan_layer(x, basis, mode, W, wb, b, K=layer._terms(),
-                       input_map=getattr(layer, "input_map", "none"), **kw)
+                       input_map=getattr(layer, "input_map", "none"), out_round=out_round, **kw)
+
+
+def layer_err(y, layer, x, mode, basis):
+    """Engine output vs the unrounded oracle, final output rounding allowed (half an ulp)."""
+    ref = oracle_for_layer(layer, x, mode, basis, out_round=False)
+    return O.max_rel_err_rounded(np.asarray(y).astype(np.float64), ref, mode)
 
 
 def make_layer(basis, d_in, d_out, K, *, bias=True, use_base=True, input_map="none", seed=0,

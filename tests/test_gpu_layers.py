@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 from conftest import group, load_npz
-from kan_cases import TOL, make_layer, oracle_for_layer, randomize_bias, set_mode
+from kan_cases import TOL, layer_err, make_layer, oracle_for_layer, randomize_bias, set_mode
 from oracle import kan_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -104,8 +104,7 @@ def test_random_layers_vs_oracle(mk, shape, mode, path):
     lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
     x = rng.uniform(lo, hi, (B, d_in)).astype(np.float32)
     y = layer.forward(x, path=PATHS[path])
-    ref = oracle_for_layer(layer, x, mode, basis)
-    err = O.max_rel_err(y, ref)
+    err = layer_err(y, layer, x, mode, basis)
     assert err <= TOL[mode], f"{shape} {mode} {path}: {err:.3e}"
 
 
@@ -122,8 +121,7 @@ def test_layernorm_fastkan(mk, mode, path):
     set_mode(l, mode)
     x = rng.normal(0, 1, (640, 256)).astype(np.float32)
     y = l.forward(x, path=PATHS[path])
-    ref = oracle_for_layer(l, x, mode, "rbf")
-    assert O.max_rel_err(y, ref) <= TOL[mode]
+    assert layer_err(y, l, x, mode, "rbf") <= TOL[mode]
 
 
 @pytest.mark.parametrize("wt", ["mexican_hat", "morlet", "dog"])
@@ -132,7 +130,7 @@ def test_wavelet_types(mk, wt, mode):
     layer = set_mode(make_layer("wavelet", 16, 24, 6, seed=3, wavelet_type=wt), mode)
     x = np.random.default_rng(2).uniform(-1, 1, (96, 16)).astype(np.float32)
     y = layer(x)
-    assert O.max_rel_err(y, oracle_for_layer(layer, x, mode, "wavelet")) <= TOL[mode]
+    assert layer_err(y, layer, x, mode, "wavelet") <= TOL[mode]
 
 
 def test_edge_inputs(mk):
@@ -148,7 +146,7 @@ def test_edge_inputs(mk):
     xb = np.array([[-1.0, -0.999, 0.0, 0.999, 1.0, -0.5, 0.5, 30.0]] * 4, np.float16)
     y = c(xb)
     assert np.isfinite(y.astype(np.float32)).all()  # tests/test_optimizations.py:16-26
-    assert O.max_rel_err(y, oracle_for_layer(c, xb, "f16", "cheby")) <= TOL["f16"]
+    assert layer_err(y, c, xb, "f16", "cheby") <= TOL["f16"]
 
 
 def test_bad_arguments_raise(mk):
