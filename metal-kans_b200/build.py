@@ -28,8 +28,14 @@ NVCC_COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", IN
 # Host quantisers must round once per source operation (no fma contraction).
 CXX_FLAGS = ["-Xcompiler", "-ffp-contract=off"]
 
-SOURCES = ["kan_abi.cpp", "kan_misc.cu", "kan_simt.cu", "kan_tc.cu"]
-HEADERS = ["kan_device.cuh", "kan_launch.h", "kan_args.h"]
+# (source, object name, extra defines): the tensor-core kernels are instantiated once per
+# (activation dtype, basis) in separate translation units so that they compile in parallel.
+SOURCES = [("kan_abi.cpp", "kan_abi", []), ("kan_misc.cu", "kan_misc", []),
+           ("kan_simt.cu", "kan_simt", []), ("kan_tc.cu", "kan_tc", [])] + [
+    ("kan_tc_inst.cu", f"kan_tc_inst_{m}_{b}", [f"-DKAN_TC_MODE={m}", f"-DKAN_TC_BASIS={b}"])
+    for m in (1, 2) for b in (0, 1, 2, 3)]
+HEADERS = ["kan_device.cuh", "kan_launch.h", "kan_args.h", "kan_tc_kernel.cuh",
+           "kan_tc_dispatch.h"]
 
 
 def nvcc() -> str:
@@ -46,13 +52,14 @@ def _newer(src_paths, target):
     return any(os.path.getmtime(p) > t for p in src_paths)
 
 
-def _compile(src: str, verbose: bool) -> str:
+def _compile(spec, verbose: bool) -> str:
+    src, name, defines = spec
     path = os.path.join(CSRC, src)
-    obj = os.path.join(BUILD, src + ".o")
+    obj = os.path.join(BUILD, name + ".o")
     deps = [path] + [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "kan_cuda.h")]
     if not _newer(deps, obj):
         return obj
-    cmd = [nvcc(), *ARCH, *NVCC_COMMON, "-c", path, "-o", obj]
+    cmd = [nvcc(), *ARCH, *NVCC_COMMON, *defines, "-c", path, "-o", obj]
     if src.endswith(".cpp"):
         cmd += CXX_FLAGS
     else:
@@ -65,7 +72,7 @@ def _compile(src: str, verbose: bool) -> str:
     return obj
 
 
-def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> str:
+def build(force: bool = False, jobs: int = 8, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     os.makedirs(OUT_DIR, exist_ok=True)
     if force:
@@ -84,7 +91,7 @@ def build(force: bool = False, jobs: int = 4, verbose: bool = False) -> str:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
-    ap.add_argument("-j", type=int, default=4)
+    ap.add_argument("-j", type=int, default=8)
     ap.add_argument("-v", action="store_true", help="print ptxas resource usage")
     a = ap.parse_args()
     print(build(force=a.force, jobs=a.j, verbose=a.v))

@@ -63,10 +63,10 @@ struct PendingCopy {
   size_t bytes;
 };
 
-// Engine scratch of one stream: packed tensor-core weights (when the caller passes none), split-K
-// partial tiles and their arrival counters, GatedKAN gate/up activations.  Kept per stream so
-// that work queued on different streams never shares a buffer.
-enum ScratchId { SC_TCW, SC_PART, SC_CNT, SC_GATE, SC_UP, NUM_SCRATCH };
+// Engine scratch of one stream: packed tensor-core weights (when the caller passes none) and the
+// GatedKAN gate/up activations.  Kept per stream so that work queued on different streams never
+// shares a buffer.
+enum ScratchId { SC_TCW, SC_GATE, SC_UP, NUM_SCRATCH };
 struct Scratch {
   cudaStream_t stream = nullptr;
   void* ptr[NUM_SCRATCH] = {};
@@ -159,12 +159,6 @@ static int scratch_buf(DeviceState* d, cudaStream_t s, int id, size_t bytes, boo
   return KAN_OK;
 }
 
-// After an aborted kernel the split-K counters may be left non-zero: clear them all.
-static void reset_counters(DeviceState* d) {
-  for (Scratch* sc : d->scratch)
-    if (sc->ptr[SC_CNT]) cudaMemset(sc->ptr[SC_CNT], 0, sc->cap[SC_CNT]);
-}
-
 static int stage_in(DeviceState* d, int s, const void* host, size_t bytes, void** dev) {
   int rc = slot(d, s, bytes, dev);
   if (rc) return rc;
@@ -178,7 +172,6 @@ static int check_device_error(DeviceState* d) {
   if (v) {
     int z = 0;
     cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice);
-    reset_counters(d);
     return fail(KAN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
   }
   return KAN_OK;
@@ -297,8 +290,7 @@ static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceSt
   return KAN_OK;
 }
 
-// Tensor-core launch: packs the weights into scratch when the caller did not, and provides the
-// split-K scratch the plan asks for.
+// Tensor-core launch: packs the weights into scratch when the caller did not.
 static int run_tc(LayerArgs& a, int act_dtype, cudaStream_t s, DeviceState* d) {
   const TcPlan p = tc_plan(a);
   int rc;
@@ -309,13 +301,6 @@ static int run_tc(LayerArgs& a, int act_dtype, cudaStream_t s, DeviceState* d) {
     cudaError_t e = launch_tc_pack(a, act_dtype, buf, s);
     if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "weight pack: %s", cudaGetErrorString(e));
     a.tc_weights = buf;
-  }
-  if (p.splits > 1) {
-    void *part, *cnt;
-    if ((rc = scratch_buf(d, s, SC_PART, p.partial_floats * 4, false, &part))) return rc;
-    if ((rc = scratch_buf(d, s, SC_CNT, p.counters * 4, true, &cnt))) return rc;
-    a.partials = (float*)part;
-    a.counters = (int*)cnt;
   }
   cudaError_t e = launch_tc(a, act_dtype, p, s);
   if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "tensor-core launch: %s", cudaGetErrorString(e));

@@ -19,10 +19,6 @@ struct LayerArgs {
   kan_weight w, wb;
   int* err;  // device error word (set when a bounded wait expires)
   const void* tc_weights;  // tensor-core layout weights (kan_tc_pack), act dtype
-  // split-K scratch of the tensor-core path: fp32 partial tiles and per-tile arrival counters
-  // (counters start at zero and are reset by the CTA that completes a tile)
-  float* partials;
-  int* counters;
 };
 
 // Feature blocking of the tensor-core weight layout: F whole features of KT terms per 64-column

@@ -17,12 +17,11 @@ int* device_error_ptr();
 
 // kan_simt.cu
 cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s);
-// kan_tc.cu: the tensor-core path.  tc_plan() picks the tile width, the split-K factor and the
-// scratch the launch needs; launch_tc() needs a.tc_weights (the packed layout) and, when
-// splits > 1, a.partials (partial_floats floats) and a.counters (zeroed ints).
+// kan_tc.cu: the tensor-core path.  tc_plan() picks the tile width and the split-K factor (the
+// split CTAs of a tile form a cluster and reduce through distributed shared memory);
+// launch_tc() needs a.tc_weights (the packed layout).
 struct TcPlan {
   int BN, nb, mtiles, ntiles, splits;
-  size_t partial_floats, counters;
 };
 bool tc_supported(const LayerArgs& a, int act_dtype);
 TcPlan tc_plan(const LayerArgs& a);

@@ -1,0 +1,735 @@
+// kan_tc_kernel.cuh -- fused KAN layer on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Y[B, D_out] = bias + [Phi(x) | silu(x)] Wp^T is one dense contraction.  The weights are packed
+// once (kan_tc_pack) into a feature-blocked layout: each 64-column K block holds F = 64 / KT whole
+// input features of KT = K + has_base columns (the K basis terms of the feature, then its
+// base-branch weight), zero padded.  One CTA computes a 128 x BN output tile over a range of K
+// blocks:
+//
+//   warps 0-7  basis producers, two groups of four warps taking alternate pipeline stages; each
+//              thread owns one row of the 128 x 64 A tile.  It prefetches the inputs of its next
+//              block into registers, evaluates the K basis terms and SiLU of the block's F
+//              features in registers (reference rounding points, see kan_device.cuh) and stores
+//              the row as eight 16-byte chunks in the 128-byte-swizzled K-major layout the MMA
+//              reads.  Phi never reaches HBM (the reference writes it to a scratch buffer and runs
+//              MPS GEMMs on it, metal_kan_bridge.mm:503-523).  After the K loop these warps run
+//              the epilogue: tcgen05.ld of the fp32 accumulator, + bias, round, store.
+//   warp 8     TMA producer: one cp.async.bulk.tensor.2d per stage for the BN x 64 weight tile.
+//   warp 9     TMEM allocator and MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::f16
+//              (M=128, N=BN, K=16) per stage into the TMEM accumulator; tcgen05.commit frees the
+//              stage and finally signals the epilogue.
+//
+// Split-K (grid.z = S > 1, launched as clusters of S CTAs along z) serves grids too small to fill
+// the 148 SMs without recomputing the basis per N tile: each CTA of the cluster parks its fp32
+// partial tile in its own shared memory, and CTA z then reduces column slice z of the tile over
+// the S partials read through distributed shared memory, always in split order (deterministic),
+// adds the bias and stores Y.  No global scratch is involved.
+//
+// Every mbarrier wait is bounded (about one second of SM clocks); on expiry the kernel records
+// the error in the device error word, skips its remaining work, still joins every CTA-wide and
+// cluster-wide barrier and releases TMEM.
+#pragma once
+
+#include <cuda.h>
+
+#include "kan_device.cuh"
+#include "kan_launch.h"
+
+namespace kan {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;                 // 64 16-bit elements = one 128-byte swizzle row
+constexpr int STAGES = 4;              // even: producer group g owns stages g, g+2
+constexpr int A_STAGE_BYTES = BM * BK * 2;
+constexpr int B_STAGE_BYTES = 256 * BK * 2;  // sized for the widest tile (BN = 256)
+constexpr int NUM_PRODUCER_WARPS = 8;
+constexpr int PRODUCER_THREADS = NUM_PRODUCER_WARPS * 32;
+constexpr int TMA_WARP = 8;
+constexpr int MMA_WARP = 9;
+constexpr int THREADS = 320;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;  // ~1 s at the B200 boost clock
+constexpr int MAX_SPLITS = 8;                          // portable cluster size
+
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
+constexpr int OFF_BAR = OFF_B + STAGES * B_STAGE_BYTES;
+constexpr int NUM_BARS = 3 * STAGES + 1;
+constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
+constexpr int OFF_FLAG = OFF_TMEM + 4;
+constexpr int OFF_EPI = OFF_FLAG + 4;
+constexpr int OFF_STATS = (OFF_EPI + 4 + 15) / 16 * 16;    // LayerNorm partial sums / stats
+constexpr int SMEM_BYTES = OFF_STATS + 4 * BM * 4;
+constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
+// split-K partial tile [128][BN + 4] fp32, parked over the (finished) pipeline buffers
+constexpr int PART_STRIDE = 256 + 4;
+static_assert(BM * PART_STRIDE * 4 <= OFF_BAR, "partial tile must fit in the stage buffers");
+
+// ---------------------------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity`; false when the limit expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+  }
+  return true;
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row core groups 1024 B
+// apart (SBO), LBO unused for swizzled K-major (encoded 1), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: D fp32, A/B f16 (0) or bf16 (1), both K-major, N>>3, M>>4.
+__device__ __forceinline__ uint32_t instr_desc(int ab_fmt, int n, int m) {
+  return (1u << 4) | ((uint32_t)ab_fmt << 7) | ((uint32_t)ab_fmt << 10) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Round two fp32 values (RNE) into one 32-bit pair of the operand dtype, low half first.
+template <int MODE>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if (MODE == MODE_F16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// Swizzled address of 16-byte chunk `chunk` of row `r` inside an A stage.
+__device__ __forceinline__ uint32_t a_chunk_off(int r, int chunk) {
+  return (uint32_t)(r * 128 + ((chunk ^ (r & 7)) << 4));
+}
+
+// ---------------------------------------------------------------------------------------------
+// LayerNorm statistics: the two owner threads of a row (one per producer group) each sum one half
+// of the row -- shifted by the row's first value, so that the one-pass variance keeps its
+// precision when |mean| >> std -- and combine through shared memory.
+// ---------------------------------------------------------------------------------------------
+template <int MODE>
+__device__ __forceinline__ void ln_partial(const typename Act<MODE>::T* xrow, bool valid,
+                                           int D_in, int half, float& s, float& ss,
+                                           float& pivot) {
+  using T = typename Act<MODE>::T;
+  s = 0.f;
+  ss = 0.f;
+  pivot = valid ? Act<MODE>::to_f(xrow[0]) : 0.f;
+  if (!valid) return;
+  const int lo = half ? D_in / 2 : 0, hi = half ? D_in : D_in / 2;
+  const bool vec = ((D_in & 15) == 0) && ((((uintptr_t)xrow) & 15) == 0);
+  if (vec) {
+    // 16-byte loads, 4 in flight
+    for (int c = lo; c < hi; c += 32) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        raw[u] = (c + 8 * u < hi) ? *reinterpret_cast<const uint4*>(xrow + c + 8 * u)
+                                  : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (c + 8 * u >= hi) continue;
+        const T* e = reinterpret_cast<const T*>(&raw[u]);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float d = Act<MODE>::to_f(e[t]) - pivot;
+          s += d;
+          ss = fmaf(d, d, ss);
+        }
+      }
+    }
+  } else {
+    for (int c = lo; c < hi; ++c) {
+      const float d = Act<MODE>::to_f(xrow[c]) - pivot;
+      s += d;
+      ss = fmaf(d, d, ss);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// A-tile producers: one row of one 64-column block
+// ---------------------------------------------------------------------------------------------
+
+// Compile-time K: the F inputs of the next block are prefetched into registers while the current
+// block is evaluated; all 64 values live in registers and are rounded once, when packed.
+template <int BASIS, int MODE, int K, bool HB>
+struct RowProducer {
+  static constexpr int KT = K + (HB ? 1 : 0);
+  static constexpr int F = 64 / KT;
+  using T = typename Act<MODE>::T;
+  float g[K];                // RBF centres
+  __half2 gh2[(K + 1) / 2];  // fp16 mode: centres as half pairs
+  __half2 neg_inv2;          // fp16 mode: -inv_den as halves
+  float xn[F];               // prefetched raw inputs of the next block
+
+  __device__ __forceinline__ void setup(const LayerArgs& a) {
+    if (BASIS == KAN_RBF) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) g[k] = __ldg(a.grid + k);
+      if (MODE == MODE_F16) {
+#pragma unroll
+        for (int j = 0; j < (K + 1) / 2; ++j)
+          gh2[j] = __floats2half2_rn(g[2 * j], 2 * j + 1 < K ? g[2 * j + 1] : 0.f);
+        neg_inv2 = __float2half2_rn(-a.inv_den);
+      }
+    }
+  }
+
+  // Inputs of features blk*F .. blk*F+F-1 (0 for rows >= B or features >= D_in: their packed
+  // weights are zero and every basis value of 0 is finite, so they contribute nothing).
+  __device__ __forceinline__ void prefetch(const T* xrow, bool valid, int blk, int D_in) {
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int i = blk * F + f;
+      xn[f] = (valid && i < D_in) ? Act<MODE>::to_f(xrow[i]) : 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void produce(uint8_t* a_stage, int r, const float (&xs)[F],
+                                          int blk, const LayerArgs& a, float mean, float rstd) {
+    float xm[F];
+    if (a.input_map == KAN_MAP_LAYERNORM) {
+#pragma unroll
+      for (int f = 0; f < F; ++f) xm[f] = Act<MODE>::round((xs[f] - mean) * rstd);
+    } else if (a.input_map == KAN_MAP_TANH) {
+#pragma unroll
+      for (int f = 0; f < F; ++f) xm[f] = Act<MODE>::round(tanhf(xs[f]));
+    } else {
+#pragma unroll
+      for (int f = 0; f < F; ++f) xm[f] = xs[f];
+    }
+    float v[64];
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      float* vf = v + f * KT;
+      if (BASIS == KAN_CHEBY) {
+        // T_k(clamp(x)) by the fp32 recurrence; the stored value is rounded at pack time
+        const float xc = fminf(fmaxf(xm[f], -1.0f), 1.0f);
+        const float x2 = 2.0f * xc;
+        float t0 = 1.0f, t1 = xc;
+        vf[0] = 1.0f;
+        if (K > 1) vf[1] = xc;
+#pragma unroll
+        for (int k = 2; k < K; ++k) {
+          const float t2 = fmaf(x2, t1, -t0);
+          vf[k] = t2;
+          t0 = t1;
+          t1 = t2;
+        }
+      } else if (BASIS == KAN_RBF) {
+        if (MODE == MODE_F16) {
+          // reference half arithmetic two centres at a time: diff = x - c and
+          // (-diff*diff) * inv_den (computed as (diff*diff) * -inv_den: the same rounded value),
+          // then exp of the half argument in fp32
+          const __half2 xh2 = __float2half2_rn(xm[f]);
+#pragma unroll
+          for (int j = 0; j < (K + 1) / 2; ++j) {
+            const __half2 diff = __hsub2(xh2, gh2[j]);
+            const __half2 t = __hmul2(__hmul2(diff, diff), neg_inv2);
+            const float2 tf = __half22float2(t);
+            vf[2 * j] = __expf(tf.x);
+            if (2 * j + 1 < K) vf[2 * j + 1] = __expf(tf.y);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            const float d = xm[f] - g[k];
+            vf[k] = __expf(-(d * d) * a.inv_den);
+          }
+        }
+      } else if (BASIS == KAN_BSPLINE) {
+        BsplineGen<MODE> gen;
+        gen.init(xm[f], 0, a);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          const int d = k - gen.span;
+          float val = 0.f;
+          val = (d == 0) ? gen.b0 : val;
+          val = (d == 1) ? gen.b1 : val;
+          val = (d == 2) ? gen.b2 : val;
+          val = (d == 3) ? gen.b3 : val;
+          vf[k] = val;
+        }
+      } else {
+        WaveletGen<MODE> gen;
+        gen.init(xm[f], min(blk * F + f, a.D_in - 1), a);
+#pragma unroll
+        for (int k = 0; k < K; ++k) vf[k] = gen.next();
+      }
+      if (HB) vf[K] = silu_value<MODE>(xm[f]);
+    }
+#pragma unroll
+    for (int c = F * KT; c < 64; ++c) v[c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint4 pk;
+      pk.x = pack2<MODE>(v[8 * j + 0], v[8 * j + 1]);
+      pk.y = pack2<MODE>(v[8 * j + 2], v[8 * j + 3]);
+      pk.z = pack2<MODE>(v[8 * j + 4], v[8 * j + 5]);
+      pk.w = pack2<MODE>(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) = pk;
+    }
+  }
+};
+
+// Runtime K (any K + has_base <= 64): zero the row, then 2-byte stores of the computed terms.
+template <int BASIS, int MODE>
+struct RowProducerAnyK {
+  static constexpr int F = 1;
+  using T = typename Act<MODE>::T;
+  float xn[1];  // unused: this producer loads its inputs itself
+  const T* xrow_;
+  bool valid_;
+  __device__ __forceinline__ void setup(const LayerArgs&) {}
+  __device__ __forceinline__ void prefetch(const T* xrow, bool valid, int, int) {
+    xrow_ = xrow;
+    valid_ = valid;
+  }
+  __device__ __forceinline__ void produce(uint8_t* a_stage, int r, const float (&)[F], int blk,
+                                          const LayerArgs& a, float mean, float rstd) {
+    using Gen = typename GenFor<BASIS, MODE>::type;
+    const int KT = a.K + (a.has_base ? 1 : 0);
+    const int Fr = 64 / KT;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) = make_uint4(0, 0, 0, 0);
+    for (int f = 0; f < Fr; ++f) {
+      const int i = blk * Fr + f;
+      if (!valid_ || i >= a.D_in) break;
+      const float xm = map_input<MODE>(Act<MODE>::to_f(xrow_[i]), a.input_map, mean, rstd);
+      Gen gen;
+      gen.init(xm, i, a);
+      for (int k = 0; k < KT; ++k) {
+        const float val = (k < a.K) ? gen.next() : silu_value<MODE>(xm);
+        const int c = f * KT + k;
+        *reinterpret_cast<T*>(a_stage + a_chunk_off(r, c >> 3) + (c & 7) * 2) =
+            Act<MODE>::from_f(val);
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------------------------
+template <int BASIS, int MODE, class Producer>
+__global__ void __launch_bounds__(THREADS, 1)
+    kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, LayerArgs a, int BN, int nb_total,
+                  int splits) {
+  using T = typename Act<MODE>::T;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t bar_full_a = s_base + OFF_BAR;
+  const uint32_t bar_full_b = bar_full_a + STAGES * 8;
+  const uint32_t bar_empty = bar_full_b + STAGES * 8;
+  const uint32_t bar_accum = bar_empty + STAGES * 8;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_FLAG);
+  volatile int* epi_flag = reinterpret_cast<volatile int*>(smem + OFF_EPI);
+  float* s_stats = reinterpret_cast<float*>(smem + OFF_STATS);  // [4][BM]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int z = blockIdx.z;
+  // this split's K blocks: [kb0, kb1)
+  const int kb0 = (int)((long long)nb_total * z / splits);
+  const int kb1 = (int)((long long)nb_total * (z + 1) / splits);
+  const int nj = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full_a + 8 * s, NUM_PRODUCER_WARPS / 2);
+      mbar_init(bar_full_b + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_accum, 1);
+    *abort_flag = 0;
+    *epi_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == MMA_WARP) tmem_alloc(s_base + OFF_TMEM, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp < NUM_PRODUCER_WARPS) {
+    // ------------------------------------------------------------------ basis producers
+    const int q = warp & 3, grp = warp >> 2;
+    const int r = q * 32 + lane;
+    const int row = m0 + r;
+    const bool valid = row < a.B;
+    const T* xrow = (const T*)a.X + (size_t)(valid ? row : 0) * a.D_in;
+
+    Producer prod;
+    prod.setup(a);
+    if (grp < nj) prod.prefetch(xrow, valid, kb0 + grp, a.D_in);
+
+    float mean = 0.f, rstd = 1.f;
+    if (a.input_map == KAN_MAP_LAYERNORM) {
+      float s, ss, pv;
+      ln_partial<MODE>(xrow, valid, a.D_in, grp, s, ss, pv);
+      s_stats[grp * BM + r] = s;
+      s_stats[(2 + grp) * BM + r] = ss;
+      named_bar(1, PRODUCER_THREADS);
+      const float st = s_stats[r] + s_stats[BM + r];
+      const float sst = s_stats[2 * BM + r] + s_stats[3 * BM + r];
+      const float md = st / (float)a.D_in;
+      mean = pv + md;
+      rstd = rsqrtf(fmaxf(sst / (float)a.D_in - md * md, 0.f) + a.ln_eps);
+    }
+
+    for (int j = grp; j < nj; j += 2) {
+      const int s = j % STAGES;
+      const uint32_t it = (uint32_t)(j / STAGES);
+      float xs[Producer::F];
+#pragma unroll
+      for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
+      if (j + 2 < nj) prod.prefetch(xrow, valid, kb0 + j + 2, a.D_in);
+      if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
+        raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      prod.produce(smem + OFF_A + s * A_STAGE_BYTES, r, xs, kb0 + j, a, mean, rstd);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
+    }
+
+    // ------------------------------------------------------------------ epilogue
+    if (!mbar_wait(bar_accum, 0)) {
+      raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
+      *abort_flag = 1;
+    }
+    tc_fence_after();
+    // all epilogue threads must agree on the abort decision before the barriers below
+    named_bar(3, PRODUCER_THREADS);
+    if (threadIdx.x == 0) *epi_flag = *abort_flag ? 1 : 0;
+    named_bar(3, PRODUCER_THREADS);
+    const bool aborted = (*epi_flag != 0) || nj <= 0;
+
+    const int h = grp;  // column half of the tile
+    const int HALF = BN >> 1;
+    T* Y = (T*)a.Y;
+    const T* bias = (const T*)a.bias;
+    const bool vec_ok = (a.D_out % 8) == 0;
+    auto store_chunk = [&](float (&out)[32], int col0) {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        out[jj] += (a.has_bias && col0 + jj < a.D_out) ? Act<MODE>::to_f(bias[col0 + jj]) : 0.f;
+      T* yrow = Y + (size_t)row * a.D_out;
+      if (vec_ok && col0 + 32 <= a.D_out) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          uint4 pk;
+          pk.x = pack2<MODE>(out[8 * jj + 0], out[8 * jj + 1]);
+          pk.y = pack2<MODE>(out[8 * jj + 2], out[8 * jj + 3]);
+          pk.z = pack2<MODE>(out[8 * jj + 4], out[8 * jj + 5]);
+          pk.w = pack2<MODE>(out[8 * jj + 6], out[8 * jj + 7]);
+          *reinterpret_cast<uint4*>(yrow + col0 + 8 * jj) = pk;
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+          if (col0 + jj < a.D_out) yrow[col0 + jj] = Act<MODE>::from_f(out[jj]);
+      }
+    };
+
+    if (splits == 1) {
+      if (!aborted) {
+#pragma unroll 1
+        for (int cc = 0; cc < HALF; cc += 32) {
+          uint32_t acc[32];
+          const int ct = h * HALF + cc;
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
+          const int col0 = n0 + ct;
+          if (!valid || col0 >= a.D_out) continue;
+          float out[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) out[jj] = __uint_as_float(acc[jj]);
+          store_chunk(out, col0);
+        }
+      }
+    } else {
+      // park this split's partial tile in shared memory (over the finished stage buffers)
+      float* part = reinterpret_cast<float*>(smem);
+      if (!aborted) {
+#pragma unroll 1
+        for (int cc = 0; cc < HALF; cc += 32) {
+          uint32_t acc[32];
+          const int ct = h * HALF + cc;
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
+          float4* dst = reinterpret_cast<float4*>(part + r * PART_STRIDE + ct);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj)
+            dst[jj] = make_float4(__uint_as_float(acc[4 * jj]), __uint_as_float(acc[4 * jj + 1]),
+                                  __uint_as_float(acc[4 * jj + 2]),
+                                  __uint_as_float(acc[4 * jj + 3]));
+        }
+      }
+    }
+  } else if (warp == TMA_WARP) {
+    // ------------------------------------------------------------------ weight TMA
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)BN * BK * 2;
+      int issued = 0;
+      for (int j = 0; j < nj; ++j) {
+        const int s = j % STAGES;
+        const uint32_t it = (uint32_t)(j / STAGES);
+        if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(bar_full_b + 8 * s, bytes);
+        tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES, &tmap_w, bar_full_b + 8 * s,
+                    (kb0 + j) * BK, n0);
+        ++issued;
+      }
+      // drain: wait (bounded) for the copies still landing in shared memory
+      for (int j = issued - 1; j >= 0 && j >= issued - STAGES; --j)
+        (void)mbar_wait(bar_full_b + 8 * (j % STAGES), (uint32_t)(j / STAGES) & 1u);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, BN, BM);
+      for (int j = 0; j < nj; ++j) {
+        const int s = j % STAGES;
+        const uint32_t par = (uint32_t)(j / STAGES) & 1u;
+        bool ok = mbar_wait(bar_full_a + 8 * s, par);
+        if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
+        if (ok && !mbar_wait(bar_full_b + 8 * s, par)) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
+          ok = false;
+        }
+        if (!ok || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = s_base + OFF_A + s * A_STAGE_BYTES;
+        const uint32_t b_addr = s_base + OFF_B + s * B_STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          mma_f16(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
+                  idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(bar_empty + 8 * s);
+      }
+      // signal the epilogue (also on abort, so that it does not wait out its own limit)
+      mma_commit(bar_accum);
+    }
+    __syncwarp();
+  }
+
+  if (splits > 1) {
+    __syncwarp();
+    // every CTA of the cluster has parked its partial tile: reduce column slice z over the
+    // cluster in split order, add the bias, store
+    cluster_sync_all();
+    if (warp < NUM_PRODUCER_WARPS && *epi_flag == 0 && nj > 0) {
+      const int slice = BN / splits;  // host guarantees BN % (32 * splits) == 0
+      const int r = threadIdx.x & (BM - 1);
+      const int row = m0 + r;
+      const int per_thread = slice / 2;  // two threads per row
+      const int c_lo = z * slice + (threadIdx.x >> 7) * per_thread;
+      const uint32_t local = s_base + (uint32_t)((r * PART_STRIDE + c_lo) * 4);
+      if (row < a.B) {
+        T* Y = (T*)a.Y;
+        const T* bias = (const T*)a.bias;
+#pragma unroll 1
+        for (int c = 0; c < per_thread; c += 4) {
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int zz = 0; zz < splits; ++zz) {
+            const float4 p = ld_cluster_f4(map_to_rank(local + c * 4, (uint32_t)zz));
+            sum.x += p.x;
+            sum.y += p.y;
+            sum.z += p.z;
+            sum.w += p.w;
+          }
+          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int col = n0 + c_lo + c + t;
+            if (col < a.D_out) {
+              const float b = a.has_bias ? Act<MODE>::to_f(bias[col]) : 0.f;
+              Y[(size_t)row * a.D_out + col] = Act<MODE>::from_f(vals[t] + b);
+            }
+          }
+        }
+      }
+    }
+    // no CTA may leave while another still reads its shared memory
+    cluster_sync_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem_d, TMEM_COLS);
+  }
+}
+
+template <int BASIS, int MODE, class Producer>
+static cudaError_t launch_kernel(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
+                                 int splits, dim3 grid, cudaStream_t s) {
+  auto kern = kan_tc_kernel<BASIS, MODE, Producer>;
+  static bool configured = false;  // one per template instance
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SMEM_ALLOC);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_ALLOC;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = splits > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, tw, a, BN, nb, splits);
+}
+
+// Compile-time-K producers for the shapes the BASELINE configs and common layers use; any other
+// K runs the runtime-K producer.
+template <int BASIS, int MODE>
+static cudaError_t dispatch_k(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
+                              int splits, dim3 grid, cudaStream_t s) {
+#define KAN_TC_CASE(KK, HBV)                                                                  \
+  if (a.K == KK && (a.has_base != 0) == HBV)                                                  \
+    return launch_kernel<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, a, BN, nb, splits, \
+                                                                         grid, s);
+  if (BASIS == KAN_CHEBY) {
+    KAN_TC_CASE(4, true) KAN_TC_CASE(4, false) KAN_TC_CASE(5, true) KAN_TC_CASE(5, false)
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false) KAN_TC_CASE(9, true) KAN_TC_CASE(9, false)
+  } else if (BASIS == KAN_RBF) {
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
+  } else if (BASIS == KAN_BSPLINE) {
+    KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
+  } else {
+    KAN_TC_CASE(6, true) KAN_TC_CASE(6, false) KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
+  }
+#undef KAN_TC_CASE
+  return launch_kernel<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, a, BN, nb, splits, grid, s);
+}
+
+}  // namespace tc
+}  // namespace kan
