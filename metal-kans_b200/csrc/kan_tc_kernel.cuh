@@ -30,6 +30,7 @@
 // cluster-wide barrier and releases TMEM.
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include "kan_device.cuh"
@@ -55,16 +56,23 @@ constexpr int MAX_SPLITS = 8;                          // portable cluster size
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
 constexpr int OFF_BAR = OFF_B + STAGES * B_STAGE_BYTES;
-constexpr int NUM_BARS = 3 * STAGES + 1;
+constexpr int NUM_BARS = 3 * STAGES + 3;  // full A/B, empty per stage; accum; x tile; reduction
 constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
 constexpr int OFF_FLAG = OFF_TMEM + 4;
 constexpr int OFF_EPI = OFF_FLAG + 4;
 constexpr int OFF_STATS = (OFF_EPI + 4 + 15) / 16 * 16;    // LayerNorm partial sums / stats
 constexpr int SMEM_BYTES = OFF_STATS + 4 * BM * 4;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
-// split-K partial tile [128][BN + 4] fp32, parked over the (finished) pipeline buffers
-constexpr int PART_STRIDE = 256 + 4;
-static_assert(BM * PART_STRIDE * 4 <= OFF_BAR, "partial tile must fit in the stage buffers");
+// Split-K receive buffers, over the (finished) pipeline buffers: one [128][slice + 4] fp32 slot per
+// split (slice = BN / splits columns); the largest case is 8 slots of 32-column slices.
+__host__ __device__ constexpr int recv_bytes(int splits, int slice) {
+  return splits * BM * (slice + 4) * 4;
+}
+static_assert(recv_bytes(4, 64) <= OFF_BAR && recv_bytes(8, 32) <= OFF_BAR &&
+                  recv_bytes(2, 128) <= OFF_BAR,
+              "split-K receive slots must fit in the stage buffers");
+// LayerNorm input tile (rows of <= 256 features) staged over the A stages before the first block
+static_assert(BM * 256 * 2 <= STAGES * A_STAGE_BYTES, "x tile must fit in the A stages");
 
 // ---------------------------------------------------------------------------------------------
 // PTX wrappers
@@ -94,14 +102,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity`; false when the limit expired.
+// Bounded wait for the phase of `parity`; false when the limit expired.  Failed polls back off
+// with a short sleep so that idle waiters do not crowd the shared-memory pipe the producers use.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(64);
     if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
   }
   return true;
+}
+// Warp-wide bounded wait: lane 0 polls, the outcome is broadcast, each lane then takes the
+// completed phase with one (immediately successful) try_wait for its own acquire ordering, and
+// the warp leaves reconverged -- per-lane polling would let the lanes leave the loop at different
+// iterations and run the following code (shuffles, the A-tile producer) diverged.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
+  uint32_t ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1u : 0u;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_try_wait(bar, parity);
+  __syncwarp();
+  return ok != 0;
 }
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -118,13 +140,39 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
   return r;
 }
+// Loads issued as volatile asm in program order: a block of them leaves the SM before any of
+// their results is consumed (memory-level parallelism the compiler would not otherwise keep).
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+               : "r"(addr));
   return v;
+}
+__device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// 16-byte store into another CTA's shared memory; completes `bytes` on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a0, float a1, float a2,
+                                            float a3, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, "
+      "[%5];" ::"r"(remote_addr),
+      "f"(a0), "f"(a1), "f"(a2), "f"(a3), "r"(remote_bar)
+      : "memory");
+}
+// Contiguous global -> shared copy by the bulk-copy engine, completing on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
@@ -177,6 +225,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&f)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
+}
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row core groups 1024 B
 // apart (SBO), LBO unused for swizzled K-major (encoded 1), descriptor version 1 (sm_100).
@@ -224,15 +285,15 @@ __device__ __forceinline__ void ln_partial(const typename Act<MODE>::T* xrow, bo
   const int lo = half ? D_in / 2 : 0, hi = half ? D_in : D_in / 2;
   const bool vec = ((D_in & 15) == 0) && ((((uintptr_t)xrow) & 15) == 0);
   if (vec) {
-    // 16-byte loads, 4 in flight
-    for (int c = lo; c < hi; c += 32) {
-      uint4 raw[4];
+    // 16-byte loads, 8 in flight
+    for (int c = lo; c < hi; c += 64) {
+      uint4 raw[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < 8; ++u)
         raw[u] = (c + 8 * u < hi) ? *reinterpret_cast<const uint4*>(xrow + c + 8 * u)
                                   : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         if (c + 8 * u >= hi) continue;
         const T* e = reinterpret_cast<const T*>(&raw[u]);
 #pragma unroll
@@ -250,6 +311,59 @@ __device__ __forceinline__ void ln_partial(const typename Act<MODE>::T* xrow, bo
       ss = fmaf(d, d, ss);
     }
   }
+}
+
+// Rows of at most 256 features (D_in % 8 == 0, 16-byte aligned) are staged into shared memory by
+// one bulk copy (the CTA's rows are contiguous in X).  The two owner threads of a row (one per
+// producer group) then each sum one half of it -- 16-byte chunks visited in a per-row rotated
+// order so that the 32 rows of a warp spread over the banks -- and combine through shared memory;
+// mean and variance are two exact passes (no shuffles).
+__device__ __forceinline__ bool ln_smem_ok(const LayerArgs& a) {
+  return a.D_in <= 256 && (a.D_in % 16) == 0 && ((((uintptr_t)a.X) & 15) == 0);
+}
+
+template <int MODE>
+__device__ __forceinline__ float ln_half_pass(const uint8_t* xrow_s, int nchunk, int c0, int r,
+                                              float mean, bool second) {
+  using T = typename Act<MODE>::T;
+  float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < nchunk; ++i) {
+    const int c = c0 + (i + r) % nchunk;
+    const uint4 raw = *reinterpret_cast<const uint4*>(xrow_s + c * 16);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int t = 0; t < 8; t += 2) {
+      const float x0 = Act<MODE>::to_f(e[t]), x1 = Act<MODE>::to_f(e[t + 1]);
+      if (second) {
+        acc0 = fmaf(x0 - mean, x0 - mean, acc0);
+        acc1 = fmaf(x1 - mean, x1 - mean, acc1);
+      } else {
+        acc0 += x0;
+        acc1 += x1;
+      }
+    }
+  }
+  return acc0 + acc1;
+}
+
+// Statistics of row r (its two owner threads call this; `part` is [2][BM] floats of scratch).
+template <int MODE>
+__device__ __forceinline__ void ln_row_stats(const LayerArgs& a, const uint8_t* xtile, int r,
+                                             int grp, bool valid, float* part, float& mean,
+                                             float& rstd) {
+  const int nchunk = a.D_in / 16;  // 16-byte chunks per half row
+  const uint8_t* xrow_s = xtile + (size_t)r * a.D_in * 2;
+  const float inv_n = 1.0f / (float)a.D_in;
+  float s = valid ? ln_half_pass<MODE>(xrow_s, nchunk, grp * nchunk, r, 0.f, false) : 0.f;
+  part[grp * BM + r] = s;
+  named_bar(1, PRODUCER_THREADS);
+  mean = (part[r] + part[BM + r]) * inv_n;
+  named_bar(1, PRODUCER_THREADS);
+  float ss = valid ? ln_half_pass<MODE>(xrow_s, nchunk, grp * nchunk, r, mean, true) : 0.f;
+  part[grp * BM + r] = ss;
+  named_bar(1, PRODUCER_THREADS);
+  rstd = rsqrtf((part[r] + part[BM + r]) * inv_n + a.ln_eps);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -430,6 +544,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t bar_full_b = bar_full_a + STAGES * 8;
   const uint32_t bar_empty = bar_full_b + STAGES * 8;
   const uint32_t bar_accum = bar_empty + STAGES * 8;
+  const uint32_t bar_x = bar_accum + 8;     // LayerNorm x tile landed
+  const uint32_t bar_red = bar_x + 8;       // split-K slices from the other CTAs landed
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_FLAG);
   volatile int* epi_flag = reinterpret_cast<volatile int*>(smem + OFF_EPI);
@@ -442,6 +558,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int kb0 = (int)((long long)nb_total * z / splits);
   const int kb1 = (int)((long long)nb_total * (z + 1) / splits);
   const int nj = kb1 - kb0;
+  const bool ln_staged = a.input_map == KAN_MAP_LAYERNORM && ln_smem_ok(a);
+  const int rows_valid = min(BM, a.B - m0);
+  const int slice = BN / splits;  // split-K: columns of the tile this CTA finishes
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -450,15 +569,27 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_accum, 1);
+    mbar_init(bar_x, 1);
+    mbar_init(bar_red, 1);
     *abort_flag = 0;
     *epi_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (ln_staged) {
+      // the CTA's input rows are one contiguous block of X
+      const uint32_t bytes = (uint32_t)(rows_valid * a.D_in * 2);
+      mbar_arrive_expect_tx(bar_x, bytes);
+      bulk_g2s(s_base + OFF_A, (const T*)a.X + (size_t)m0 * a.D_in, bytes, bar_x);
+    }
+    // the other splits' slices arrive after the first cluster barrier, i.e. after this point
+    if (splits > 1)
+      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * BM * slice * 4));
   }
   if (warp == MMA_WARP) tmem_alloc(s_base + OFF_TMEM, TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
+  bool producer_aborted = true;  // set by the epilogue threads (the producer warps)
 
   if (warp < NUM_PRODUCER_WARPS) {
     // ------------------------------------------------------------------ basis producers
@@ -473,7 +604,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (grp < nj) prod.prefetch(xrow, valid, kb0 + grp, a.D_in);
 
     float mean = 0.f, rstd = 1.f;
-    if (a.input_map == KAN_MAP_LAYERNORM) {
+    if (ln_staged) {
+      if (!mbar_wait_warp(bar_x, 0)) {
+        raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
+        *abort_flag = 1;
+      }
+      ln_row_stats<MODE>(a, smem + OFF_A, r, grp, valid, s_stats, mean, rstd);
+      // every thread is done with the x tile before the A stages are overwritten
+      named_bar(1, PRODUCER_THREADS);
+    } else if (a.input_map == KAN_MAP_LAYERNORM) {
       float s, ss, pv;
       ln_partial<MODE>(xrow, valid, a.D_in, grp, s, ss, pv);
       s_stats[grp * BM + r] = s;
@@ -493,7 +632,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
       for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
       if (j + 2 < nj) prod.prefetch(xrow, valid, kb0 + j + 2, a.D_in);
-      if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
+      if (!mbar_wait_warp(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
         *abort_flag = 1;
         break;
@@ -506,7 +645,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 
     // ------------------------------------------------------------------ epilogue
-    if (!mbar_wait(bar_accum, 0)) {
+    if (!mbar_wait_warp(bar_accum, 0)) {
       raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
       *abort_flag = 1;
     }
@@ -559,24 +698,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           store_chunk(out, col0);
         }
       }
-    } else {
-      // park this split's partial tile in shared memory (over the finished stage buffers)
-      float* part = reinterpret_cast<float*>(smem);
-      if (!aborted) {
-#pragma unroll 1
-        for (int cc = 0; cc < HALF; cc += 32) {
-          uint32_t acc[32];
-          const int ct = h * HALF + cc;
-          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)ct, acc);
-          float4* dst = reinterpret_cast<float4*>(part + r * PART_STRIDE + ct);
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj)
-            dst[jj] = make_float4(__uint_as_float(acc[4 * jj]), __uint_as_float(acc[4 * jj + 1]),
-                                  __uint_as_float(acc[4 * jj + 2]),
-                                  __uint_as_float(acc[4 * jj + 3]));
-        }
-      }
     }
+    producer_aborted = aborted;
   } else if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ weight TMA
     if (lane == 0) {
@@ -635,43 +758,112 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (splits > 1) {
     __syncwarp();
-    // every CTA of the cluster has parked its partial tile: reduce column slice z over the
-    // cluster in split order, add the bias, store
+    // every CTA of the cluster has finished its main loop: stage buffers may now receive slices
     cluster_sync_all();
-    if (warp < NUM_PRODUCER_WARPS && *epi_flag == 0 && nj > 0) {
-      const int slice = BN / splits;  // host guarantees BN % (32 * splits) == 0
-      const int r = threadIdx.x & (BM - 1);
+    if (warp < NUM_PRODUCER_WARPS) {
+      const int q = warp & 3, h = warp >> 2;
+      const int r = q * 32 + lane;
       const int row = m0 + r;
-      const int per_thread = slice / 2;  // two threads per row
-      const int c_lo = z * slice + (threadIdx.x >> 7) * per_thread;
-      const uint32_t local = s_base + (uint32_t)((r * PART_STRIDE + c_lo) * 4);
-      if (row < a.B) {
+      const int half = slice >> 1;  // slice columns per warp (host: slice % 32 == 0)
+      const int pitch = slice + 4;  // receive-slot row pitch in floats
+      const uint32_t taddr0 = tmem_d + ((uint32_t)(q * 32) << 16);
+      bool ok = !producer_aborted && nj > 0;
+      // 1. push slice zz of this CTA's accumulator into slot z of CTA zz (remote async stores
+      //    completing on CTA zz's reduction barrier)
+      if (ok) {
+        for (int zz = 0; zz < splits; ++zz) {
+          if (zz == z) continue;
+          const uint32_t rdst = map_to_rank(s_base + OFF_A, (uint32_t)zz) +
+                                (uint32_t)((z * BM + r) * pitch * 4);
+          const uint32_t rbar = map_to_rank(bar_red, (uint32_t)zz);
+#pragma unroll 1
+          for (int cc = 0; cc < half; cc += 16) {
+            const int cs = h * half + cc;  // column within the slice
+            float v[16];
+            tmem_ld16(taddr0 + (uint32_t)(zz * slice + cs), v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              st_async_v4(rdst + (uint32_t)((cs + 4 * u) * 4), v[4 * u], v[4 * u + 1],
+                          v[4 * u + 2], v[4 * u + 3], rbar);
+          }
+        }
+      }
+      // 2. the other splits' slices of this CTA's own columns have landed (always waited for:
+      //    no remote store may still target this CTA's shared memory when it exits)
+      if (!mbar_wait_warp(bar_red, 0)) {
+        raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
+        ok = false;
+      }
+      // 3. sum in split order (deterministic), bias, store 16 outputs at a time
+      if (ok) {
         T* Y = (T*)a.Y;
         const T* bias = (const T*)a.bias;
+        const bool vec = (a.D_out % 8) == 0;
+        const float* recv = reinterpret_cast<const float*>(smem + OFF_A);
 #pragma unroll 1
-        for (int c = 0; c < per_thread; c += 4) {
-          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int zz = 0; zz < splits; ++zz) {
-            const float4 p = ld_cluster_f4(map_to_rank(local + c * 4, (uint32_t)zz));
-            sum.x += p.x;
-            sum.y += p.y;
-            sum.z += p.z;
-            sum.w += p.w;
-          }
-          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+        for (int cc = 0; cc < half; cc += 16) {
+          const int cs = h * half + cc;
+          float own[16];
+          tmem_ld16(taddr0 + (uint32_t)(z * slice + cs), own);  // warp-collective
+          float sum[16];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int col = n0 + c_lo + c + t;
-            if (col < a.D_out) {
-              const float b = a.has_bias ? Act<MODE>::to_f(bias[col]) : 0.f;
-              Y[(size_t)row * a.D_out + col] = Act<MODE>::from_f(vals[t] + b);
+          for (int t = 0; t < 16; ++t) sum[t] = 0.f;
+          for (int zz = 0; zz < splits; ++zz) {
+            if (zz == z) {
+#pragma unroll
+              for (int t = 0; t < 16; ++t) sum[t] += own[t];
+            } else {
+              const float4* src =
+                  reinterpret_cast<const float4*>(recv + (zz * BM + r) * pitch + cs);
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const float4 p = src[u];
+                sum[4 * u] += p.x;
+                sum[4 * u + 1] += p.y;
+                sum[4 * u + 2] += p.z;
+                sum[4 * u + 3] += p.w;
+              }
+            }
+          }
+          const int col0 = n0 + z * slice + cs;
+          if (row >= a.B || col0 >= a.D_out) continue;
+          if (vec && col0 + 16 <= a.D_out) {
+            if (a.has_bias) {
+              const uint4 b0 = *reinterpret_cast<const uint4*>(bias + col0);
+              const uint4 b1 = *reinterpret_cast<const uint4*>(bias + col0 + 8);
+              const T* bb0 = reinterpret_cast<const T*>(&b0);
+              const T* bb1 = reinterpret_cast<const T*>(&b1);
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                sum[t] += Act<MODE>::to_f(bb0[t]);
+                sum[8 + t] += Act<MODE>::to_f(bb1[t]);
+              }
+            }
+            uint4 o0, o1;
+            o0.x = pack2<MODE>(sum[0], sum[1]);
+            o0.y = pack2<MODE>(sum[2], sum[3]);
+            o0.z = pack2<MODE>(sum[4], sum[5]);
+            o0.w = pack2<MODE>(sum[6], sum[7]);
+            o1.x = pack2<MODE>(sum[8], sum[9]);
+            o1.y = pack2<MODE>(sum[10], sum[11]);
+            o1.z = pack2<MODE>(sum[12], sum[13]);
+            o1.w = pack2<MODE>(sum[14], sum[15]);
+            uint4* dst = reinterpret_cast<uint4*>(Y + (size_t)row * a.D_out + col0);
+            dst[0] = o0;
+            dst[1] = o1;
+          } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const int col = col0 + t;
+              if (col < a.D_out) {
+                const float b = a.has_bias ? Act<MODE>::to_f(bias[col]) : 0.f;
+                Y[(size_t)row * a.D_out + col] = Act<MODE>::from_f(sum[t] + b);
+              }
             }
           }
         }
       }
     }
-    // no CTA may leave while another still reads its shared memory
-    cluster_sync_all();
   }
 
   tc_fence_before();
