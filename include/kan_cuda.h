@@ -231,6 +231,20 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
 int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
                       const void* X, void* H, void* Y, int B, void* stream);
 
+/* No counterpart in the reference.  kan_gated_forward() for callers that cannot allocate device
+ * memory (allocation forbidden after start-up by a memory arena or a serving runtime, or a
+ * cudaMalloc that would synchronise or fail at that point): the gate and up activations live in
+ * a fixed 32 MiB device array that every GPU loading the library holds until exit, so
+ * 2 * B * gate->D_out * sizeof(act dtype) must be <= 32 MiB (else KAN_ERR_UNSUPPORTED).  H and
+ * Y are the caller's, as in kan_gated_forward().  The first call on a device looks up the array's
+ * device address (and sets up the library's per-device state); make it before any stream
+ * capture.  All calls on a device share the array and keep the previous call's contents (nothing
+ * in it needs zeroing), so calls that overlap on the GPU race.  f16/bf16 layers use the tensor
+ * cores only if their tc_weights are packed in advance; without them they run on the CUDA-core
+ * path, which needs no scratch. */
+int kan_gated_forward_noalloc(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
+                              const void* X, void* H, void* Y, int B, void* stream);
+
 /* Dequantise any weight format to a dense matrix of `out_dtype` ([rows][cols]); the fp32 value
  * is bit-identical to the reference dequantiser, then rounded (RNE) for f16/bf16 outputs. */
 int kan_dequantize(const kan_weight* w, int rows, int cols, void* out, int out_dtype,

@@ -46,6 +46,8 @@ static int fail(int code, const char* fmt, ...) {
                   __FILE__, __LINE__);                                                     \
   } while (0)
 
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 static std::atomic<long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(); }

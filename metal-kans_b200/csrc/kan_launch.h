@@ -12,6 +12,8 @@ inline int BasisOf(const LayerArgs& a) { return a.basis; }
 
 void note_launch();
 long long launch_count();
+// Record `msg` as this thread's kan_last_error() and return `code` (kan_abi.cpp).
+int set_error(int code, const char* msg);
 // Address of the device error word on the current device (kan_misc.cu).
 int* device_error_ptr();
 

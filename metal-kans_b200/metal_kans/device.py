@@ -98,6 +98,7 @@ SIGNATURES = [
     ("kan_forward", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, vp]),
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
+    ("kan_gated_forward_noalloc", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
     ("kan_tc_packed_bytes", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(sz)]),
     ("kan_tc_pack", i32, [ctypes.POINTER(KanLayer), vp, vp]),
     ("kan_dequantize", i32, [ctypes.POINTER(KanWeight), i32, i32, vp, i32, vp]),
