@@ -35,9 +35,17 @@ class KANLayerBase(E.DeviceLayerMixin):
         return getattr(self, self.MAIN).dtype
 
     def _cast(self, dt, extra=()):
-        setattr(self, self.MAIN, getattr(self, self.MAIN).astype(dt))
+        def cast_weight(name):
+            # a packed weight stays authoritative through a dtype cast: the cast array is its
+            # dequantised values rounded to `dt`, exactly what the kernels decode and round to
+            q = self._packed(name)
+            setattr(self, name, getattr(self, name).astype(dt))
+            if q is not None:
+                q._source_version = self._version(name)
+
+        cast_weight(self.MAIN)
         if self.has_base:
-            self.w_base = self.w_base.astype(dt)
+            cast_weight("w_base")
         if self.has_bias:
             self.bias = self.bias.astype(dt)
         for name in extra:

@@ -154,6 +154,33 @@ class Int2QuantizedWeight(_PackedMixin):
         w.data, w.scales, w.codebook = p.ptr, s.ptr, c.ptr
 
 
+def packed_from_codes(kind: str, w_packed: np.ndarray, scales: np.ndarray, shape,
+                      group_size: int, codebook=None):
+    """Build a Ternary/Int2QuantizedWeight straight from its packed codes and scales (same
+    layout as the quantisers produce), e.g. for synthetic or externally quantised weights."""
+    cls = TernaryQuantizedWeight if kind == "ternary" else Int2QuantizedWeight
+    q = cls.__new__(cls)
+    q.group_size = int(group_size)
+    q.shape = tuple(shape)
+    q.w_packed = np.ascontiguousarray(w_packed, np.uint32)
+    q.scales = np.ascontiguousarray(scales, np.float32)
+    if kind != "ternary":
+        q.codebook = np.ascontiguousarray(
+            codebook if codebook is not None else [-1.0, -0.33333, 0.33333, 1.0], np.float32)
+    return q
+
+
+def attach_packed(layer: Any, attr: str, q) -> Any:
+    """Install packed weight `q` on `layer.attr` the way to_int*/to_ternary do: the attribute
+    becomes the dequantised fp32 array and `q` stays authoritative for the kernels."""
+    suffix = {QuantizedWeight: "_quantized", TernaryQuantizedWeight: "_ternary",
+              Int2QuantizedWeight: "_int2"}[type(q)]
+    setattr(layer, f"_{attr}{suffix}", q)
+    setattr(layer, attr, q.dequantize())
+    q._source_version = getattr(layer, "_versions", {}).get(attr, 0)
+    return layer
+
+
 WEIGHT_ATTRS = ["w_cheby", "w_rbf", "w_relu", "w_wav", "w_fourier", "w_jacobi", "w_p", "w_q",
                 "w_spline", "w_up", "w_base"]
 
