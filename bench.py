@@ -149,7 +149,8 @@ def spec_c3(rank=0):
 
 
 def engine_c3(mk, w):
-    net = mk.MetalKAN(C3_DIMS, basis_type="bspline", bias=True, use_base=True)
+    # MetalKAN passes `degree` as the B-spline grid size (metal_kan.py:76-77): 5 -> 8 bases
+    net = mk.MetalKAN(C3_DIMS, basis_type="bspline", degree=5, bias=True, use_base=True)
     for l, p in zip(net.layers, w.W):
         l.w_spline, l.w_base, l.bias = p["w_spline"], p["w_base"], p["bias"]
     net.half()
@@ -258,15 +259,26 @@ def engine_c5(mk, w):
     return l, [l]
 
 
-def get_spec(config, rank=0):
+def get_spec(config, rank=0, rows=0):
+    """(Workload, engine builder) for "c1".."c4" or "c5:<ternary|int2>:<B>"; rows > 0 keeps the
+    config's weights and takes the first `rows` input rows (a smaller case of the same layer)."""
     parts = config.split(":")
     if parts[0] == "c5":
         kind = parts[1] if len(parts) > 1 else "ternary"
         B = int(parts[2]) if len(parts) > 2 else 4096
-        return spec_c5(rank, B=B, kind=kind), engine_c5
-    return {"c1": (spec_c1, engine_c1), "c2": (spec_c2, engine_c2), "c3": (spec_c3, engine_c3),
-            "c4": (spec_c4, engine_c4)}[parts[0]][0](rank), \
-        {"c1": engine_c1, "c2": engine_c2, "c3": engine_c3, "c4": engine_c4}[parts[0]]
+        w, eng = spec_c5(rank, B=rows or B, kind=kind), engine_c5
+    else:
+        spec, eng = {"c1": (spec_c1, engine_c1), "c2": (spec_c2, engine_c2),
+                     "c3": (spec_c3, engine_c3), "c4": (spec_c4, engine_c4)}[parts[0]]
+        w = spec(rank)
+        if rows:
+            scale = rows / w.B
+            w.x = np.ascontiguousarray(w.x[:rows]) if rows <= w.B else \
+                np.ascontiguousarray(np.resize(w.x, (rows, w.x.shape[1])))
+            w.flops *= scale
+            w.B = rows
+            w.cfg = {**w.cfg, "rows_override": rows}
+    return w, eng
 
 
 # --------------------------------------------------------------------------------------------
@@ -381,6 +393,8 @@ def main():
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the per-GPU batch (smaller cases of a config for profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -407,7 +421,7 @@ def main():
 
     lib = mk.get_metal_bridge()
     lib.kan_set_device(local)
-    w, engine = get_spec(args.config, rank)
+    w, engine = get_spec(args.config, rank, args.rows)
     obj, layers = engine(mk, w)
     oshard = world > 1 and args.config.startswith("c5") and w.B <= 16
     stream = torch.cuda.ExternalStream(lib.kan_default_stream())
@@ -485,8 +499,10 @@ def main():
                 "frac": achieved / pk["hbm"], "peak_src": pk["src"] + " copy",
                 "traffic": TRAFFIC.get(args.config), "algorithmic_bytes_per_step": per_rank_bytes}
 
-    e2e = e2e_measure(sharded if oshard else obj, w, args, barrier, dist, rows_per_step)
-    cpu = cpu_baseline(w, args.cpu_seconds) if (rank == 0 and world == 1) else None
+    e2e = (e2e_measure(sharded if oshard else obj, w, args, barrier, dist, rows_per_step)
+           if args.e2e_steps > 0 else None)
+    cpu = (cpu_baseline(w, args.cpu_seconds)
+           if (rank == 0 and world == 1 and args.cpu_seconds > 0) else None)
     if dist is not None:
         dist.barrier()
     if rank == 0:
@@ -543,7 +559,7 @@ def reference_arm(args, rank, world):
     if rank != 0:
         return
     cores = len(os.sched_getaffinity(0))
-    w, _ = get_spec(args.config, 0)
+    w, _ = get_spec(args.config, 0, args.rows)
     sample = min(w.B, 512)
     xs = np.ascontiguousarray(w.x[:sample])
     for _ in range(min(args.warmup, 3)):

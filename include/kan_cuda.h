@@ -169,7 +169,10 @@ enum kan_wformat {
   KAN_W_TERNARY = 3, /* u32 [rows][ceil(cols/16)], fp32 scales [rows][ceil(cols/gs)]           */
   KAN_W_INT2 = 4     /* as ternary + fp32 codebook[4]                                          */
 };
-/* Kernel selection for kan_forward (KAN_PATH_AUTO picks by shape and batch). */
+/* Kernel selection for kan_forward_path.  KAN_PATH_AUTO: the small-batch kernel (GEMV) when it
+   applies (f16/bf16 Chebyshev layer, ternary/INT2 weights, B <= 64, D_in >= 512, D_out >= 256),
+   else the tensor-core kernel (TC) for f16/bf16, else the CUDA-core kernel (SIMT).  An explicit
+   path a layer does not fit returns KAN_ERR_UNSUPPORTED. */
 enum kan_path { KAN_PATH_AUTO = 0, KAN_PATH_SIMT = 1, KAN_PATH_TC = 2, KAN_PATH_GEMV = 3 };
 
 /* One weight matrix with `rows` = D_out and `cols` = D_in*K (basis) or D_in (base branch). */

@@ -68,7 +68,7 @@ struct PendingCopy {
 // Engine scratch of one stream: packed tensor-core weights (when the caller passes none) and the
 // GatedKAN gate/up activations.  Kept per stream so that work queued on different streams never
 // shares a buffer.
-enum ScratchId { SC_TCW, SC_GATE, SC_UP, NUM_SCRATCH };
+enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, NUM_SCRATCH };
 struct Scratch {
   cudaStream_t stream = nullptr;
   void* ptr[NUM_SCRATCH] = {};
@@ -316,16 +316,26 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
   if (rc) return rc;
   if (B == 0) return KAN_OK;
   cudaError_t e;
+  const bool gemv_ok = gemv_supported(a, L->act_dtype);
   if (path == KAN_PATH_AUTO) {
-    path = (L->act_dtype != KAN_F32 && tc_supported(a, L->act_dtype)) ? KAN_PATH_TC
-                                                                        : KAN_PATH_SIMT;
+    path = gemv_ok ? KAN_PATH_GEMV
+                   : (L->act_dtype != KAN_F32 && tc_supported(a, L->act_dtype)) ? KAN_PATH_TC
+                                                                                 : KAN_PATH_SIMT;
   }
   if (path == KAN_PATH_TC) {
     if (!tc_supported(a, L->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED,
                   "tensor-core path needs an f16/bf16 layer with K + has_base <= 64");
     return run_tc(a, L->act_dtype, s, d);
-  } else if (path == KAN_PATH_SIMT || path == KAN_PATH_GEMV) {
+  } else if (path == KAN_PATH_GEMV) {
+    if (!gemv_ok)
+      return fail(KAN_ERR_UNSUPPORTED,
+                  "small-batch path needs an f16/bf16 Chebyshev layer with ternary/INT2 weights "
+                  "(group 32/64/128), B <= 64, D_in >= 512, D_out >= 256");
+    void* phi;
+    if ((rc = scratch_buf(d, s, SC_PHI, gemv_phi_bytes(a), false, &phi))) return rc;
+    e = launch_gemv(a, L->act_dtype, phi, s);
+  } else if (path == KAN_PATH_SIMT) {
     e = launch_simt(a, L->act_dtype, s);
   } else {
     return fail(KAN_ERR_ARG, "unknown path %d", path);

@@ -29,6 +29,12 @@ bool tc_supported(const LayerArgs& a, int act_dtype);
 TcPlan tc_plan(const LayerArgs& a);
 cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& plan, cudaStream_t s);
 cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s);
+// kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
+// from the packed codes into TMEM; no dense copy)
+// launch_gemv also runs the basis pre-pass into `phi` (gemv_phi_bytes() of device scratch).
+bool gemv_supported(const LayerArgs& a, int act_dtype);
+size_t gemv_phi_bytes(const LayerArgs& a);
+cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream_t s);
 // kan_misc.cu
 cudaError_t launch_dequantize(const kan_weight& w, int rows, int cols, void* out, int out_dtype,
                               cudaStream_t s);
