@@ -3,6 +3,12 @@
 
 #include "../../include/kan_cuda.h"
 
+#ifdef __CUDACC__
+#define KAN_HD __host__ __device__
+#else
+#define KAN_HD
+#endif
+
 namespace kan {
 
 // Everything a kernel needs about one layer call (a flattened kan_layer + the call operands).
@@ -26,7 +32,7 @@ struct LayerArgs {
 struct TcBlocking {
   int KT, F, NB;
 };
-inline TcBlocking tc_blocking(int D_in, int K, int has_base) {
+KAN_HD inline TcBlocking tc_blocking(int D_in, int K, int has_base) {
   TcBlocking b;
   b.KT = K + (has_base ? 1 : 0);
   b.F = b.KT > 0 ? 64 / b.KT : 0;

@@ -77,6 +77,23 @@ static bool make_tmap(CUtensorMap* m, const void* base, int rows, long long cols
   return r == CUDA_SUCCESS;
 }
 
+// 2-D tensor map over the input X[B][D_in] (16-bit), box = 64 features x 128 rows, 128-byte
+// swizzle; zero fill beyond B rows and D_in features.  Needs 16-byte aligned rows.
+static bool make_tmap_x(CUtensorMap* m, const void* base, int B, int D_in, int mode) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc || ((uintptr_t)base & 15) || (D_in % 8) != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)D_in, (cuuint64_t)B};
+  cuuint64_t strides[1] = {(cuuint64_t)D_in * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)BM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, mode == MODE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static const DispatchFn kDispatch[3][4] = {
     {nullptr, nullptr, nullptr, nullptr},
     {dispatch_1_0, dispatch_1_1, dispatch_1_2, dispatch_1_3},
@@ -120,9 +137,12 @@ cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& p, cudaSt
   CUtensorMap tw;
   if (!tc::make_tmap(&tw, a.tc_weights, a.D_out, (long long)p.nb * tc::BK, p.BN, mode))
     return cudaErrorInvalidValue;
+  // the input in 64-feature x 128-row tiles for the producers (rows of 16-byte multiples only)
+  CUtensorMap tx = tw;
+  const int x_tma = tc::make_tmap_x(&tx, a.X, a.B, a.D_in, mode) ? 1 : 0;
   note_launch();
   dim3 grid(p.ntiles, p.mtiles, p.splits);
-  return tc::kDispatch[mode][a.basis](tw, a, p.BN, p.nb, p.splits, grid, s);
+  return tc::kDispatch[mode][a.basis](tw, tx, x_tma, a, p.BN, p.nb, p.splits, grid, s);
 }
 
 cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s) {

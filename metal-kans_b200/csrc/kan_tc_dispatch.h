@@ -10,12 +10,15 @@
 namespace kan {
 namespace tc {
 
-using DispatchFn = cudaError_t (*)(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
-                                   int splits, dim3 grid, cudaStream_t s);
+// tw: the packed weights; tx: the input [B][D_in] in 64-feature x 128-row tiles, used when x_tma
+using DispatchFn = cudaError_t (*)(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
+                                   const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
+                                   cudaStream_t s);
 
-#define KAN_TC_DECL(MODE, BASIS)                                                        \
-  cudaError_t dispatch_##MODE##_##BASIS(const CUtensorMap& tw, const LayerArgs& a, int BN, \
-                                        int nb, int splits, dim3 grid, cudaStream_t s);
+#define KAN_TC_DECL(MODE, BASIS)                                                              \
+  cudaError_t dispatch_##MODE##_##BASIS(const CUtensorMap& tw, const CUtensorMap& tx,          \
+                                        int x_tma, const LayerArgs& a, int BN, int nb,         \
+                                        int splits, dim3 grid, cudaStream_t s);
 KAN_TC_DECL(1, 0) KAN_TC_DECL(1, 1) KAN_TC_DECL(1, 2) KAN_TC_DECL(1, 3)
 KAN_TC_DECL(2, 0) KAN_TC_DECL(2, 1) KAN_TC_DECL(2, 2) KAN_TC_DECL(2, 3)
 #undef KAN_TC_DECL

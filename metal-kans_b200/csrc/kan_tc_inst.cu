@@ -14,9 +14,10 @@ namespace kan {
 namespace tc {
 
 cudaError_t KAN_CAT(dispatch_, KAN_TC_MODE, KAN_TC_BASIS)(const CUtensorMap& tw,
+                                                          const CUtensorMap& tx, int x_tma,
                                                           const LayerArgs& a, int BN, int nb,
                                                           int splits, dim3 grid, cudaStream_t s) {
-  return dispatch_k<KAN_TC_BASIS, KAN_TC_MODE>(tw, a, BN, nb, splits, grid, s);
+  return dispatch_k<KAN_TC_BASIS, KAN_TC_MODE>(tw, tx, x_tma, a, BN, nb, splits, grid, s);
 }
 
 }  // namespace tc

@@ -41,22 +41,28 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;                 // 64 16-bit elements = one 128-byte swizzle row
-constexpr int STAGES = 4;              // even: producer group g owns stages g, g+2
+constexpr int STAGES = 4;              // basis (A) tiles
+constexpr int BSTAGES = 3;             // weight (B) tiles
+constexpr int XSTAGES = 3;             // input tiles: 64 features x 128 rows, TMA-loaded
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int B_STAGE_BYTES = 256 * BK * 2;  // sized for the widest tile (BN = 256)
+constexpr int X_STAGE_BYTES = BM * 64 * 2;
 constexpr int NUM_PRODUCER_WARPS = 8;
 constexpr int PRODUCER_THREADS = NUM_PRODUCER_WARPS * 32;
 constexpr int TMA_WARP = 8;
 constexpr int MMA_WARP = 9;
-constexpr int THREADS = 320;
+constexpr int XTMA_WARP = 10;
+constexpr int THREADS = 352;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;  // ~1 s at the B200 boost clock
 constexpr int MAX_SPLITS = 8;                          // portable cluster size
 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
-constexpr int OFF_BAR = OFF_B + STAGES * B_STAGE_BYTES;
-constexpr int NUM_BARS = 3 * STAGES + 3;  // full A/B, empty per stage; accum; x tile; reduction
+constexpr int OFF_X = OFF_B + BSTAGES * B_STAGE_BYTES;
+constexpr int OFF_BAR = OFF_X + XSTAGES * X_STAGE_BYTES;
+// full/empty per A stage, per B stage and per x stage; accum; LayerNorm x tile; reduction
+constexpr int NUM_BARS = 2 * STAGES + 2 * BSTAGES + 2 * XSTAGES + 3;
 constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
 constexpr int OFF_FLAG = OFF_TMEM + 4;
 constexpr int OFF_EPI = OFF_FLAG + 4;
@@ -374,6 +380,7 @@ __device__ __forceinline__ void ln_row_stats(const LayerArgs& a, const uint8_t* 
 // block is evaluated; all 64 values live in registers and are rounded once, when packed.
 template <int BASIS, int MODE, int K, bool HB>
 struct RowProducer {
+  static constexpr bool kXFromTiles = true;  // reads its inputs from the TMA input tiles
   static constexpr int KT = K + (HB ? 1 : 0);
   static constexpr int F = 64 / KT;
   using T = typename Act<MODE>::T;
@@ -495,6 +502,7 @@ struct RowProducer {
 // Runtime K (any K + has_base <= 64): zero the row, then 2-byte stores of the computed terms.
 template <int BASIS, int MODE>
 struct RowProducerAnyK {
+  static constexpr bool kXFromTiles = false;  // loads its inputs from global memory itself
   static constexpr int F = 1;
   using T = typename Act<MODE>::T;
   float xn[1];  // unused: this producer loads its inputs itself
@@ -534,16 +542,20 @@ struct RowProducerAnyK {
 // ---------------------------------------------------------------------------------------------
 template <int BASIS, int MODE, class Producer>
 __global__ void __launch_bounds__(THREADS, 1)
-    kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, LayerArgs a, int BN, int nb_total,
-                  int splits) {
+    kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                  const __grid_constant__ CUtensorMap tmap_x, LayerArgs a, int BN, int nb_total,
+                  int splits, int x_tma) {
   using T = typename Act<MODE>::T;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_full_a = s_base + OFF_BAR;
-  const uint32_t bar_full_b = bar_full_a + STAGES * 8;
-  const uint32_t bar_empty = bar_full_b + STAGES * 8;
-  const uint32_t bar_accum = bar_empty + STAGES * 8;
+  const uint32_t bar_empty = bar_full_a + STAGES * 8;     // A stage consumed by the MMA
+  const uint32_t bar_full_b = bar_empty + STAGES * 8;
+  const uint32_t bar_empty_b = bar_full_b + BSTAGES * 8;  // B stage consumed by the MMA
+  const uint32_t bar_full_x = bar_empty_b + BSTAGES * 8;
+  const uint32_t bar_empty_x = bar_full_x + XSTAGES * 8;  // x stage released by every producer
+  const uint32_t bar_accum = bar_empty_x + XSTAGES * 8;
   const uint32_t bar_x = bar_accum + 8;     // LayerNorm x tile landed
   const uint32_t bar_red = bar_x + 8;       // split-K slices from the other CTAs landed
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
@@ -562,11 +574,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int rows_valid = min(BM, a.B - m0);
   const int slice = BN / splits;  // split-K: columns of the tile this CTA finishes
 
+  // input stages of this split: 64-feature tiles covering features [F*kb0, F*kb1)
+  const TcBlocking blocking = tc_blocking(a.D_in, a.K, a.has_base);
+  const int xs_first = (blocking.F * kb0) / 64;
+  const int xs_last = nj > 0 ? (blocking.F * kb1 - 1) / 64 : xs_first - 1;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full_a + 8 * s, NUM_PRODUCER_WARPS / 2);
-      mbar_init(bar_full_b + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < BSTAGES; ++s) {
+      mbar_init(bar_full_b + 8 * s, 1);
+      mbar_init(bar_empty_b + 8 * s, 1);
+    }
+    for (int s = 0; s < XSTAGES; ++s) {
+      mbar_init(bar_full_x + 8 * s, 1);
+      mbar_init(bar_empty_x + 8 * s, NUM_PRODUCER_WARPS);
     }
     mbar_init(bar_accum, 1);
     mbar_init(bar_x, 1);
@@ -601,7 +625,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     Producer prod;
     prod.setup(a);
-    if (grp < nj) prod.prefetch(xrow, valid, kb0 + grp, a.D_in);
+    if (!x_tma && grp < nj) prod.prefetch(xrow, valid, kb0 + grp, a.D_in);
+    int xs_rel = xs_first;  // next input stage this warp has to release
+    auto release_x_until = [&](int stage_end) {  // release stages < stage_end
+      for (; xs_rel < stage_end && xs_rel <= xs_last; ++xs_rel) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty_x + 8 * ((xs_rel - xs_first) % XSTAGES));
+      }
+    };
 
     float mean = 0.f, rstd = 1.f;
     if (ln_staged) {
@@ -629,9 +660,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int s = j % STAGES;
       const uint32_t it = (uint32_t)(j / STAGES);
       float xs[Producer::F];
+      if (x_tma) {
+        // this block's inputs from the TMA-loaded input tiles (rows >= B and features >= D_in
+        // read as zero)
+        const int lo = (kb0 + j) * Producer::F;
+        const int st_lo = lo / 64, st_hi = (lo + Producer::F - 1) / 64;
+        release_x_until(st_lo);
+        bool ok = true;
+        for (int st = st_lo; st <= st_hi && ok; ++st) {
+          const int u = st - xs_first;
+          ok = mbar_wait_warp(bar_full_x + 8 * (u % XSTAGES), (uint32_t)(u / XSTAGES) & 1u);
+        }
+        if (!ok) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
+          *abort_flag = 1;
+          break;
+        }
 #pragma unroll
-      for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
-      if (j + 2 < nj) prod.prefetch(xrow, valid, kb0 + j + 2, a.D_in);
+        for (int f = 0; f < Producer::F; ++f) {
+          const int i = lo + f;
+          const int u = i / 64 - xs_first, c = i & 63;
+          const uint8_t* xt = smem + OFF_X + (u % XSTAGES) * X_STAGE_BYTES;
+          xs[f] = Act<MODE>::to_f(*reinterpret_cast<const T*>(
+              xt + r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2));
+        }
+      } else {
+#pragma unroll
+        for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
+        if (j + 2 < nj) prod.prefetch(xrow, valid, kb0 + j + 2, a.D_in);
+      }
       if (!mbar_wait_warp(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
         *abort_flag = 1;
@@ -643,6 +700,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
     }
+    if (x_tma) release_x_until(xs_last + 1);
 
     // ------------------------------------------------------------------ epilogue
     if (!mbar_wait_warp(bar_accum, 0)) {
@@ -706,9 +764,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t bytes = (uint32_t)BN * BK * 2;
       int issued = 0;
       for (int j = 0; j < nj; ++j) {
-        const int s = j % STAGES;
-        const uint32_t it = (uint32_t)(j / STAGES);
-        if (!mbar_wait(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
+        const int s = j % BSTAGES;
+        const uint32_t it = (uint32_t)(j / BSTAGES);
+        if (!mbar_wait(bar_empty_b + 8 * s, (it & 1u) ^ 1u)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
@@ -720,20 +778,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         ++issued;
       }
       // drain: wait (bounded) for the copies still landing in shared memory
-      for (int j = issued - 1; j >= 0 && j >= issued - STAGES; --j)
-        (void)mbar_wait(bar_full_b + 8 * (j % STAGES), (uint32_t)(j / STAGES) & 1u);
+      for (int j = issued - 1; j >= 0 && j >= issued - BSTAGES; --j)
+        (void)mbar_wait(bar_full_b + 8 * (j % BSTAGES), (uint32_t)(j / BSTAGES) & 1u);
     }
     __syncwarp();
-  } else {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, BN, BM);
       for (int j = 0; j < nj; ++j) {
-        const int s = j % STAGES;
+        const int s = j % STAGES, sb = j % BSTAGES;
         const uint32_t par = (uint32_t)(j / STAGES) & 1u;
         bool ok = mbar_wait(bar_full_a + 8 * s, par);
         if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
-        if (ok && !mbar_wait(bar_full_b + 8 * s, par)) {
+        if (ok && !mbar_wait(bar_full_b + 8 * sb, (uint32_t)(j / BSTAGES) & 1u)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
           ok = false;
         }
@@ -743,15 +801,37 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_fence_after();
         const uint32_t a_addr = s_base + OFF_A + s * A_STAGE_BYTES;
-        const uint32_t b_addr = s_base + OFF_B + s * B_STAGE_BYTES;
+        const uint32_t b_addr = s_base + OFF_B + sb * B_STAGE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
           mma_f16(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
                   idesc, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(bar_empty + 8 * s);
+        mma_commit(bar_empty_b + 8 * sb);
       }
       // signal the epilogue (also on abort, so that it does not wait out its own limit)
       mma_commit(bar_accum);
+    }
+    __syncwarp();
+  } else if (warp == XTMA_WARP) {
+    // ------------------------------------------------------------------ input tile TMA
+    if (lane == 0 && x_tma) {
+      int issued = 0;
+      for (int st = xs_first; st <= xs_last; ++st) {
+        const int u = st - xs_first, slot = u % XSTAGES;
+        if (!mbar_wait(bar_empty_x + 8 * slot, ((uint32_t)(u / XSTAGES) & 1u) ^ 1u)) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        mbar_arrive_expect_tx(bar_full_x + 8 * slot, (uint32_t)X_STAGE_BYTES);
+        tma_load_2d(s_base + OFF_X + slot * X_STAGE_BYTES, &tmap_x, bar_full_x + 8 * slot,
+                    st * 64, m0);
+        ++issued;
+      }
+      for (int u = issued - 1; u >= 0 && u >= issued - XSTAGES; --u)
+        (void)mbar_wait(bar_full_x + 8 * (u % XSTAGES), (uint32_t)(u / XSTAGES) & 1u);
     }
     __syncwarp();
   }
@@ -875,8 +955,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int BASIS, int MODE, class Producer>
-static cudaError_t launch_kernel(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
-                                 int splits, dim3 grid, cudaStream_t s) {
+static cudaError_t launch_kernel(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
+                                 const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
+                                 cudaStream_t s) {
   auto kern = kan_tc_kernel<BASIS, MODE, Producer>;
   static bool configured = false;  // one per template instance
   if (!configured) {
@@ -897,18 +978,20 @@ static cudaError_t launch_kernel(const CUtensorMap& tw, const LayerArgs& a, int 
   attr[0].val.clusterDim.z = (unsigned)splits;
   cfg.attrs = attr;
   cfg.numAttrs = splits > 1 ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, tw, a, BN, nb, splits);
+  const int use_x = (x_tma && Producer::kXFromTiles) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, tw, tx, a, BN, nb, splits, use_x);
 }
 
 // Compile-time-K producers for the shapes the BASELINE configs and common layers use; any other
 // K runs the runtime-K producer.
 template <int BASIS, int MODE>
-static cudaError_t dispatch_k(const CUtensorMap& tw, const LayerArgs& a, int BN, int nb,
-                              int splits, dim3 grid, cudaStream_t s) {
-#define KAN_TC_CASE(KK, HBV)                                                                  \
-  if (a.K == KK && (a.has_base != 0) == HBV)                                                  \
-    return launch_kernel<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, a, BN, nb, splits, \
-                                                                         grid, s);
+static cudaError_t dispatch_k(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
+                              const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
+                              cudaStream_t s) {
+#define KAN_TC_CASE(KK, HBV)                                                              \
+  if (a.K == KK && (a.has_base != 0) == HBV)                                              \
+    return launch_kernel<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, tx, x_tma, a, BN, \
+                                                                         nb, splits, grid, s);
   if (BASIS == KAN_CHEBY) {
     KAN_TC_CASE(4, true) KAN_TC_CASE(4, false) KAN_TC_CASE(5, true) KAN_TC_CASE(5, false)
     KAN_TC_CASE(8, true) KAN_TC_CASE(8, false) KAN_TC_CASE(9, true) KAN_TC_CASE(9, false)
@@ -920,7 +1003,8 @@ static cudaError_t dispatch_k(const CUtensorMap& tw, const LayerArgs& a, int BN,
     KAN_TC_CASE(6, true) KAN_TC_CASE(6, false) KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   }
 #undef KAN_TC_CASE
-  return launch_kernel<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, a, BN, nb, splits, grid, s);
+  return launch_kernel<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, tx, x_tma, a, BN, nb, splits,
+                                                                   grid, s);
 }
 
 }  // namespace tc
