@@ -88,6 +88,9 @@ SHAPES = [  # (basis, d_in, d_out, K, B)
     ("bspline", 24, 10, 8, 64),
     ("wavelet", 64, 96, 6, 200),
     ("wavelet", 32, 40, 8, 1),
+    # small grids of 256-wide tiles: the column-split cluster kernel (ragged rows and columns)
+    ("wavelet", 64, 320, 6, 200),
+    ("cheby", 256, 512, 9, 130),
 ]
 
 
