@@ -198,15 +198,6 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-// Bounded wait without sleeping between polls (the MMA issuers: their latency paces the kernel).
-__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity) {
-  if (tc::mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!tc::mbar_try_wait(bar, parity))
-    if (clock64() - t0 > tc::WAIT_LIMIT_CYCLES) return false;
-  return true;
-}
-
 // The abort flag as one value for the whole warp (lanes must not split around warp-wide steps).
 __device__ __forceinline__ bool warp_aborted(volatile int* flag) {
   return __shfl_sync(0xffffffffu, *flag, 0) != 0;
@@ -336,8 +327,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int lc = iss; lc < nch; lc += NUM_ISSUERS) {
         const int s = lc % SLOTS;
         const uint32_t par = (uint32_t)(lc / SLOTS) & 1u;
-        bool ok = mbar_wait_spin(bar_afull + 8 * s, par);
-        if (ok) ok = mbar_wait_spin(bar_pfull + 8 * s, par);
+        bool ok = mbar_wait(bar_afull + 8 * s, par);
+        if (ok) ok = mbar_wait(bar_pfull + 8 * s, par);
         if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
         if (!ok || *abort_flag) {
           *abort_flag = 1;

@@ -108,15 +108,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity`; false when the limit expired.  Failed polls back off
-// with a short sleep so that idle waiters do not crowd the shared-memory pipe the producers use.
+// try_wait with a suspend-time hint: the thread is suspended in hardware until the phase
+// completes or about `ns` nanoseconds pass, so a waiter neither spins on the issue slots the
+// working warps need nor wakes late.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity`; false when the limit expired.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    __nanosleep(64);
+  while (!mbar_try_wait_hint(bar, parity, 20000u))
     if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
-  }
   return true;
 }
 // Warp-wide bounded wait: lane 0 polls, the outcome is broadcast, each lane then takes the
