@@ -79,6 +79,7 @@ struct DeviceState {
   bool init = false;
   cudaStream_t stream = nullptr;
   int* err_word = nullptr;
+  int* err_host = nullptr;  // pinned mirror of the error word (read back on the engine stream)
   void* slot_ptr[NUM_SLOTS] = {};
   size_t slot_cap[NUM_SLOTS] = {};
   std::vector<PendingCopy> pending;     // async-mode results waiting for metal_kan_sync()
@@ -107,6 +108,7 @@ static int current_state(DeviceState** out) {
       KAN_CUDA_TRY(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
       d.err_word = device_error_ptr();
       if (!d.err_word) return fail(KAN_ERR_CUDA, "device error word unavailable");
+      KAN_CUDA_TRY(cudaHostAlloc((void**)&d.err_host, sizeof(int), cudaHostAllocDefault));
       d.init = true;
     }
   }
@@ -168,14 +170,26 @@ static int stage_in(DeviceState* d, int s, const void* host, size_t bytes, void*
   return KAN_OK;
 }
 
+// Read (and clear) the device error word through the pinned mirror on the engine stream: a
+// 4-byte copy ordered after the work already queued there, no device-wide synchronisation.
+static int read_device_error(DeviceState* d, int* out) {
+  KAN_CUDA_TRY(cudaMemcpyAsync(d->err_host, d->err_word, sizeof(int), cudaMemcpyDeviceToHost,
+                               d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  const int v = *d->err_host;
+  if (v) {
+    KAN_CUDA_TRY(cudaMemsetAsync(d->err_word, 0, sizeof(int), d->stream));
+    KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  }
+  *out = v;
+  return KAN_OK;
+}
+
 static int check_device_error(DeviceState* d) {
   int v = 0;
-  KAN_CUDA_TRY(cudaMemcpy(&v, d->err_word, sizeof(int), cudaMemcpyDeviceToHost));
-  if (v) {
-    int z = 0;
-    cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice);
-    return fail(KAN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
-  }
+  int rc = read_device_error(d, &v);
+  if (rc) return rc;
+  if (v) return fail(KAN_ERR_DEVICE_TIMEOUT, "a kernel's bounded wait expired (code %d)", v);
   return KAN_OK;
 }
 
@@ -532,11 +546,7 @@ int kan_device_error(int* code) {
   int rc = current_state(&d);
   if (rc) return rc;
   int v = 0;
-  KAN_CUDA_TRY(cudaMemcpy(&v, d->err_word, sizeof(int), cudaMemcpyDeviceToHost));
-  if (v) {
-    int z = 0;
-    KAN_CUDA_TRY(cudaMemcpy(d->err_word, &z, sizeof(int), cudaMemcpyHostToDevice));
-  }
+  if ((rc = read_device_error(d, &v))) return rc;
   if (code) *code = v;
   return KAN_OK;
 }

@@ -9,6 +9,7 @@
 from __future__ import annotations
 
 import ctypes
+import threading
 from typing import Dict, Optional, Tuple
 
 import numpy as np
@@ -114,6 +115,63 @@ class _Pinned:
             pass
 
 
+# ---------------------------------------------------------------------------------------------
+# results in pinned host memory: a device->host copy into pageable memory goes through the
+# driver's staging buffers at a fraction of the link rate, so forward() returns arrays backed by
+# page-locked buffers from a small pool (a buffer goes back to the pool when its array dies)
+# ---------------------------------------------------------------------------------------------
+_PIN_MIN = 1 << 16            # smaller results stay in ordinary memory
+_PIN_POOL_BYTES = 1 << 30     # pooled (idle) page-locked bytes kept for reuse
+_pin_pool: Dict[int, list] = {}
+_pin_pool_bytes = 0
+_pin_lock = threading.Lock()
+
+
+def _pin_take(nbytes: int) -> "_Pinned":
+    size = 1 << max(16, (int(nbytes) - 1).bit_length())
+    with _pin_lock:
+        lst = _pin_pool.get(size)
+        if lst:
+            global _pin_pool_bytes
+            _pin_pool_bytes -= size
+            return lst.pop()
+    return _Pinned(size)
+
+
+def _pin_give(buf: "_Pinned") -> None:
+    global _pin_pool_bytes
+    with _pin_lock:
+        if _pin_pool_bytes + buf.nbytes <= _PIN_POOL_BYTES:
+            _pin_pool.setdefault(buf.nbytes, []).append(buf)
+            _pin_pool_bytes += buf.nbytes
+            return
+    del buf  # over the pool's budget: freed
+
+
+class _PinnedOwner:
+    """Base object of a pinned result array: holds the buffer, returns it to the pool."""
+
+    def __init__(self, buf: "_Pinned", shape, dtype):
+        self._buf = buf
+        self.__array_interface__ = {"data": (buf.ptr, False), "shape": tuple(shape),
+                                    "typestr": "|V%d" % np.dtype(dtype).itemsize, "version": 3}
+
+    def __del__(self):
+        try:
+            _pin_give(self._buf)
+        except Exception:
+            pass
+
+
+def pinned_empty(shape, dtype) -> np.ndarray:
+    """np.empty(shape, dtype) in page-locked memory when the result is large enough to matter."""
+    dtype = np.dtype(dtype)
+    nbytes = int(np.prod(shape)) * dtype.itemsize
+    if nbytes < _PIN_MIN:
+        return np.empty(shape, dtype)
+    return np.asarray(_PinnedOwner(_pin_take(nbytes), shape, dtype)).view(dtype)
+
+
 def fetch(dev: DeviceBuffer, out: np.ndarray) -> np.ndarray:
     """Copy a device result into ``out``: now, or after ``sync()`` in async mode."""
     L = lib()
@@ -150,6 +208,11 @@ class DeviceLayerMixin:
     _WEIGHTS: Tuple[str, ...] = ()
 
     def __setattr__(self, name, value):
+        if not name.startswith("_"):
+            # any public assignment (a weight, a basis parameter, a flag) invalidates the cached
+            # kernel descriptor
+            d = self.__dict__
+            d["_pver"] = d.get("_pver", 0) + 1
         if name in type(self)._WEIGHTS and isinstance(value, np.ndarray):
             v = np.array(value, order="C", copy=True)
             v.flags.writeable = False

@@ -110,7 +110,27 @@ class KANLayerBase(E.DeviceLayerMixin):
         keep.append(hit[1])
         L.tc_weights = hit[1].ptr
 
+    def _desc_key(self):
+        """What the descriptor depends on: the public-attribute assignment counter (weights,
+        basis parameters such as inv_denominator, the input map and flags are all assigned
+        through __setattr__; to_int*/half() reassign the weights) and the dtype."""
+        return (self.__dict__.get("_pver", 0), self.dtype.str)
+
     def _descriptor(self, keep: list) -> D.KanLayer:
+        """The ``kan_layer`` descriptor, built once per weight/parameter state and cached (the
+        device buffers it points at are kept alive with it)."""
+        key = self._desc_key()
+        hit = self.__dict__.get("_desc_cache")
+        if hit is not None and hit[0] == key:
+            keep.extend(hit[2])
+            return hit[1]
+        own: list = []
+        L = self._build_descriptor(own)
+        object.__setattr__(self, "_desc_cache", (key, L, own))
+        keep.extend(own)
+        return L
+
+    def _build_descriptor(self, keep: list) -> D.KanLayer:
         act = self.dtype
         L = D.KanLayer()
         L.basis = self.BASIS
@@ -152,7 +172,7 @@ class KANLayerBase(E.DeviceLayerMixin):
         act = self.dtype
         x2, orig = E.as_activation(x, act, self.in_features)
         B = x2.shape[0]
-        y = np.empty((B, self.out_features), dtype=act)
+        y = E.pinned_empty((B, self.out_features), act)
         if B:
             s = self._scratch()
             dx = s.get("x", x2.nbytes).upload(x2)

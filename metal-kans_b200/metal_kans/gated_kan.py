@@ -78,7 +78,7 @@ class GatedKAN:
             raise TypeError("gate/up/down layers must share one dtype")
         x2, orig = E.as_activation(x, act, self.d_model)
         B = x2.shape[0]
-        y = np.empty((B, self.d_model), act)
+        y = E.pinned_empty((B, self.d_model), act)
         if B:
             esz = np.dtype(act).itemsize
             dx = self._scratch.get("x", x2.nbytes).upload(x2)

@@ -108,7 +108,7 @@ class MetalKAN:
         out_dim = self.layers_hidden[-1]
         if self.pipeline and len(self.layers) > 1 and act == np.float32:
             return E.restore_shape(self._forward_pipelined_cheby(x2), orig, out_dim)
-        y = np.empty((B, out_dim), act)
+        y = E.pinned_empty((B, out_dim), act)
         if B:
             dx = self._scratch.get("x", x2.nbytes).upload(x2)
             dy = self._scratch.get("y", y.nbytes)

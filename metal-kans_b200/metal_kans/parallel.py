@@ -75,7 +75,7 @@ def slice_layer_outputs(layer, start: int, stop: int):
 
     new = copy.copy(layer)
     d = new.__dict__
-    for k in ("_dev_cache", "_tc_cache", "_scratch_bufs", "_keepalive"):
+    for k in ("_dev_cache", "_tc_cache", "_scratch_bufs", "_keepalive", "_desc_cache"):
         d.pop(k, None)
     d["_versions"] = dict(layer.__dict__.get("_versions", {}))
     new.out_features = stop - start

@@ -164,3 +164,23 @@ def test_bad_arguments_raise(mk):
     L = mk.device.KanLayer()
     with pytest.raises(mk.KanError):
         lib.kan_forward(ctypes.byref(L), None, None, 1, None)
+
+
+def test_descriptor_cache_follows_parameter_changes(mk):
+    """The cached kernel descriptor is rebuilt when a weight, a basis parameter or the dtype
+    changes between calls."""
+    np.random.seed(5)
+    l = mk.FastKAN(64, 96, num_centers=8, grid_range=(-2, 2)).half()
+    x = np.random.default_rng(5).uniform(-2, 2, (200, 64)).astype(np.float32)
+    y0 = l(x)
+    assert layer_err(y0, l, x, "f16", "rbf") <= TOL["f16"]
+    l.inv_denominator = 0.5 * float(l.inv_denominator)
+    y1 = l(x)
+    assert not np.array_equal(y0, y1)
+    assert layer_err(y1, l, x, "f16", "rbf") <= TOL["f16"]
+    l.w_rbf = (np.asarray(l.w_rbf, np.float32) * 2).astype(np.float16)
+    y2 = l(x)
+    assert layer_err(y2, l, x, "f16", "rbf") <= TOL["f16"]
+    l.float()
+    y3 = l(x)
+    assert y3.dtype == np.float32 and layer_err(y3, l, x, "f32", "rbf") <= TOL["f32"]
