@@ -12,7 +12,7 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int MAX_SPLITS = 8;
+constexpr int MAX_SPLITS = 4;  // split-K cluster size (reduction slots sized for it)
 
 // Pack W (basis terms) and Wb (base weights) into Wp[D_out][NB*64]: block b, column j holds term
 // t = j % KT of feature i = b*F + j/KT (t < K: W[o, i*K + t]; t == K: Wb[o, i]); zero elsewhere.

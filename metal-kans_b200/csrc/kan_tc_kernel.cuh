@@ -30,7 +30,6 @@
 // cluster-wide barrier and releases TMEM.
 #pragma once
 
-#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include "kan_device.cuh"
@@ -55,7 +54,7 @@ constexpr int XTMA_WARP = 10;
 constexpr int THREADS = 352;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;  // ~1 s at the B200 boost clock
-constexpr int MAX_SPLITS = 8;                          // portable cluster size
+constexpr int MAX_SPLITS = 4;                          // split-K cluster size
 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_STAGE_BYTES;
@@ -69,14 +68,13 @@ constexpr int OFF_EPI = OFF_FLAG + 4;
 constexpr int OFF_STATS = (OFF_EPI + 4 + 15) / 16 * 16;    // LayerNorm partial sums / stats
 constexpr int SMEM_BYTES = OFF_STATS + 4 * BM * 4;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
-// Split-K receive buffers, over the (finished) pipeline buffers: one [128][slice + 4] fp32 slot per
-// split (slice = BN / splits columns); the largest case is 8 slots of 32-column slices.
-__host__ __device__ constexpr int recv_bytes(int splits, int slice) {
-  return splits * BM * (slice + 4) * 4;
+// Split-K reduction buffers, over the (finished) pipeline buffers: (splits - 1) receive slots and
+// (splits - 1) staging slots of [128][slice + 4] fp32 (slice = BN / splits columns).
+__host__ __device__ constexpr int red_bytes(int splits, int slice) {
+  return 2 * (splits - 1) * BM * (slice + 4) * 4;
 }
-static_assert(recv_bytes(4, 64) <= OFF_BAR && recv_bytes(8, 32) <= OFF_BAR &&
-                  recv_bytes(2, 128) <= OFF_BAR,
-              "split-K receive slots must fit in the stage buffers");
+static_assert(red_bytes(4, 64) <= OFF_BAR && red_bytes(2, 128) <= OFF_BAR,
+              "split-K reduction slots must fit in the stage buffers");
 // LayerNorm input tile (rows of <= 256 features) staged over the A stages before the first block
 static_assert(BM * 256 * 2 <= STAGES * A_STAGE_BYTES, "x tile must fit in the A stages");
 
@@ -157,29 +155,13 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
   return r;
 }
-// Loads issued as volatile asm in program order: a block of them leaves the SM before any of
-// their results is consumed (memory-level parallelism the compiler would not otherwise keep).
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-// 16-byte store into another CTA's shared memory; completes `bytes` on that CTA's mbarrier.
-__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a0, float a1, float a2,
-                                            float a3, uint32_t remote_bar) {
+// Shared -> shared copy into another CTA of the cluster, completing on that CTA's mbarrier.
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, uint32_t src_cta,
+                                               uint32_t bytes, uint32_t bar_cluster) {
   asm volatile(
-      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, "
-      "[%5];" ::"r"(remote_addr),
-      "f"(a0), "f"(a1), "f"(a2), "f"(a3), "r"(remote_bar)
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
       : "memory");
 }
 // Contiguous global -> shared copy by the bulk-copy engine, completing on an mbarrier.
@@ -617,7 +599,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     // the other splits' slices arrive after the first cluster barrier, i.e. after this point
     if (splits > 1)
-      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * BM * slice * 4));
+      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * BM * (slice + 4) * 4));
   }
   if (warp == MMA_WARP) tmem_alloc(s_base + OFF_TMEM, TMEM_COLS);
   tc_fence_before();
@@ -848,25 +830,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   if (splits > 1) {
-    __syncwarp();
-    // every CTA of the cluster has finished its main loop: stage buffers may now receive slices
-    cluster_sync_all();
+    // Split-K reduction.  Slot k of a CTA's receive area [0, (S-1) slots) holds the slice sent by
+    // the k-th other split; its staging area (the next S-1 slots) holds the slices it sends.
+    const int pitch = slice + 4;  // slot row pitch in floats
+    const int slot_bytes = BM * pitch * 4;
+    auto other = [&](int zz, int self) { return zz < self ? zz : zz - 1; };
+    const int half = slice >> 1;  // slice columns per producer warp (host: slice % 32 == 0)
+    bool ok = !producer_aborted && nj > 0;
     if (warp < NUM_PRODUCER_WARPS) {
+      // 1. stage this CTA's slices of the other splits' columns (TMEM -> shared)
       const int q = warp & 3, h = warp >> 2;
       const int r = q * 32 + lane;
-      const int row = m0 + r;
-      const int half = slice >> 1;  // slice columns per warp (host: slice % 32 == 0)
-      const int pitch = slice + 4;  // receive-slot row pitch in floats
       const uint32_t taddr0 = tmem_d + ((uint32_t)(q * 32) << 16);
-      bool ok = !producer_aborted && nj > 0;
-      // 1. push slice zz of this CTA's accumulator into slot z of CTA zz (remote async stores
-      //    completing on CTA zz's reduction barrier)
       if (ok) {
         for (int zz = 0; zz < splits; ++zz) {
           if (zz == z) continue;
-          const uint32_t rdst = map_to_rank(s_base + OFF_A, (uint32_t)zz) +
-                                (uint32_t)((z * BM + r) * pitch * 4);
-          const uint32_t rbar = map_to_rank(bar_red, (uint32_t)zz);
+          float* stage = reinterpret_cast<float*>(smem + OFF_A + (splits - 1 + other(zz, z)) *
+                                                                   slot_bytes) + r * pitch;
 #pragma unroll 1
           for (int cc = 0; cc < half; cc += 16) {
             const int cs = h * half + cc;  // column within the slice
@@ -874,18 +854,37 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_ld16(taddr0 + (uint32_t)(zz * slice + cs), v);
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              st_async_v4(rdst + (uint32_t)((cs + 4 * u) * 4), v[4 * u], v[4 * u + 1],
-                          v[4 * u + 2], v[4 * u + 3], rbar);
+              *reinterpret_cast<float4*>(stage + cs + 4 * u) =
+                  make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
           }
         }
       }
-      // 2. the other splits' slices of this CTA's own columns have landed (always waited for:
-      //    no remote store may still target this CTA's shared memory when it exits)
+      fence_proxy_async_smem();  // the staged slices are read by the bulk-copy engine
+    }
+    __syncwarp();
+    // every CTA has finished its main loop (its receive area is free) and staged its slices
+    cluster_sync_all();
+    // 2. one bulk copy per other split: staging slot -> that CTA's receive slot for this split
+    if (threadIdx.x == 0 && ok) {
+      for (int zz = 0; zz < splits; ++zz) {
+        if (zz == z) continue;
+        bulk_s2cluster(map_to_rank(s_base + OFF_A + other(z, zz) * slot_bytes, (uint32_t)zz),
+                       s_base + OFF_A + (splits - 1 + other(zz, z)) * slot_bytes,
+                       (uint32_t)slot_bytes, map_to_rank(bar_red, (uint32_t)zz));
+      }
+    }
+    if (warp < NUM_PRODUCER_WARPS) {
+      const int q = warp & 3, h = warp >> 2;
+      const int r = q * 32 + lane;
+      const int row = m0 + r;
+      const uint32_t taddr0 = tmem_d + ((uint32_t)(q * 32) << 16);
+      // 3. the other splits' slices of this CTA's own columns have landed (always waited for:
+      //    no copy may still target this CTA's shared memory when it exits)
       if (!mbar_wait_warp(bar_red, 0)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
         ok = false;
       }
-      // 3. sum in split order (deterministic), bias, store 16 outputs at a time
+      // 4. sum in split order (deterministic), bias, store 16 outputs at a time
       if (ok) {
         T* Y = (T*)a.Y;
         const T* bias = (const T*)a.bias;
@@ -904,8 +903,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
               for (int t = 0; t < 16; ++t) sum[t] += own[t];
             } else {
-              const float4* src =
-                  reinterpret_cast<const float4*>(recv + (zz * BM + r) * pitch + cs);
+              const float4* src = reinterpret_cast<const float4*>(
+                  recv + (other(zz, z) * BM + r) * pitch + cs);
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 const float4 p = src[u];
@@ -955,6 +954,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
+    // every copy out of this CTA's staging slots has landed (its receiver waited for it)
+    __syncwarp();
+    cluster_sync_all();
   }
 
   tc_fence_before();
