@@ -366,6 +366,60 @@ __device__ __forceinline__ void ln_row_stats(const LayerArgs& a, const uint8_t* 
 }
 
 // ---------------------------------------------------------------------------------------------
+// inputs of a block from the input tiles (64 features x 128 rows, 128-byte swizzled)
+// ---------------------------------------------------------------------------------------------
+// 16-bit element e of a uint4 array (e < 8 * N, compile-time after unrolling)
+template <int N>
+__device__ __forceinline__ uint32_t half_bits(const uint4 (&ch)[N], int e) {
+  const uint4 c = ch[e >> 3];
+  const uint32_t w = ((e & 7) >> 1) == 0 ? c.x : ((e & 7) >> 1) == 1 ? c.y : ((e & 7) >> 1) == 2 ? c.z : c.w;
+  return (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// Features lo .. lo + F - 1 of row r.  Inside one tile: the 16-byte chunks covering them (one
+// 16-byte load each, conflict-free across the warp thanks to the swizzle), the features picked
+// out in registers; a block that straddles two tiles reads its features one by one.
+template <int MODE, int F>
+__device__ __forceinline__ void read_x_block(const uint8_t* xring, int lo, int xs_first, int r,
+                                             float (&xs)[F]) {
+  using T = typename Act<MODE>::T;
+  const int e0 = lo & 63;
+  if (e0 + F <= 64) {
+    constexpr int NCH = (F + 7 + 7) / 8;  // chunks covering any start offset 0..7
+    const uint8_t* row = xring + ((lo / 64 - xs_first) % XSTAGES) * X_STAGE_BYTES + r * 128;
+    const int c0 = e0 >> 3, o = e0 & 7;
+    uint4 ch[NCH];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = c0 + k;
+      ch[k] = c < 8 ? *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4))
+                    : make_uint4(0, 0, 0, 0);
+    }
+    switch (o) {
+#define KAN_X_CASE(O)                                                                  \
+  case O:                                                                              \
+    _Pragma("unroll") for (int f = 0; f < F; ++f) {                                    \
+      const uint16_t b = (uint16_t)half_bits<NCH>(ch, O + f);                          \
+      xs[f] = Act<MODE>::to_f(*reinterpret_cast<const T*>(&b));                        \
+    }                                                                                  \
+    break;
+      KAN_X_CASE(0) KAN_X_CASE(1) KAN_X_CASE(2) KAN_X_CASE(3)
+      KAN_X_CASE(4) KAN_X_CASE(5) KAN_X_CASE(6) KAN_X_CASE(7)
+#undef KAN_X_CASE
+    }
+  } else {
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int i = lo + f;
+      const int u = i / 64 - xs_first, c = i & 63;
+      const uint8_t* xt = xring + (u % XSTAGES) * X_STAGE_BYTES;
+      xs[f] = Act<MODE>::to_f(*reinterpret_cast<const T*>(
+          xt + r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // A-tile producers: one row of one 64-column block
 // ---------------------------------------------------------------------------------------------
 
@@ -669,14 +723,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           *abort_flag = 1;
           break;
         }
-#pragma unroll
-        for (int f = 0; f < Producer::F; ++f) {
-          const int i = lo + f;
-          const int u = i / 64 - xs_first, c = i & 63;
-          const uint8_t* xt = smem + OFF_X + (u % XSTAGES) * X_STAGE_BYTES;
-          xs[f] = Act<MODE>::to_f(*reinterpret_cast<const T*>(
-              xt + r * 128 + ((((c >> 3) ^ (r & 7))) << 4) + (c & 7) * 2));
-        }
+        read_x_block<MODE, Producer::F>(smem + OFF_X, lo, xs_first, r, xs);
       } else {
 #pragma unroll
         for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
