@@ -8,17 +8,18 @@
 //
 //   warp 0      TMA producer: per stage, a 128-row x 32-word (512 codes) tile of the packed codes
 //               (128-byte swizzle) and the matching per-(row, group) fp32 scales.
-//   warp 1      TMEM allocator and MMA issuer: per 64-code chunk, 4
-//               tcgen05.mma.cta_group::1.kind::f16 with A read from TMEM (the decoded weights),
-//               B from shared memory (the basis tile), fp32 accumulators in TMEM.
-//   warp 2      basis TMA: per chunk, the [B x 64] tile of the basis matrix (below).
-//   warps 3-18  decoders, four warps per TMEM lane quarter taking turns by chunk; a thread owns
-//               one output row: 16-byte shared load of its four code words, per-group lookup
-//               tables (two registers: low and high bytes of the four
-//               dequantised values act(code_value * scale)), then per code pair one byte
-//               permute (prmt) -> a bf16x2 / f16x2 operand pair; tcgen05.st of the 32 columns into
-//               the TMEM A ring (8 chunks deep, to cover the MMA round trip).  After the K loop
-//               the first four read the accumulators.
+//   warps 1, 19 TMEM allocator (1) and MMA issuers, taking alternate units (a unit = two 64-code
+//               chunks): per chunk 4 tcgen05.mma.cta_group::1.kind::f16 with A read from TMEM
+//               (the decoded weights), B from shared memory (the basis tile), fp32 accumulators
+//               in TMEM (one per issuer, summed in the epilogue).
+//   warp 2      basis TMA: per unit, the two [B x 64] tiles of the basis matrix (below).
+//   warps 3-18  decoders, four groups of four warps (one per TMEM lane quarter); group h decodes
+//               unit h of every code stage.  A thread owns one output row: two 16-byte shared
+//               loads of its eight code words, per-group lookup tables (two registers: low and
+//               high bytes of the four dequantised values act(code_value * scale)), then per code
+//               pair one byte permute (prmt) -> a bf16x2 / f16x2 operand pair; tcgen05.st of the
+//               64 columns into the TMEM A ring (6 units deep, to cover the MMA round trip).
+//               After the K loop group 0 reads the accumulators.
 //
 // The decoded operand equals the reference's dequantised weight rounded once to the operand
 // dtype (metal_kan_bridge.mm:5073-5146, fused_kan.metal:2392-2441; code 3 of ternary -> 0).
@@ -68,31 +69,34 @@ using tc::tmem_alloc;
 using tc::tmem_dealloc;
 
 constexpr int ROWS = 128;              // output rows per CTA (the MMA's M)
-constexpr int CHUNK = 64;              // codes per pipeline step (4 words, 4 MMAs of K = 16)
+constexpr int CHUNK = 64;              // codes of one basis tile (4 words, 4 MMAs of K = 16)
+constexpr int UNIT = 2;                // chunks per pipeline unit (one decoder step, 8 MMAs)
 constexpr int STAGE_CHUNKS = 8;        // TMA stage: 32 words (128 B) per row
+constexpr int UNITS_PER_STAGE = STAGE_CHUNKS / UNIT;
 constexpr int CODE_STAGES = 4;
-constexpr int SLOTS = 8;               // TMEM A ring and shared basis ring
+constexpr int SLOTS = 6;               // TMEM A ring and shared basis ring, in units
 constexpr int MAXN = 64;               // largest (padded) batch
 constexpr int MAX_SPLITS = 8;
-constexpr int DEC_GROUPS = 4;          // decoder warp groups (one warp per lane quarter each)
+constexpr int DEC_GROUPS = UNITS_PER_STAGE;  // decoder group h decodes unit h of every stage
 constexpr int NUM_ISSUERS = 2;         // MMA-issuing threads (lane 0 of warp 1 and of the last warp)
 constexpr int WARP_TMA = 0, WARP_MMA = 1, WARP_PHI = 2, WARP_DEC0 = 3,
               NUM_DEC_WARPS = 4 * DEC_GROUPS, WARP_MMA2 = WARP_DEC0 + NUM_DEC_WARPS;
 constexpr int THREADS = (WARP_MMA2 + NUM_ISSUERS - 1) * 32;  // 640
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int A_COLS = 32;             // TMEM columns of one chunk (64 16-bit values per lane)
-constexpr int ACC_COL = SLOTS * A_COLS;  // accumulators after the A ring (256)
-// Several MMA issuers (issuer i takes the chunks lc with lc % NUM_ISSUERS == i), one accumulator
+constexpr int ACC_COL = SLOTS * UNIT * A_COLS;  // accumulators after the A ring (384)
+// Several MMA issuers (issuer i takes the units u with u % NUM_ISSUERS == i), one accumulator
 // each: at N = 16 the issue of tcgen05.mma, not the tensor pipe, bounds the rate, so more issuing
 // threads raise it.  The accumulators are summed in the epilogue.
 constexpr int NACC = NUM_ISSUERS;
 constexpr int CODE_STAGE_BYTES = ROWS * 128;
+static_assert(UNITS_PER_STAGE % NUM_ISSUERS == 0, "an issuer takes fixed unit positions");
 
 // Shared memory: code stages, scale stages (sized by the group size), the basis ring (sized by the
 // padded batch), the CTA's input slice when it fits, barriers.  Offsets are planned on the host.
 constexpr int OFF_CODE = 0;
 constexpr int OFF_SCALE = OFF_CODE + CODE_STAGES * CODE_STAGE_BYTES;
-// code full/empty per stage; A full, basis full, slot empty per slot; accumulators ready
+// code full/empty per stage; A full, basis full, slot empty per unit slot; accumulators ready
 constexpr int NUM_BARS = 2 * CODE_STAGES + 3 * SLOTS + 1;
 constexpr int SMEM_LIMIT = 227 * 1024;
 static_assert(ROWS * MAXN * 4 <= CODE_STAGES * CODE_STAGE_BYTES, "partials fit the code stages");
@@ -110,6 +114,7 @@ struct GemvParams {
   int off_phi, off_bar, smem_alloc;  // shared-memory layout
   int kb_cols;   // basis columns of the basis matrix (D_in*K rounded up to 64); base columns follow
   int kpad;      // columns of the basis matrix
+  uint32_t mul17;  // 0x11, passed at run time so that the selector products stay multiplies
 };
 
 // Position inside a 16-code word of the MMA K index that code u lands on (see decode_word).
@@ -125,15 +130,16 @@ __device__ __forceinline__ uint32_t phi_off(int n, int k) {
 
 // 16 codes of one word -> 8 operand pairs.  Column j (0..3) holds codes (j, j+4), column 4+j holds
 // codes (j+8, j+12): byte t of a_j is code 4t+j; the selector byte 17*c + 64 = nibbles (c, c+4)
-// picks the low byte of value c from tlo and its high byte from thi.
-__device__ __forceinline__ void decode_word(uint32_t w, uint32_t tlo, uint32_t thi,
-                                            uint32_t* out) {
+// picks the low byte of value c from tlo and its high byte from thi.  The selector of the upper
+// code pair is the high word of a_j * (17 << 16) (a multiply-high, on the FMA pipe like the
+// lower one, which leaves the integer pipe to the masks and byte permutes).
+__device__ __forceinline__ void decode_word(uint32_t w, uint32_t tlo, uint32_t thi, uint32_t m17,
+                                            uint32_t m17h, uint32_t* out) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t aj = (w >> (2 * j)) & 0x03030303u;
-    const uint32_t sel = aj * 0x11u + 0x40404040u;
-    out[j] = __byte_perm(tlo, thi, sel);
-    out[4 + j] = __byte_perm(tlo, thi, sel >> 16);
+    out[j] = __byte_perm(tlo, thi, aj * m17 + 0x40404040u);
+    out[4 + j] = __byte_perm(tlo, thi, __umulhi(aj, m17h) + 0x4040u);
   }
 }
 
@@ -147,7 +153,7 @@ __device__ __forceinline__ uint32_t act_bits(float v) {
 // Lookup table of the four dequantised values of a group with scale s: tlo = their low bytes,
 // thi = their high bytes (byte c = value of code c).
 template <int MODE, int FMT>
-__device__ __forceinline__ void make_table(float s, const float (&cb)[4], uint32_t& tlo,
+__device__ __forceinline__ void make_table(float s, const float* cb, uint32_t& tlo,
                                            uint32_t& thi) {
   if (FMT == KAN_W_TERNARY) {
     // codes 0, 1, 2, 3 -> -s, 0, +s, 0 (the product by -1 / +1 is exact: act(-s) = -act(s))
@@ -176,15 +182,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15])
-      : "memory");
-}
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -208,32 +205,29 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   return v;
 }
 
-// Chunk `lc` of this CTA's sequence (basis chunks, then base chunks).
-struct ChunkInfo {
-  int part;   // 0 basis (W), 1 base (Wb)
-  int cid;    // chunk index within the row of that matrix (codes 64*cid .. 64*cid + 63)
-  int stage;  // global stage index
-  int pos;    // chunk within the stage
-};
-__device__ __forceinline__ ChunkInfo chunk_info(int lc, int nb_ch, int cb0, int cB0,
-                                                int nst_b) {
-  ChunkInfo c;
-  if (lc < nb_ch) {
-    c.part = 0;
-    c.cid = cb0 + lc;
-    c.stage = lc / STAGE_CHUNKS;
-    c.pos = lc % STAGE_CHUNKS;
-  } else {
-    const int lb = lc - nb_ch;
-    c.part = 1;
-    c.cid = cB0 + lb;
-    c.stage = nst_b + lb / STAGE_CHUNKS;
-    c.pos = lb % STAGE_CHUNKS;
+// The CTA's work: the basis chunks [cb0, cb0 + nb_ch) of W, then the base chunks
+// [cB0, cB0 + nB_ch) of Wb, in code stages of 8 chunks (a part's last stage may be short; the base
+// part starts a new stage).  Unit u = 4 * stage + h covers chunks 2h, 2h + 1 of its stage; units
+// past the end of a short stage are empty but still pass through every ring (so that all roles
+// count units alike).
+struct Plan {
+  int cb0, cB0, nb_ch, nB_ch, nst_b, nst;
+  __device__ __forceinline__ bool base(int st) const { return st >= nst_b; }
+  __device__ __forceinline__ int first_cid(int st) const {
+    return st < nst_b ? cb0 + st * STAGE_CHUNKS : cB0 + (st - nst_b) * STAGE_CHUNKS;
   }
-  return c;
-}
+  __device__ __forceinline__ int stage_chunks(int st) const {
+    return st < nst_b ? min(STAGE_CHUNKS, nb_ch - st * STAGE_CHUNKS)
+                      : min(STAGE_CHUNKS, nB_ch - (st - nst_b) * STAGE_CHUNKS);
+  }
+  // chunks in unit u (0, 1 or 2)
+  __device__ __forceinline__ int unit_chunks(int u) const {
+    const int h = u % UNITS_PER_STAGE;
+    return max(0, min(UNIT, stage_chunks(u / UNITS_PER_STAGE) - UNIT * h));
+  }
+};
 
-template <int MODE, int FMT>
+template <int MODE, int FMT, bool HALF_GROUPS>
 __global__ void __launch_bounds__(THREADS, 1)
     kan_gemv_kernel(const __grid_constant__ CUtensorMap tm_wc,
                     const __grid_constant__ CUtensorMap tm_ws,
@@ -253,7 +247,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile uint32_t* tmem_slot =
       reinterpret_cast<volatile uint32_t*>(smem + p.off_bar + NUM_BARS * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_bar + NUM_BARS * 8 + 4);
-  const int phi_slot_bytes = p.npad * 128;
+  const int tile_bytes = p.npad * 128;            // one chunk's basis tile
+  const int phi_slot_bytes = UNIT * tile_bytes;   // one unit's
   const int scale_stage_bytes = ROWS * p.scale_pitch * 4;  // a multiple of 1024
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -262,12 +257,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int B = a.B, K = a.K;
   // this split's input features and the chunk ranges they cover
   const int f0 = z * p.FS, f1 = min(a.D_in, f0 + p.FS);
-  const int cb0 = (f0 * K) / CHUNK, cb1 = (f1 * K + CHUNK - 1) / CHUNK;
-  const int cB0 = f0 / CHUNK, cB1 = a.has_base ? (f1 + CHUNK - 1) / CHUNK : cB0;
-  const int nb_ch = max(0, cb1 - cb0), nB_ch = max(0, cB1 - cB0);
-  const int nch = nb_ch + nB_ch;
-  const int nst_b = (nb_ch + STAGE_CHUNKS - 1) / STAGE_CHUNKS;
-  const int nst = nst_b + (nB_ch + STAGE_CHUNKS - 1) / STAGE_CHUNKS;
+  Plan pl;
+  pl.cb0 = (f0 * K) / CHUNK;
+  pl.cB0 = f0 / CHUNK;
+  const int cb1 = (f1 * K + CHUNK - 1) / CHUNK;
+  const int cB1 = a.has_base ? (f1 + CHUNK - 1) / CHUNK : pl.cB0;
+  pl.nb_ch = max(0, cb1 - pl.cb0);
+  pl.nB_ch = max(0, cB1 - pl.cB0);
+  pl.nst_b = (pl.nb_ch + STAGE_CHUNKS - 1) / STAGE_CHUNKS;
+  pl.nst = pl.nst_b + (pl.nB_ch + STAGE_CHUNKS - 1) / STAGE_CHUNKS;
+  const int nst = pl.nst, nunits = nst * UNITS_PER_STAGE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < CODE_STAGES; ++s) {
@@ -275,7 +274,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar_cempty + 8 * s, NUM_DEC_WARPS);
     }
     for (int s = 0; s < SLOTS; ++s) {
-      mbar_init(bar_afull + 8 * s, 4);  // the four warps of the chunk's decoder group
+      mbar_init(bar_afull + 8 * s, 4);  // the four warps of the unit's decoder group
       mbar_init(bar_pfull + 8 * s, 1);
       mbar_init(bar_sempty + 8 * s, 1);
     }
@@ -302,9 +301,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         if (*abort_flag) break;
-        const bool base = st >= nst_b;
-        const int first_cid = base ? cB0 + (st - nst_b) * STAGE_CHUNKS
-                                   : cb0 + st * STAGE_CHUNKS;
+        const bool base = pl.base(st);
+        const int first_cid = pl.first_cid(st);
         const int g0 = first_cid * CHUNK / p.gs;
         mbar_arrive_expect_tx(bar_cfull + 8 * slot, bytes);
         tma_load_2d(s_base + OFF_CODE + slot * CODE_STAGE_BYTES, base ? &tm_bc : &tm_wc,
@@ -324,9 +322,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int iss = warp == WARP_MMA ? 0 : 1 + warp - WARP_MMA2;
       const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, p.npad, 128);
       const uint32_t dacc = tmem + ACC_COL + (uint32_t)(iss * p.npad);
-      for (int lc = iss; lc < nch; lc += NUM_ISSUERS) {
-        const int s = lc % SLOTS;
-        const uint32_t par = (uint32_t)(lc / SLOTS) & 1u;
+      uint32_t acc_flag = 0u;  // the issuer's first MMA overwrites its accumulator
+      for (int u = iss; u < nunits; u += NUM_ISSUERS) {
+        const int s = u % SLOTS;
+        const uint32_t par = (uint32_t)(u / SLOTS) & 1u;
         bool ok = mbar_wait(bar_afull + 8 * s, par);
         if (ok) ok = mbar_wait(bar_pfull + 8 * s, par);
         if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
@@ -335,13 +334,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        // K advance of 32 B inside the 128-byte swizzle row = +2 in the descriptor address field
-        const uint64_t bdesc = smem_desc_sw128(s_base + p.off_phi + s * phi_slot_bytes);
-        const uint32_t aaddr = tmem + (uint32_t)(s * A_COLS);
+        const int nv = pl.unit_chunks(u);
+        for (int c = 0; c < nv; ++c) {
+          // K advance of 32 B inside the 128-byte swizzle row = +2 in the descriptor address
+          const uint64_t bdesc =
+              smem_desc_sw128(s_base + p.off_phi + s * phi_slot_bytes + c * tile_bytes);
+          const uint32_t aaddr = tmem + (uint32_t)((s * UNIT + c) * A_COLS);
 #pragma unroll
-        for (int kk = 0; kk < CHUNK / 16; ++kk)
-          mma_ts(dacc, aaddr + (uint32_t)(kk * 8), bdesc + (uint64_t)(2 * kk), idesc,
-                 (lc >= NUM_ISSUERS || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < CHUNK / 16; ++kk) {
+            mma_ts(dacc, aaddr + (uint32_t)(kk * 8), bdesc + (uint64_t)(2 * kk), idesc, acc_flag);
+            acc_flag = 1u;
+          }
+        }
         mma_commit(bar_sempty + 8 * s);
       }
       mma_commit(bar_acc);
@@ -352,33 +356,40 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       // the basis matrix is written by the pre-pass kernel this launch depends on
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      const uint32_t bytes = (uint32_t)phi_slot_bytes;
       int issued = 0;
-      for (int lc = 0; lc < nch; ++lc) {
-        const int s = lc % SLOTS;
-        if (!mbar_wait(bar_sempty + 8 * s, ((uint32_t)(lc / SLOTS) & 1u) ^ 1u)) {
+      for (int u = 0; u < nunits; ++u) {
+        const int s = u % SLOTS;
+        if (!mbar_wait(bar_sempty + 8 * s, ((uint32_t)(u / SLOTS) & 1u) ^ 1u)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
-        const ChunkInfo ci = chunk_info(lc, nb_ch, cb0, cB0, nst_b);
-        const int col = (ci.part == 0 ? 0 : p.kb_cols) + ci.cid * CHUNK;
-        mbar_arrive_expect_tx(bar_pfull + 8 * s, bytes);
-        tma_load_2d(s_base + p.off_phi + s * phi_slot_bytes, &tm_phi, bar_pfull + 8 * s, col, 0);
+        const int nv = pl.unit_chunks(u);
+        const int st = u / UNITS_PER_STAGE, h = u % UNITS_PER_STAGE;
+        if (nv == 0) {
+          mbar_arrive(bar_pfull + 8 * s);
+        } else {
+          const int col = (pl.base(st) ? p.kb_cols : 0) + (pl.first_cid(st) + UNIT * h) * CHUNK;
+          mbar_arrive_expect_tx(bar_pfull + 8 * s, (uint32_t)(nv * tile_bytes));
+          for (int c = 0; c < nv; ++c)
+            tma_load_2d(s_base + p.off_phi + s * phi_slot_bytes + c * tile_bytes, &tm_phi,
+                        bar_pfull + 8 * s, col + c * CHUNK, 0);
+        }
         ++issued;
       }
-      for (int lc = issued - 1; lc >= 0 && lc >= issued - SLOTS; --lc)
-        (void)mbar_wait(bar_pfull + 8 * (lc % SLOTS), (uint32_t)(lc / SLOTS) & 1u);
+      for (int u = issued - 1; u >= 0 && u >= issued - SLOTS; --u)
+        (void)mbar_wait(bar_pfull + 8 * (u % SLOTS), (uint32_t)(u / SLOTS) & 1u);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ decoders + epilogue
     const int dw = warp - WARP_DEC0;
     const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int h = dw >> 2;            // this warp decodes the chunks lc with lc % DEC_GROUPS == h
+    const int h = dw >> 2;            // this warp's group decodes unit h of every stage
     const int r = q * 32 + lane;      // row within the CTA tile
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t m17 = p.mul17, m17h = p.mul17 << 16;
     float cbw[4] = {0.f, 0.f, 0.f, 0.f}, cbb[4] = {0.f, 0.f, 0.f, 0.f};
     if (FMT == KAN_W_INT2) {
 #pragma unroll
@@ -387,10 +398,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         cbb[c] = a.has_base ? __ldg(a.wb.codebook + c) : 0.f;
       }
     }
-    // Four warp groups decode alternate chunks, so one group's TMEM store latency overlaps the
-    // other groups' decoding; each chunk is published as soon as its store has completed.
+    // Per stage: wait for the codes, take this group's unit (two 16-byte loads per row and the
+    // scales of its groups), release the stage, decode into the TMEM A ring, publish the unit.
     uint32_t op[32];
-    int lc = 0;
     for (int st = 0; st < nst && !warp_aborted(abort_flag); ++st) {
       const int slot = st % CODE_STAGES;
       if (!mbar_wait_warp(bar_cfull + 8 * slot, (uint32_t)(st / CODE_STAGES) & 1u)) {
@@ -398,51 +408,67 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 1;
         break;
       }
-      const bool base = st >= nst_b;
-      const int first_cid = base ? cB0 + (st - nst_b) * STAGE_CHUNKS : cb0 + st * STAGE_CHUNKS;
+      const int u = st * UNITS_PER_STAGE + h;
+      const int s = u % SLOTS;
+      const int nv = pl.unit_chunks(u);
+      const bool base = pl.base(st);
+      const int first_cid = pl.first_cid(st);
       const int gbase = ((first_cid * CHUNK) >> p.gs_log2) & ~3;
-      const int nchunks = base ? min(STAGE_CHUNKS, nB_ch - (st - nst_b) * STAGE_CHUNKS)
-                               : min(STAGE_CHUNKS, nb_ch - st * STAGE_CHUNKS);
+      const int cid0 = first_cid + UNIT * h;
       const uint8_t* cst = smem + OFF_CODE + slot * CODE_STAGE_BYTES + r * 128;
-      bool stage_ok = true;
       const float* sst = reinterpret_cast<const float*>(smem + OFF_SCALE +
                                                         slot * scale_stage_bytes) +
                          r * p.scale_pitch;
-      for (int pos = 0; pos < nchunks; ++pos, ++lc) {
-        if (lc % DEC_GROUPS != h) continue;
-        const int s = lc % SLOTS;
-        if (!mbar_wait_warp(bar_sempty + 8 * s, ((uint32_t)(lc / SLOTS) & 1u) ^ 1u)) {
-          raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
-          *abort_flag = 1;
-          stage_ok = false;
-          break;
+      uint4 wv0 = make_uint4(0u, 0u, 0u, 0u), wv1 = wv0;
+      // lookup tables of the unit's four 32-code quarters (a group covers whole quarters)
+      uint32_t tlo[4], thi[4];
+      if (nv > 0) {
+        wv0 = *reinterpret_cast<const uint4*>(cst + (((UNIT * h) ^ (r & 7)) << 4));
+        if (nv > 1) wv1 = *reinterpret_cast<const uint4*>(cst + (((UNIT * h + 1) ^ (r & 7)) << 4));
+        const float* cb = base ? cbb : cbw;
+        if (HALF_GROUPS) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            make_table<MODE, FMT>(sst[((cid0 * CHUNK + 32 * j) >> p.gs_log2) - gbase], cb, tlo[j],
+                                  thi[j]);
+        } else {
+          // groups of 64 or 128 codes: one table per chunk
+#pragma unroll
+          for (int c = 0; c < UNIT; ++c) {
+            make_table<MODE, FMT>(sst[(((cid0 + c) * CHUNK) >> p.gs_log2) - gbase], cb,
+                                  tlo[2 * c], thi[2 * c]);
+            tlo[2 * c + 1] = tlo[2 * c];
+            thi[2 * c + 1] = thi[2 * c];
+          }
         }
-        const int cid = first_cid + pos;
-        const uint4 wv = *reinterpret_cast<const uint4*>(cst + ((pos ^ (r & 7)) << 4));
-        // groups of words 0-1 and 2-3 (a group spans >= 2 words: gs >= 32)
-        const int ga = ((cid * CHUNK) >> p.gs_log2) - gbase;
-        const int gb = ((cid * CHUNK + 32) >> p.gs_log2) - gbase;
-        uint32_t tlo0, thi0, tlo1, thi1;
-        make_table<MODE, FMT>(sst[ga], base ? cbb : cbw, tlo0, thi0);
-        if (gb != ga) make_table<MODE, FMT>(sst[gb], base ? cbb : cbw, tlo1, thi1);
-        else {
-          tlo1 = tlo0;
-          thi1 = thi0;
-        }
-        decode_word(wv.x, tlo0, thi0, op);
-        decode_word(wv.y, tlo0, thi0, op + 8);
-        decode_word(wv.z, tlo1, thi1, op + 16);
-        decode_word(wv.w, tlo1, thi1, op + 24);
-        tmem_st32(tmem + lane_base + (uint32_t)(s * A_COLS), op);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_afull + 8 * s);
       }
-      if (!stage_ok) break;
-      // every code word of this stage has been read into registers
+      // every code word and scale of this stage this warp needs is in registers
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_cempty + 8 * slot);
+      if (!mbar_wait_warp(bar_sempty + 8 * s, ((uint32_t)(u / SLOTS) & 1u) ^ 1u)) {
+        raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
+        *abort_flag = 1;
+        break;
+      }
+      if (nv > 0) {
+        const uint32_t ta = tmem + lane_base + (uint32_t)(s * UNIT * A_COLS);
+        decode_word(wv0.x, tlo[0], thi[0], m17, m17h, op);
+        decode_word(wv0.y, tlo[0], thi[0], m17, m17h, op + 8);
+        decode_word(wv0.z, tlo[1], thi[1], m17, m17h, op + 16);
+        decode_word(wv0.w, tlo[1], thi[1], m17, m17h, op + 24);
+        tmem_st32(ta, op);
+        if (nv > 1) {
+          decode_word(wv1.x, tlo[2], thi[2], m17, m17h, op);
+          decode_word(wv1.y, tlo[2], thi[2], m17, m17h, op + 8);
+          decode_word(wv1.z, tlo[3], thi[3], m17, m17h, op + 16);
+          decode_word(wv1.w, tlo[3], thi[3], m17, m17h, op + 24);
+          tmem_st32(ta + (uint32_t)A_COLS, op);
+        }
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_afull + 8 * s);
     }
 
     // ------------------------------------------------------------------ epilogue
@@ -455,6 +481,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     // issuers in a fixed order) into the partials [n][ROWS] over the finished code stages
     const bool reader = h == 0;
     float* part = reinterpret_cast<float*>(smem + OFF_CODE);
+    // issuer u takes the units whose position in the stage is u mod 2: it had an MMA iff some
+    // stage holds more than 2u chunks
+    const int maxc = max(min(STAGE_CHUNKS, pl.nb_ch), min(STAGE_CHUNKS, pl.nB_ch));
     for (int c = 0; c < p.npad; c += 16) {
       if (!reader) break;
       float acc[16];
@@ -462,7 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int t = 0; t < 16; ++t) acc[t] = 0.f;
 #pragma unroll
       for (int u = 0; u < NACC; ++u) {
-        if (u >= nch) continue;  // issuer u had no chunk
+        if (maxc <= UNIT * u) continue;  // issuer u had no chunk
         float v[16];
         tc::tmem_ld16(tmem + lane_base + (uint32_t)(ACC_COL + u * p.npad + c), v);
 #pragma unroll
@@ -623,10 +652,11 @@ static GemvParams plan(const LayerArgs& a) {
   p.words_b = (a.D_in + 15) / 16;
   const int scale_end = OFF_SCALE + CODE_STAGES * ROWS * p.scale_pitch * 4;
   p.off_phi = (scale_end + 1023) / 1024 * 1024;
-  p.off_bar = p.off_phi + SLOTS * p.npad * 128;
+  p.off_bar = p.off_phi + SLOTS * UNIT * p.npad * 128;
   p.smem_alloc = p.off_bar + NUM_BARS * 8 + 16 + 1024;  // + slack to align the base to 1024 B
   p.kb_cols = (a.D_in * a.K + CHUNK - 1) / CHUNK * CHUNK;
   p.kpad = p.kb_cols + (a.has_base ? (a.D_in + CHUNK - 1) / CHUNK * CHUNK : 0);
+  p.mul17 = 0x11u;
   return p;
 }
 
@@ -713,12 +743,17 @@ cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
-               const CUtensorMap, LayerArgs, GemvParams) =
-      bf ? (tern ? kan_gemv_kernel<MODE_BF16, KAN_W_TERNARY> : kan_gemv_kernel<MODE_BF16, KAN_W_INT2>)
-         : (tern ? kan_gemv_kernel<MODE_F16, KAN_W_TERNARY> : kan_gemv_kernel<MODE_F16, KAN_W_INT2>);
-  static bool configured[4] = {false, false, false, false};
-  const int ki = (bf ? 2 : 0) + (tern ? 0 : 1);
+  using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const CUtensorMap, const CUtensorMap, LayerArgs, GemvParams);
+  // [bf16][int2][32-code groups]
+  static const KernFn kerns[8] = {
+      kan_gemv_kernel<MODE_F16, KAN_W_TERNARY, false>, kan_gemv_kernel<MODE_F16, KAN_W_TERNARY, true>,
+      kan_gemv_kernel<MODE_F16, KAN_W_INT2, false>, kan_gemv_kernel<MODE_F16, KAN_W_INT2, true>,
+      kan_gemv_kernel<MODE_BF16, KAN_W_TERNARY, false>, kan_gemv_kernel<MODE_BF16, KAN_W_TERNARY, true>,
+      kan_gemv_kernel<MODE_BF16, KAN_W_INT2, false>, kan_gemv_kernel<MODE_BF16, KAN_W_INT2, true>};
+  const int ki = (bf ? 4 : 0) + (tern ? 0 : 2) + (p.gs == 32 ? 1 : 0);
+  const KernFn kern = kerns[ki];
+  static bool configured[8] = {false, false, false, false, false, false, false, false};
   if (!configured[ki]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SMEM_LIMIT);
