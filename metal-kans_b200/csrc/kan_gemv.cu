@@ -96,8 +96,9 @@ static_assert(UNITS_PER_STAGE % NUM_ISSUERS == 0, "an issuer takes fixed unit po
 // padded batch), the CTA's input slice when it fits, barriers.  Offsets are planned on the host.
 constexpr int OFF_CODE = 0;
 constexpr int OFF_SCALE = OFF_CODE + CODE_STAGES * CODE_STAGE_BYTES;
-// code full/empty per stage; A full, basis full, slot empty per unit slot; accumulators ready
-constexpr int NUM_BARS = 2 * CODE_STAGES + 3 * SLOTS + 1;
+// code full/empty per stage; unit full (decoded A + basis tiles), slot empty per unit slot;
+// accumulators ready
+constexpr int NUM_BARS = 2 * CODE_STAGES + 2 * SLOTS + 1;
 constexpr int SMEM_LIMIT = 227 * 1024;
 static_assert(ROWS * MAXN * 4 <= CODE_STAGES * CODE_STAGE_BYTES, "partials fit the code stages");
 static_assert(ACC_COL + NACC * MAXN <= (int)TMEM_COLS, "TMEM budget");
@@ -240,9 +241,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_cfull = s_base + p.off_bar;
   const uint32_t bar_cempty = bar_cfull + CODE_STAGES * 8;
-  const uint32_t bar_afull = bar_cempty + CODE_STAGES * 8;
-  const uint32_t bar_pfull = bar_afull + SLOTS * 8;
-  const uint32_t bar_sempty = bar_pfull + SLOTS * 8;
+  const uint32_t bar_afull = bar_cempty + CODE_STAGES * 8;  // decoders + basis TMA
+  const uint32_t bar_sempty = bar_afull + SLOTS * 8;
   const uint32_t bar_acc = bar_sempty + SLOTS * 8;
   volatile uint32_t* tmem_slot =
       reinterpret_cast<volatile uint32_t*>(smem + p.off_bar + NUM_BARS * 8);
@@ -274,8 +274,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(bar_cempty + 8 * s, NUM_DEC_WARPS);
     }
     for (int s = 0; s < SLOTS; ++s) {
-      mbar_init(bar_afull + 8 * s, 4);  // the four warps of the unit's decoder group
-      mbar_init(bar_pfull + 8 * s, 1);
+      // the four warps of the unit's decoder group + the basis TMA's arrival (with its bytes)
+      mbar_init(bar_afull + 8 * s, 5);
       mbar_init(bar_sempty + 8 * s, 1);
     }
     mbar_init(bar_acc, NUM_ISSUERS);  // one commit per MMA issuer
@@ -322,31 +322,42 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int iss = warp == WARP_MMA ? 0 : 1 + warp - WARP_MMA2;
       const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, p.npad, 128);
       const uint32_t dacc = tmem + ACC_COL + (uint32_t)(iss * p.npad);
+      // descriptor of slot 0's first basis tile; slot s, chunk c, K step kk add
+      // (s * phi_slot_bytes + c * tile_bytes + 32 * kk) >> 4 to its address field
+      const uint64_t bdesc0 = smem_desc_sw128(s_base + p.off_phi);
       uint32_t acc_flag = 0u;  // the issuer's first MMA overwrites its accumulator
+      int s = iss % SLOTS;
+      uint32_t par = (uint32_t)(iss / SLOTS) & 1u;
       for (int u = iss; u < nunits; u += NUM_ISSUERS) {
-        const int s = u % SLOTS;
-        const uint32_t par = (uint32_t)(u / SLOTS) & 1u;
-        bool ok = mbar_wait(bar_afull + 8 * s, par);
-        if (ok) ok = mbar_wait(bar_pfull + 8 * s, par);
-        if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
-        if (!ok || *abort_flag) {
+        if (!mbar_wait(bar_afull + 8 * s, par)) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
           *abort_flag = 1;
           break;
         }
+        if (*abort_flag) break;
         tc_fence_after();
         const int nv = pl.unit_chunks(u);
-        for (int c = 0; c < nv; ++c) {
-          // K advance of 32 B inside the 128-byte swizzle row = +2 in the descriptor address
-          const uint64_t bdesc =
-              smem_desc_sw128(s_base + p.off_phi + s * phi_slot_bytes + c * tile_bytes);
-          const uint32_t aaddr = tmem + (uint32_t)((s * UNIT + c) * A_COLS);
+        const uint64_t bd = bdesc0 + (uint64_t)((s * phi_slot_bytes) >> 4);
+        const uint32_t ad = tmem + (uint32_t)(s * UNIT * A_COLS);
+        if (nv > 0) {
 #pragma unroll
           for (int kk = 0; kk < CHUNK / 16; ++kk) {
-            mma_ts(dacc, aaddr + (uint32_t)(kk * 8), bdesc + (uint64_t)(2 * kk), idesc, acc_flag);
+            mma_ts(dacc, ad + (uint32_t)(kk * 8), bd + (uint64_t)(2 * kk), idesc, acc_flag);
             acc_flag = 1u;
           }
         }
+        if (nv > 1) {
+          const uint64_t bd1 = bd + (uint64_t)(tile_bytes >> 4);
+#pragma unroll
+          for (int kk = 0; kk < CHUNK / 16; ++kk)
+            mma_ts(dacc, ad + (uint32_t)(A_COLS + kk * 8), bd1 + (uint64_t)(2 * kk), idesc, 1u);
+        }
         mma_commit(bar_sempty + 8 * s);
+        s += NUM_ISSUERS;
+        if (s >= SLOTS) {
+          s -= SLOTS;
+          par ^= 1u;
+        }
       }
       mma_commit(bar_acc);
     }
@@ -368,18 +379,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int nv = pl.unit_chunks(u);
         const int st = u / UNITS_PER_STAGE, h = u % UNITS_PER_STAGE;
         if (nv == 0) {
-          mbar_arrive(bar_pfull + 8 * s);
+          mbar_arrive(bar_afull + 8 * s);
         } else {
           const int col = (pl.base(st) ? p.kb_cols : 0) + (pl.first_cid(st) + UNIT * h) * CHUNK;
-          mbar_arrive_expect_tx(bar_pfull + 8 * s, (uint32_t)(nv * tile_bytes));
+          mbar_arrive_expect_tx(bar_afull + 8 * s, (uint32_t)(nv * tile_bytes));
           for (int c = 0; c < nv; ++c)
             tma_load_2d(s_base + p.off_phi + s * phi_slot_bytes + c * tile_bytes, &tm_phi,
-                        bar_pfull + 8 * s, col + c * CHUNK, 0);
+                        bar_afull + 8 * s, col + c * CHUNK, 0);
         }
         ++issued;
       }
+      // drain: the last copies land before the CTA may exit (the issuer waited for them unless
+      // it aborted)
       for (int u = issued - 1; u >= 0 && u >= issued - SLOTS; --u)
-        (void)mbar_wait(bar_pfull + 8 * (u % SLOTS), (uint32_t)(u / SLOTS) & 1u);
+        (void)mbar_wait(bar_afull + 8 * (u % SLOTS), (uint32_t)(u / SLOTS) & 1u);
     }
     __syncwarp();
   } else {
