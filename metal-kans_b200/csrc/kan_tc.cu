@@ -126,6 +126,25 @@ TcPlan tc_plan(const LayerArgs& a) {
     splits = splits > tc::MAX_SPLITS ? tc::MAX_SPLITS : splits;
     while (splits > 1 && (p.BN % (32 * splits)) != 0) --splits;
     splits = splits < 1 ? 1 : splits;
+  } else {
+    // several waves of one-CTA-per-SM tiles: the last wave of tiles * S CTAs on 148 SMs runs
+    // partly empty.  Split K (S = 2 or 4, at least 32 K blocks per split, so the cluster
+    // reduction stays small against the main loop) when that fills the waves better by more
+    // than 2 %: e.g. 512 tiles = 3.46 waves (86 % filled), split in two = 6.92 waves (99 %).
+    auto fill = [&](int S) {
+      const long long ctas = tiles * S;
+      const long long waves = (ctas + 147) / 148;
+      return (double)ctas / (double)(waves * 148);
+    };
+    double best = fill(1);
+    for (int S = 2; S <= tc::MAX_SPLITS; S *= 2) {
+      if (p.BN % (32 * S) != 0 || p.nb / S < 32) continue;
+      const double f = fill(S);
+      if (f > best + 0.02) {
+        best = f;
+        splits = S;
+      }
+    }
   }
   p.splits = splits;
   return p;
