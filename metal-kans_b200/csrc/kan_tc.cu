@@ -160,7 +160,7 @@ cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& p, cudaSt
   CUtensorMap tx = tw;
   const int x_tma = tc::make_tmap_x(&tx, a.X, a.B, a.D_in, mode) ? 1 : 0;
   note_launch();
-  dim3 grid(p.ntiles, p.mtiles, p.splits);
+  dim3 grid(p.mtiles, p.ntiles, p.splits);
   return tc::kDispatch[mode][a.basis](tw, tx, x_tma, a, p.BN, p.nb, p.splits, grid, s);
 }
 

@@ -611,7 +611,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   float* s_stats = reinterpret_cast<float*>(smem + OFF_STATS);  // [4][BM]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // M tiles vary fastest in the grid: the CTAs resident at one time share a few weight panels
+  // (read from HBM about once, then from L2) instead of every panel at once
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int z = blockIdx.z;
   // this split's K blocks: [kb0, kb1)
   const int kb0 = (int)((long long)nb_total * z / splits);
