@@ -38,10 +38,10 @@ for p in (os.path.join(REPO, "metal-kans_b200"), REPO):
 METRIC = "fused KAN layer rows/sec at 1/2/4/8 B200; % tensor-pipe or HBM roofline"
 
 # ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the
-# captures summarised in profiles/ (None when not captured at the config's size):
-#   c2 kan_tc_kernel_c2_fastkan_fp16_b4096.md, c1 kan_simt_kernel_c1_cheby_fp32_b1024.md,
-#   c5:ternary:4096 kan_tc_kernel_c5_ternary_bf16_b4096.md
-TRAFFIC = {"c2": 3377664, "c1": 437504, "c5:ternary:4096": 1469946368 + 32890368}
+# `ncu --set full` captures summarised under profiles/ (one summary per kernel and workload);
+# None when the config was not captured at its own size (c3, c4 are captured on 2048 rows)
+TRAFFIC = {"c2": 3386368, "c1": 453632, "c5:ternary:4096": 699785728 + 33294592,
+           "c5:ternary:16": 53773568 + 152064}
 
 
 def peaks():
