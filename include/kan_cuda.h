@@ -228,6 +228,12 @@ int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* str
 /* Same with an explicit kernel path (tests, benchmarks). */
 int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int path,
                      void* stream);
+/* No counterpart in the reference's device API; replaces the host-pointer convention of the
+ * bridge's forwards (metal_kan_bridge.mm:1890-1971: copy in, compute, copy out, synchronous) for
+ * any kan_layer.  X [B][D_in] and Y [B][D_out] are HOST memory (page-locked for overlap);
+ * returns when Y is written.  Large batches run as two chunks on separate copy and compute
+ * streams, so that transfers overlap the kernels. */
+int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B);
 
 /* GatedKAN block: H = silu(gate(X)) * up(X) (act dtype, [B][D_ffn]); Y = down(H).  H is caller
  * memory ([B][gate.D_out] elements of the act dtype). */

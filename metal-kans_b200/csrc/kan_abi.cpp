@@ -68,7 +68,7 @@ struct PendingCopy {
 // Engine scratch of one stream: packed tensor-core weights (when the caller passes none) and the
 // GatedKAN gate/up activations.  Kept per stream so that work queued on different streams never
 // shares a buffer.
-enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, NUM_SCRATCH };
+enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, SC_HX, SC_HY, NUM_SCRATCH };
 struct Scratch {
   cudaStream_t stream = nullptr;
   void* ptr[NUM_SCRATCH] = {};
@@ -85,6 +85,9 @@ struct DeviceState {
   std::vector<PendingCopy> pending;     // async-mode results waiting for metal_kan_sync()
   std::vector<std::pair<void*, size_t>> pinned_free;  // reusable pinned buffers
   std::vector<Scratch*> scratch;        // one per stream that ran the engine
+  // kan_forward_host: copy streams (host->device, device->host) and per-chunk events
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_in[2] = {}, ev_done[2] = {};
 };
 
 static DeviceState g_dev[MAX_DEVICES];
@@ -385,6 +388,59 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
 
 int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* stream) {
   return kan_forward_path(layer, X, Y, B, KAN_PATH_AUTO, stream);
+}
+
+int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!layer) return fail(KAN_ERR_ARG, "forward_host: NULL layer");
+  if (B < 0) return fail(KAN_ERR_ARG, "forward_host: B < 0");
+  if (B == 0) return KAN_OK;
+  if (!X || !Y) return fail(KAN_ERR_ARG, "forward_host: NULL X or Y");
+  const size_t esz = dtype_size(layer->act_dtype);
+  const size_t xrow = (size_t)layer->D_in * esz, yrow = (size_t)layer->D_out * esz;
+  if (!d->h2d) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!d->h2d) {
+      KAN_CUDA_TRY(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
+      for (int c = 0; c < 2; ++c) {
+        KAN_CUDA_TRY(cudaEventCreateWithFlags(&d->ev_in[c], cudaEventDisableTiming));
+        KAN_CUDA_TRY(cudaEventCreateWithFlags(&d->ev_done[c], cudaEventDisableTiming));
+      }
+      cudaStream_t h;
+      KAN_CUDA_TRY(cudaStreamCreateWithFlags(&h, cudaStreamNonBlocking));
+      d->h2d = h;
+    }
+  }
+  void *dX, *dY;
+  if ((rc = scratch_buf(d, d->stream, SC_HX, (size_t)B * xrow, false, &dX))) return rc;
+  if ((rc = scratch_buf(d, d->stream, SC_HY, (size_t)B * yrow, false, &dY))) return rc;
+  // two chunks (at a 128-row boundary) once the copies are worth overlapping: the second
+  // chunk's input crosses the link while the first computes, the first chunk's result returns
+  // while the second computes
+  const int nc = (B >= 2048 && (size_t)B * (xrow + yrow) >= ((size_t)2 << 20)) ? 2 : 1;
+  const int rows0 = nc == 2 ? (B / 2 + 127) / 128 * 128 : B;
+  for (int c = 0; c < nc; ++c) {
+    const int r0 = c == 0 ? 0 : rows0, rows = c == 0 ? rows0 : B - rows0;
+    const char* xs = (const char*)X + (size_t)r0 * xrow;
+    char* xd = (char*)dX + (size_t)r0 * xrow;
+    char* yd = (char*)dY + (size_t)r0 * yrow;
+    KAN_CUDA_TRY(cudaMemcpyAsync(xd, xs, (size_t)rows * xrow, cudaMemcpyHostToDevice, d->h2d));
+    KAN_CUDA_TRY(cudaEventRecord(d->ev_in[c], d->h2d));
+    KAN_CUDA_TRY(cudaStreamWaitEvent(d->stream, d->ev_in[c], 0));
+    if ((rc = run_forward(layer, xd, yd, rows, KAN_PATH_AUTO, d->stream, d))) {
+      cudaStreamSynchronize(d->h2d);
+      cudaStreamSynchronize(d->stream);
+      return rc;
+    }
+    KAN_CUDA_TRY(cudaEventRecord(d->ev_done[c], d->stream));
+    KAN_CUDA_TRY(cudaStreamWaitEvent(d->d2h, d->ev_done[c], 0));
+    KAN_CUDA_TRY(cudaMemcpyAsync((char*)Y + (size_t)r0 * yrow, yd, (size_t)rows * yrow,
+                                 cudaMemcpyDeviceToHost, d->d2h));
+  }
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->d2h));
+  return check_device_error(d);
 }
 
 int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,

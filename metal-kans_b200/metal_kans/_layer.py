@@ -173,7 +173,14 @@ class KANLayerBase(E.DeviceLayerMixin):
         x2, orig = E.as_activation(x, act, self.in_features)
         B = x2.shape[0]
         y = E.pinned_empty((B, self.out_features), act)
-        if B:
+        if B and not path and not D.async_enabled():
+            # one call: host copies and kernels on the engine's copy and compute streams
+            keep: list = []
+            L = self._descriptor(keep)
+            E.lib().kan_forward_host(ctypes.byref(L), ctypes.c_void_p(x2.ctypes.data),
+                                     ctypes.c_void_p(y.ctypes.data), int(B))
+            self._keepalive = keep
+        elif B:
             s = self._scratch()
             dx = s.get("x", x2.nbytes).upload(x2)
             dy = s.get("y", y.nbytes)

@@ -97,6 +97,7 @@ SIGNATURES = [
     ("benchmark_metal_wavkan", ctypes.c_double, [vp] * 7 + [i32] * 9),
     ("kan_forward", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, vp]),
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
+    ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
     ("kan_gated_forward_noalloc", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
     ("kan_tc_packed_bytes", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(sz)]),

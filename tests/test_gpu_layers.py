@@ -184,3 +184,21 @@ def test_descriptor_cache_follows_parameter_changes(mk):
     l.float()
     y3 = l(x)
     assert y3.dtype == np.float32 and layer_err(y3, l, x, "f32", "rbf") <= TOL["f32"]
+
+
+@pytest.mark.parametrize("case", [("rbf", 256, 256, 8, 3000, "f16"), ("cheby", 256, 512, 9, 2500, "bf16"),
+                                  ("cheby", 64, 64, 9, 4100, "f32")],
+                         ids=lambda c: "-".join(map(str, c)))
+def test_host_forward_chunked(mk, case):
+    """layer(x) runs kan_forward_host: batches this large go as two chunks whose copies overlap the
+    kernels; the result must match the oracle and the one-shot device path."""
+    basis, d_in, d_out, K, B, mode = case
+    layer = set_mode(make_layer(basis, d_in, d_out, K, seed=7), mode)
+    randomize_bias(layer)
+    lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
+    x = np.random.default_rng(B).uniform(lo, hi, (B, d_in)).astype(np.float32)
+    y = layer(x)
+    assert y.shape == (B, d_out)
+    assert layer_err(y, layer, x, mode, basis) <= TOL[mode]
+    y1 = layer.forward(x, path=PATHS["simt"])
+    assert layer_err(y1, layer, x, mode, basis) <= TOL[mode]
