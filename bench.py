@@ -364,12 +364,15 @@ def device_step(mk, obj, layers, B, x_ptr, y_ptr, keep):
 
     if isinstance(obj, GatedKAN):
         descs = [l._descriptor(keep) for l in layers]
+        # gate + up packed as one tensor-core matrix (one launch, SwiGLU in its epilogue)
+        pair = obj._pair(descs[0], descs[1], keep)
         esz = np.dtype(obj.gate_kan.dtype).itemsize
         h = DeviceBuffer(B * obj.d_ffn * esz)
         keep.append(h)
-        args = [ctypes.byref(d) for d in descs] + [ctypes.c_void_p(x_ptr), ctypes.c_void_p(h.ptr),
-                                                   ctypes.c_void_p(y_ptr), B, None]
-        return lambda: lib.kan_gated_forward(*args)
+        args = ([ctypes.byref(d) for d in descs] +
+                [ctypes.c_void_p(pair), ctypes.c_void_p(x_ptr), ctypes.c_void_p(h.ptr),
+                 ctypes.c_void_p(y_ptr), B, None])
+        return lambda: lib.kan_gated_forward_pair(*args)
     esz = np.dtype(layers[0].dtype).itemsize
     width = max(l.out_features for l in layers)
     bufs = [DeviceBuffer(B * width * esz), DeviceBuffer(B * width * esz)]

@@ -240,6 +240,20 @@ int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B);
 int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
                       const void* X, void* H, void* Y, int B, void* stream);
 
+/* No counterpart in the reference (gated_kan.py:112-131 runs gate and up as two layers).  Gate and
+ * up of a GatedKAN read the same input through the same basis; kan_tc_pack_pair() packs both into
+ * one tensor-core matrix (rows interleaved in blocks of 128; kan_tc_pair_bytes() gives its size)
+ * and kan_gated_forward_pair() evaluates the basis once for both, applies SwiGLU in the epilogue
+ * and runs down.  H equals kan_gated_forward's bit for bit where that one's gate and up launches
+ * do not split K (otherwise the fp32 sums are ordered differently).  Needs two f16/bf16 Chebyshev layers
+ * of one shape, K, base branch and input map; otherwise, for grids under 120 tiles, or with a
+ * NULL pair, it runs kan_gated_forward(). */
+int kan_tc_pair_bytes(const kan_layer* gate, const kan_layer* up, size_t* bytes);
+int kan_tc_pack_pair(const kan_layer* gate, const kan_layer* up, void* out, void* stream);
+int kan_gated_forward_pair(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
+                           const void* pair, const void* X, void* H, void* Y, int B,
+                           void* stream);
+
 /* No counterpart in the reference.  kan_gated_forward() for callers that cannot allocate device
  * memory (allocation forbidden after start-up by a memory arena or a serving runtime, or a
  * cudaMalloc that would synchronise or fail at that point): the gate and up activations live in

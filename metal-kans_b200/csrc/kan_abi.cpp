@@ -443,6 +443,40 @@ int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {
   return check_device_error(d);
 }
 
+// Gate and up of a GatedKAN share their input and their basis (Chebyshev, same K, base branch and
+// input map): one launch can evaluate the basis once for both.
+static bool pair_compatible(const kan_layer* g, const kan_layer* u) {
+  return g && u && g->basis == KAN_CHEBY && u->basis == KAN_CHEBY &&
+         (g->act_dtype == KAN_F16 || g->act_dtype == KAN_BF16) && g->act_dtype == u->act_dtype &&
+         g->K == u->K && g->D_in == u->D_in && g->D_out == u->D_out &&
+         (g->has_base != 0) == (u->has_base != 0) && g->input_map == u->input_map;
+}
+
+int kan_tc_pair_bytes(const kan_layer* gate, const kan_layer* up, size_t* bytes) {
+  if (!bytes) return fail(KAN_ERR_ARG, "pair_bytes: NULL output");
+  if (!pair_compatible(gate, up))
+    return fail(KAN_ERR_UNSUPPORTED, "gate/up pair: needs two f16/bf16 Chebyshev layers of one "
+                                     "shape, K, base branch and input map");
+  const TcBlocking bl = tc_blocking(gate->D_in, gate->K, gate->has_base);
+  *bytes = (size_t)pair_rows(gate->D_out) * bl.NB * 64 * 2;
+  return KAN_OK;
+}
+
+int kan_tc_pack_pair(const kan_layer* gate, const kan_layer* up, void* out, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  size_t bytes;
+  if ((rc = kan_tc_pair_bytes(gate, up, &bytes))) return rc;
+  if (!out) return fail(KAN_ERR_ARG, "pack_pair: NULL output");
+  LayerArgs ag, au;
+  if ((rc = make_args(gate, nullptr, nullptr, 0, d, &ag))) return rc;
+  if ((rc = make_args(up, nullptr, nullptr, 0, d, &au))) return rc;
+  cudaError_t e = launch_tc_pack_pair(ag, au, gate->act_dtype, out, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "pair pack: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
 int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
                       const void* X, void* H, void* Y, int B, void* stream) {
   DeviceState* d;
@@ -462,6 +496,37 @@ int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_laye
   if ((rc = run_forward(up, X, u, B, KAN_PATH_AUTO, s, d))) return rc;
   cudaError_t e = launch_swiglu(g, u, H, (long long)n, gate->act_dtype, s);
   if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu launch: %s", cudaGetErrorString(e));
+  return run_forward(down, H, Y, B, KAN_PATH_AUTO, s, d);
+}
+
+int kan_gated_forward_pair(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
+                           const void* pair, const void* X, void* H, void* Y, int B,
+                           void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!gate || !up || !down || !H) return fail(KAN_ERR_ARG, "gated: NULL argument");
+  if (!pair || !pair_compatible(gate, up) || down->D_in != gate->D_out ||
+      down->act_dtype != gate->act_dtype)
+    return kan_gated_forward(gate, up, down, X, H, Y, B, stream);
+  cudaStream_t s = pick_stream(stream, d);
+  LayerArgs a, au;
+  if ((rc = make_args(gate, X, H, B, d, &a))) return rc;
+  if ((rc = make_args(up, X, H, B, d, &au))) return rc;
+  if (B == 0) return KAN_OK;
+  a.D_out = pair_rows(gate->D_out);
+  a.tc_weights = pair;
+  a.fuse_swiglu = 1;
+  a.h_cols = gate->D_out;
+  a.bias2 = au.bias;
+  a.has_bias2 = au.has_bias;
+  TcPlan p = tc_plan(a);
+  // the fused epilogue finishes whole tiles (no split-K); small grids take the separate launches
+  if (!tc_supported(a, gate->act_dtype) || p.BN != 256 || (long long)p.mtiles * p.ntiles < 120)
+    return kan_gated_forward(gate, up, down, X, H, Y, B, stream);
+  p.splits = 1;
+  cudaError_t e = launch_tc(a, gate->act_dtype, p, s);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
   return run_forward(down, H, Y, B, KAN_PATH_AUTO, s, d);
 }
 

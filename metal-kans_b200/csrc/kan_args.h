@@ -25,7 +25,20 @@ struct LayerArgs {
   kan_weight w, wb;
   int* err;  // device error word (set when a bounded wait expires)
   const void* tc_weights;  // tensor-core layout weights (kan_tc_pack), act dtype
+  // GatedKAN gate + up in one launch (tensor-core path only): tc_weights holds the two layers'
+  // rows interleaved in blocks of 128 (kan_tc_pack_pair), D_out counts those rows, and the
+  // epilogue writes Y = silu(gate) * up, [B][h_cols]; bias / has_bias belong to gate, bias2 /
+  // has_bias2 to up
+  int fuse_swiglu, h_cols, has_bias2;
+  const void* bias2;
 };
+
+// Rows of a gate/up pair in the interleaved tensor-core layout: per 128 output columns, 128
+// gate rows then 128 up rows.
+constexpr int PAIR_BLOCK = 128;
+KAN_HD inline int pair_rows(int d_ffn) {
+  return (d_ffn + PAIR_BLOCK - 1) / PAIR_BLOCK * 2 * PAIR_BLOCK;
+}
 
 // Feature blocking of the tensor-core weight layout: F whole features of KT terms per 64-column
 // block (KT = K + has_base: the K basis terms, then the base-branch weight).

@@ -29,6 +29,10 @@ bool tc_supported(const LayerArgs& a, int act_dtype);
 TcPlan tc_plan(const LayerArgs& a);
 cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& plan, cudaStream_t s);
 cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s);
+// GatedKAN gate/up pair: both layers packed into one [pair_rows(D_out)][NB*64] matrix, rows
+// interleaved in blocks of PAIR_BLOCK (the layout a.fuse_swiglu launches read).
+cudaError_t launch_tc_pack_pair(const LayerArgs& gate, const LayerArgs& up, int act_dtype,
+                                void* out, cudaStream_t s);
 // kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
 // from the packed codes into TMEM; no dense copy)
 // launch_gemv also runs the basis pre-pass into `phi` (gemv_phi_bytes() of device scratch).

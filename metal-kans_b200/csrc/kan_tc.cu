@@ -17,8 +17,11 @@ constexpr int MAX_SPLITS = 4;  // split-K cluster size (reduction slots sized fo
 // Pack W (basis terms) and Wb (base weights) into Wp[D_out][NB*64]: block b, column j holds term
 // t = j % KT of feature i = b*F + j/KT (t < K: W[o, i*K + t]; t == K: Wb[o, i]); zero elsewhere.
 // Packed formats are decoded to their exact fp32 value, then rounded to the act dtype.
+// part >= 0: the layer is half of a gate/up pair and its row o goes to row
+// (o / PAIR_BLOCK) * 2 * PAIR_BLOCK + part * PAIR_BLOCK + o % PAIR_BLOCK of `out`.
 template <int MODE>
-__global__ void pack_kernel(LayerArgs a, typename Act<MODE>::T* out, int KT, int F, int NB) {
+__global__ void pack_kernel(LayerArgs a, typename Act<MODE>::T* out, int KT, int F, int NB,
+                            int part) {
   const long long cols = (long long)NB * BK;
   const long long total = cols * a.D_out;
   const int Kdim = a.D_in * a.K;
@@ -34,7 +37,10 @@ __global__ void pack_kernel(LayerArgs a, typename Act<MODE>::T* out, int KT, int
       v = (t < a.K) ? weight_value<MODE>(a.w, o, i * a.K + t, Kdim)
                     : weight_value<MODE>(a.wb, o, i, a.D_in);
     }
-    out[e] = Act<MODE>::from_f(v);
+    const long long orow = part < 0 ? o
+                                    : (long long)(o / PAIR_BLOCK) * 2 * PAIR_BLOCK +
+                                          part * PAIR_BLOCK + o % PAIR_BLOCK;
+    out[orow * cols + c] = Act<MODE>::from_f(v);
   }
 }
 
@@ -164,7 +170,8 @@ cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& p, cudaSt
   return tc::kDispatch[mode][a.basis](tw, tx, x_tma, a, p.BN, p.nb, p.splits, grid, s);
 }
 
-cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s) {
+static cudaError_t pack_part(const LayerArgs& a, int act_dtype, void* out, int part,
+                             cudaStream_t s) {
   const TcBlocking bl = tc_blocking(a.D_in, a.K, a.has_base);
   if (bl.F <= 0) return cudaErrorInvalidValue;
   note_launch();
@@ -173,11 +180,26 @@ cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStr
   if (blocks > 148LL * 16) blocks = 148LL * 16;
   if (blocks < 1) blocks = 1;
   if (act_dtype == KAN_F16)
-    tc::pack_kernel<MODE_F16><<<(int)blocks, 256, 0, s>>>(a, (__half*)out, bl.KT, bl.F, bl.NB);
+    tc::pack_kernel<MODE_F16><<<(int)blocks, 256, 0, s>>>(a, (__half*)out, bl.KT, bl.F, bl.NB,
+                                                         part);
   else
     tc::pack_kernel<MODE_BF16><<<(int)blocks, 256, 0, s>>>(a, (__nv_bfloat16*)out, bl.KT, bl.F,
-                                                          bl.NB);
+                                                          bl.NB, part);
   return cudaGetLastError();
+}
+
+cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStream_t s) {
+  return pack_part(a, act_dtype, out, -1, s);
+}
+
+cudaError_t launch_tc_pack_pair(const LayerArgs& gate, const LayerArgs& up, int act_dtype,
+                                void* out, cudaStream_t s) {
+  const TcBlocking bl = tc_blocking(gate.D_in, gate.K, gate.has_base);
+  // rows past D_out in either half stay zero
+  cudaError_t e = cudaMemsetAsync(out, 0, (size_t)pair_rows(gate.D_out) * bl.NB * tc::BK * 2, s);
+  if (e != cudaSuccess) return e;
+  if ((e = pack_part(gate, act_dtype, out, 0, s)) != cudaSuccess) return e;
+  return pack_part(up, act_dtype, out, 1, s);
 }
 
 }  // namespace kan

@@ -783,7 +783,57 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     };
 
-    if (splits == 1) {
+    if (splits == 1 && a.fuse_swiglu) {
+      // gate + up pair (BN = 256): tile columns [0, 128) are gate rows, [128, 256) up rows of
+      // the same 128 outputs; group h finishes outputs [64 h, 64 h + 64).  Each layer's output
+      // is rounded to the act dtype (bias first), then silu(gate) * up with the SiLU argument
+      // clamped to +-20, as a separate SwiGLU pass over the two stored outputs computes it.
+      if (!aborted) {
+        const int QUART = BN >> 2;
+        T* Hout = (T*)a.Y;
+        const T* bg = (const T*)a.bias;
+        const T* bu = (const T*)a.bias2;
+        const int hbase = n0 >> 1;  // first output column of this tile
+        const bool hvec = (a.h_cols % 8) == 0;
+#pragma unroll 1
+        for (int cc = 0; cc < QUART; cc += 32) {
+          const int oc = h * QUART + cc;
+          uint32_t ag[32], au[32];
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)oc, ag);
+          tmem_ld32(tmem_d + ((uint32_t)(q * 32) << 16) + (uint32_t)(HALF + oc), au);
+          const int col0 = hbase + oc;
+          if (!valid || col0 >= a.h_cols) continue;
+          float out[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int col = col0 + jj;
+            const bool in = col < a.h_cols;
+            const float g = Act<MODE>::round(__uint_as_float(ag[jj]) +
+                                             ((a.has_bias && in) ? Act<MODE>::to_f(bg[col]) : 0.f));
+            const float u = Act<MODE>::round(__uint_as_float(au[jj]) +
+                                             ((a.has_bias2 && in) ? Act<MODE>::to_f(bu[col]) : 0.f));
+            const float sig = 1.0f / (1.0f + expf(-fminf(fmaxf(g, -20.0f), 20.0f)));
+            out[jj] = (g * sig) * u;
+          }
+          T* hrow = Hout + (size_t)row * a.h_cols;
+          if (hvec && col0 + 32 <= a.h_cols) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              uint4 pk;
+              pk.x = pack2<MODE>(out[8 * jj + 0], out[8 * jj + 1]);
+              pk.y = pack2<MODE>(out[8 * jj + 2], out[8 * jj + 3]);
+              pk.z = pack2<MODE>(out[8 * jj + 4], out[8 * jj + 5]);
+              pk.w = pack2<MODE>(out[8 * jj + 6], out[8 * jj + 7]);
+              *reinterpret_cast<uint4*>(hrow + col0 + 8 * jj) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+              if (col0 + jj < a.h_cols) hrow[col0 + jj] = Act<MODE>::from_f(out[jj]);
+          }
+        }
+      }
+    } else if (splits == 1) {
       if (!aborted) {
 #pragma unroll 1
         for (int cc = 0; cc < HALF; cc += 32) {

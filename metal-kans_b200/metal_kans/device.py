@@ -99,6 +99,10 @@ SIGNATURES = [
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
     ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
+    ("kan_gated_forward_pair", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, vp, i32, vp]),
+    ("kan_tc_pair_bytes", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(KanLayer),
+                                ctypes.POINTER(ctypes.c_size_t)]),
+    ("kan_tc_pack_pair", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(KanLayer), vp, vp]),
     ("kan_gated_forward_noalloc", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
     ("kan_tc_packed_bytes", i32, [ctypes.POINTER(KanLayer), ctypes.POINTER(sz)]),
     ("kan_tc_pack", i32, [ctypes.POINTER(KanLayer), vp, vp]),

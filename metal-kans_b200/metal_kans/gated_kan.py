@@ -14,6 +14,7 @@ from typing import Optional
 import numpy as np
 
 from . import _engine as E
+from . import device as D
 from .cheby_kan import ChebyKAN
 from .quantization import to_int2, to_int4, to_int8, to_ternary
 
@@ -63,12 +64,43 @@ class GatedKAN:
         self.dtype = E.BFLOAT16
         return self
 
+    def _pair(self, gate_desc, up_desc, keep: list) -> int:
+        """Gate and up packed as one tensor-core matrix (built once per weight version of either
+        layer); 0 when the two layers cannot share a launch (the block then runs them apart)."""
+        if gate_desc.act_dtype == D.KAN_F32:
+            return 0
+        key = (self.gate_kan.__dict__.get("_tc_cache", (None,))[0],
+               self.up_kan.__dict__.get("_tc_cache", (None,))[0])
+        hit = self.__dict__.get("_pair_cache")
+        if hit is None or hit[0] != key:
+            lib = E.lib()
+            n = ctypes.c_size_t(0)
+            try:
+                lib.kan_tc_pair_bytes(ctypes.byref(gate_desc), ctypes.byref(up_desc),
+                                      ctypes.byref(n))
+            except D.KanError:
+                self._pair_cache = (key, None)
+                return 0
+            buf = E.DeviceBuffer(n.value)
+            lib.kan_tc_pack_pair(ctypes.byref(gate_desc), ctypes.byref(up_desc),
+                                 ctypes.c_void_p(buf.ptr), None)
+            hit = (key, buf)
+            self._pair_cache = hit
+        if hit[1] is None:
+            return 0
+        keep.append(hit[1])
+        return hit[1].ptr
+
     def forward_device(self, x_ptr: int, h_ptr: int, y_ptr: int, B: int, stream=None) -> None:
-        """Enqueue the block on device buffers: x [B, d_model] -> hidden [B, d_ffn] -> y."""
+        """Enqueue the block on device buffers: x [B, d_model] -> hidden [B, d_ffn] -> y.  Gate and
+        up run as one tensor-core launch (shared basis tiles, SwiGLU in the epilogue) when the
+        batch fills the GPU; H is the same either way."""
         keep: list = []
         descs = [l._descriptor(keep) for l in self._layers()]
-        E.lib().kan_gated_forward(*(ctypes.byref(d) for d in descs), ctypes.c_void_p(x_ptr),
-                                  ctypes.c_void_p(h_ptr), ctypes.c_void_p(y_ptr), int(B), stream)
+        pair = self._pair(descs[0], descs[1], keep)
+        E.lib().kan_gated_forward_pair(*(ctypes.byref(d) for d in descs), ctypes.c_void_p(pair),
+                                       ctypes.c_void_p(x_ptr), ctypes.c_void_p(h_ptr),
+                                       ctypes.c_void_p(y_ptr), int(B), stream)
         self._keepalive = keep
 
     def forward(self, x: np.ndarray) -> np.ndarray:

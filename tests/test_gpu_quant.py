@@ -159,3 +159,58 @@ def test_gated_int4_golden(mk):
             np.testing.assert_array_equal(getattr(l, attr), r[f"{nm}.{attr}.deq"])
     y = blk(r["x"])
     assert O.max_rel_err(y, r["y"]) <= 1e-5
+
+
+@pytest.mark.parametrize("case", [(256, 640, 4096, "bf16", False, "int4"),
+                                  (256, 600, 4200, "f16", True, None),
+                                  (128, 384, 5120, "bf16", True, "ternary")],
+                         ids=lambda c: "-".join(map(str, c)))
+def test_gated_pair_matches_separate_launches(mk, case):
+    """Gate and up in one tensor-core launch (shared basis tiles, SwiGLU in the epilogue) give the
+    same hidden activations and output, bit for bit, as the separate gate, up and SwiGLU
+    launches (at these shapes the separate launches do not split K either, so every output sums
+    its K blocks in the same order); the block output agrees with the oracle."""
+    from metal_kans._engine import DeviceBuffer
+
+    d_model, d_ffn, B, mode, bias, quant = case
+    np.random.seed(11)
+    blk = mk.GatedKAN(d_model=d_model, d_ffn=d_ffn, degree=4, has_bias=bias)
+    if bias:
+        rng = np.random.default_rng(5)
+        for l in blk._layers():
+            l.bias = rng.normal(0, 0.1, l.out_features).astype(np.float32)
+    if quant == "int4":
+        blk.to_int4(group_size=64)
+    elif quant == "ternary":
+        blk.to_ternary(group_size=64)
+    blk.bfloat16() if mode == "bf16" else blk.half()
+    act = blk.gate_kan.dtype
+    x = np.random.default_rng(B).normal(0, 1, (B, d_model)).astype(np.float32).astype(act)
+    lib = mk.get_metal_bridge()
+    keep = []
+    descs = [l._descriptor(keep) for l in blk._layers()]
+    pair = blk._pair(descs[0], descs[1], keep)
+    assert pair, "pair packing refused a compatible gate/up"
+    dx = DeviceBuffer.from_array(x)
+    outs = []
+    for p in (pair, 0):  # one launch for gate + up, then the separate launches
+        dh = DeviceBuffer(B * d_ffn * 2)
+        dy = DeviceBuffer(B * d_model * 2)
+        lib.kan_gated_forward_pair(*(ctypes.byref(d) for d in descs), ctypes.c_void_p(p),
+                                   ctypes.c_void_p(dx.ptr), ctypes.c_void_p(dh.ptr),
+                                   ctypes.c_void_p(dy.ptr), B, None)
+        h = dh.download(np.empty((B, d_ffn), act))
+        y = dy.download(np.empty((B, d_model), act))
+        lib.kan_stream_synchronize(None)
+        outs.append((h.view(np.uint16).copy(), y.view(np.uint16).copy()))
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(outs[0][1], outs[1][1])
+    # the public forward takes the fused launch; oracle of the block: each layer rounded to the
+    # act dtype, SwiGLU rounded, down projection unrounded
+    y = blk(x)
+    xf = x.astype(np.float32)
+    g = oracle_for_layer(blk.gate_kan, xf, mode, "cheby")
+    u = oracle_for_layer(blk.up_kan, xf, mode, "cheby")
+    hid = O.swiglu(g, u).astype(np.float32).astype(act).astype(np.float32)
+    ref = oracle_for_layer(blk.down_kan, hid, mode, "cheby", out_round=False)
+    assert O.max_rel_err_rounded(y.astype(np.float64), ref, mode) <= TOL[mode]
