@@ -242,7 +242,7 @@ int kan_gated_forward(const kan_layer* gate, const kan_layer* up, const kan_laye
 
 /* No counterpart in the reference (gated_kan.py:112-131 runs gate and up as two layers).  Gate and
  * up of a GatedKAN read the same input through the same basis; kan_tc_pack_pair() packs both into
- * one tensor-core matrix (rows interleaved in blocks of 128; kan_tc_pair_bytes() gives its size)
+ * one tensor-core matrix (rows interleaved in blocks of 256; kan_tc_pair_bytes() gives its size)
  * and kan_gated_forward_pair() evaluates the basis once for both, applies SwiGLU in the epilogue
  * and runs down.  H equals kan_gated_forward's bit for bit where that one's gate and up launches
  * do not split K (otherwise the fp32 sums are ordered differently).  Needs two f16/bf16 Chebyshev layers

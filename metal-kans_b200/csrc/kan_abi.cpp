@@ -521,10 +521,9 @@ int kan_gated_forward_pair(const kan_layer* gate, const kan_layer* up, const kan
   a.bias2 = au.bias;
   a.has_bias2 = au.has_bias;
   TcPlan p = tc_plan(a);
-  // the fused epilogue finishes whole tiles (no split-K); small grids take the separate launches
-  if (!tc_supported(a, gate->act_dtype) || p.BN != 256 || (long long)p.mtiles * p.ntiles < 120)
+  // the fused epilogue needs wide, unsplit tiles; smaller grids take the separate launches
+  if (!tc_supported(a, gate->act_dtype) || p.BN != 2 * PAIR_BLOCK || p.splits != 1)
     return kan_gated_forward(gate, up, down, X, H, Y, B, stream);
-  p.splits = 1;
   cudaError_t e = launch_tc(a, gate->act_dtype, p, s);
   if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
   return run_forward(down, H, Y, B, KAN_PATH_AUTO, s, d);

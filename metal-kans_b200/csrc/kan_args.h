@@ -33,9 +33,9 @@ struct LayerArgs {
   const void* bias2;
 };
 
-// Rows of a gate/up pair in the interleaved tensor-core layout: per 128 output columns, 128
-// gate rows then 128 up rows.
-constexpr int PAIR_BLOCK = 128;
+// Rows of a gate/up pair in the interleaved tensor-core layout: per 256 output columns, 256
+// gate rows then 256 up rows (one wide tile of the tensor-core kernel).
+constexpr int PAIR_BLOCK = 256;
 KAN_HD inline int pair_rows(int d_ffn) {
   return (d_ffn + PAIR_BLOCK - 1) / PAIR_BLOCK * 2 * PAIR_BLOCK;
 }

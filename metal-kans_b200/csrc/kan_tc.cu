@@ -120,6 +120,18 @@ TcPlan tc_plan(const LayerArgs& a) {
   const TcBlocking bl = tc_blocking(a.D_in, a.K, a.has_base);
   p.nb = bl.NB;
   p.mtiles = (a.B + tc::BM - 1) / tc::BM;
+  // wide tiles (two N = 256 accumulators per basis block) halve the basis work per output; taken
+  // when the grid of wide tiles still fills the GPU (no split-K for them), never for the staged
+  // LayerNorm input
+  if (a.D_out >= 512 && a.input_map != KAN_MAP_LAYERNORM) {
+    const long long wide_tiles = (long long)p.mtiles * ((a.D_out + 511) / 512);
+    if (wide_tiles >= 120) {
+      p.BN = 512;
+      p.ntiles = (a.D_out + 511) / 512;
+      p.splits = 1;
+      return p;
+    }
+  }
   p.ntiles = (a.D_out + p.BN - 1) / p.BN;
   const long long tiles = (long long)p.mtiles * p.ntiles;
   int splits = 1;
@@ -160,7 +172,8 @@ cudaError_t launch_tc(const LayerArgs& a, int act_dtype, const TcPlan& p, cudaSt
   if (!tc_supported(a, act_dtype) || !a.tc_weights) return cudaErrorNotSupported;
   const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;
   CUtensorMap tw;
-  if (!tc::make_tmap(&tw, a.tc_weights, a.D_out, (long long)p.nb * tc::BK, p.BN, mode))
+  if (!tc::make_tmap(&tw, a.tc_weights, a.D_out, (long long)p.nb * tc::BK, p.BN > 256 ? 256 : p.BN,
+                     mode))
     return cudaErrorInvalidValue;
   // the input in 64-feature x 128-row tiles for the producers (rows of 16-byte multiples only)
   CUtensorMap tx = tw;

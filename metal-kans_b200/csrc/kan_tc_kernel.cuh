@@ -78,6 +78,30 @@ static_assert(red_bytes(4, 64) <= OFF_BAR && red_bytes(2, 128) <= OFF_BAR,
 // LayerNorm input tile (rows of <= 256 features) staged over the A stages before the first block
 static_assert(BM * 256 * 2 <= STAGES * A_STAGE_BYTES, "x tile must fit in the A stages");
 
+// Shared-memory layout of one kernel variant.  WIDE (BN = 512): two N = 256 accumulators (all 512
+// TMEM columns) take every basis block, so each block the producers build feeds twice the MMA
+// work; its 64 KB weight stages leave room for 3 A and 2 input stages, no split-K slots and no
+// staged LayerNorm tile.
+template <bool WIDE>
+struct Layout {
+  static constexpr int kStages = WIDE ? 3 : STAGES;
+  static constexpr int kBStages = WIDE ? 2 : BSTAGES;
+  static constexpr int kXStages = WIDE ? 2 : XSTAGES;
+  static constexpr int kBStageBytes = WIDE ? 2 * B_STAGE_BYTES : B_STAGE_BYTES;
+  static constexpr uint32_t kTmemCols = WIDE ? 512u : TMEM_COLS;
+  static constexpr int kOffB = OFF_A + kStages * A_STAGE_BYTES;
+  static constexpr int kOffX = kOffB + kBStages * kBStageBytes;
+  static constexpr int kOffBar = kOffX + kXStages * X_STAGE_BYTES;
+  static constexpr int kNumBars = 2 * kStages + 2 * kBStages + 2 * kXStages + 3;
+  static constexpr int kOffTmem = kOffBar + kNumBars * 8;
+  static constexpr int kOffFlag = kOffTmem + 4;
+  static constexpr int kOffEpi = kOffFlag + 4;
+  static constexpr int kOffStats = (kOffEpi + 4 + 15) / 16 * 16;
+  static constexpr int kSmemAlloc = kOffStats + 4 * BM * 4 + 1024;
+};
+static_assert(Layout<false>::kSmemAlloc == SMEM_ALLOC, "narrow layout unchanged");
+static_assert(Layout<true>::kSmemAlloc <= 227 * 1024, "wide layout fits the shared memory");
+
 // ---------------------------------------------------------------------------------------------
 // PTX wrappers
 // ---------------------------------------------------------------------------------------------
@@ -379,7 +403,7 @@ __device__ __forceinline__ uint32_t half_bits(const uint4 (&ch)[N], int e) {
 // Features lo .. lo + F - 1 of row r.  Inside one tile: the 16-byte chunks covering them (one
 // 16-byte load each, conflict-free across the warp thanks to the swizzle), the features picked
 // out in registers; a block that straddles two tiles reads its features one by one.
-template <int MODE, int F>
+template <int MODE, int F, int XSTAGES>
 __device__ __forceinline__ void read_x_block(const uint8_t* xring, int lo, int xs_first, int r,
                                              float (&xs)[F]) {
   using T = typename Act<MODE>::T;
@@ -587,12 +611,20 @@ struct RowProducerAnyK {
 // ---------------------------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------------------------
-template <int BASIS, int MODE, class Producer>
+template <int BASIS, int MODE, class Producer, bool WIDE>
 __global__ void __launch_bounds__(THREADS, 1)
     kan_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_x, LayerArgs a, int BN, int nb_total,
                   int splits, int x_tma) {
   using T = typename Act<MODE>::T;
+  // this variant's layout (the names shadow the narrow defaults)
+  using LY = Layout<WIDE>;
+  constexpr int STAGES = LY::kStages, BSTAGES = LY::kBStages, XSTAGES = LY::kXStages;
+  constexpr int B_STAGE_BYTES = LY::kBStageBytes;
+  constexpr uint32_t TMEM_COLS = LY::kTmemCols;
+  constexpr int OFF_B = LY::kOffB, OFF_X = LY::kOffX, OFF_BAR = LY::kOffBar;
+  constexpr int OFF_TMEM = LY::kOffTmem, OFF_FLAG = LY::kOffFlag, OFF_EPI = LY::kOffEpi;
+  constexpr int OFF_STATS = LY::kOffStats;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const uint32_t s_base = smem_u32(smem);
@@ -619,7 +651,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int kb0 = (int)((long long)nb_total * z / splits);
   const int kb1 = (int)((long long)nb_total * (z + 1) / splits);
   const int nj = kb1 - kb0;
-  const bool ln_staged = a.input_map == KAN_MAP_LAYERNORM && ln_smem_ok(a);
+  const bool ln_staged = !WIDE && a.input_map == KAN_MAP_LAYERNORM && ln_smem_ok(a);
   const int rows_valid = min(BM, a.B - m0);
   const int slice = BN / splits;  // split-K: columns of the tile this CTA finishes
 
@@ -725,7 +757,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        read_x_block<MODE, Producer::F>(smem + OFF_X, lo, xs_first, r, xs);
+        read_x_block<MODE, Producer::F, XSTAGES>(smem + OFF_X, lo, xs_first, r, xs);
       } else {
 #pragma unroll
         for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
@@ -784,8 +816,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     };
 
     if (splits == 1 && a.fuse_swiglu) {
-      // gate + up pair (BN = 256): tile columns [0, 128) are gate rows, [128, 256) up rows of
-      // the same 128 outputs; group h finishes outputs [64 h, 64 h + 64).  Each layer's output
+      // gate + up pair (wide tile, BN = 512): tile columns [0, 256) are gate rows, [256, 512) up
+      // rows of the same 256 outputs; group h finishes outputs [128 h, 128 h + 128).  Each layer's output
       // is rounded to the act dtype (bias first), then silu(gate) * up with the SiLU argument
       // clamped to +-20, as a separate SwiGLU pass over the two stored outputs computes it.
       if (!aborted) {
@@ -867,6 +899,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_arrive_expect_tx(bar_full_b + 8 * s, bytes);
         tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES, &tmap_w, bar_full_b + 8 * s,
                     (kb0 + j) * BK, n0);
+        // the second 256 weight rows of a wide tile (a box is at most 256 rows)
+        if (WIDE)
+          tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES + 256 * BK * 2, &tmap_w,
+                      bar_full_b + 8 * s, (kb0 + j) * BK, n0 + 256);
         ++issued;
       }
       // drain: wait (bounded) for the copies still landing in shared memory
@@ -877,7 +913,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, BN, BM);
+      const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, WIDE ? 256 : BN, BM);
       for (int j = 0; j < nj; ++j) {
         const int s = j % STAGES, sb = j % BSTAGES;
         const uint32_t par = (uint32_t)(j / STAGES) & 1u;
@@ -895,9 +931,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t a_addr = s_base + OFF_A + s * A_STAGE_BYTES;
         const uint32_t b_addr = s_base + OFF_B + sb * B_STAGE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
+        for (int kk = 0; kk < BK / 16; ++kk) {
           mma_f16(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
                   idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          // wide tile: the same basis block against weight rows 256..511, columns 256..511
+          if (WIDE)
+            mma_f16(tmem_d + 256u, smem_desc_sw128(a_addr + kk * 32),
+                    smem_desc_sw128(b_addr + 256 * BK * 2 + kk * 32), idesc,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        }
         mma_commit(bar_empty + 8 * s);
         mma_commit(bar_empty_b + 8 * sb);
       }
@@ -1066,22 +1108,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-template <int BASIS, int MODE, class Producer>
+template <int BASIS, int MODE, class Producer, bool WIDE>
 static cudaError_t launch_kernel(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
                                  const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
                                  cudaStream_t s) {
-  auto kern = kan_tc_kernel<BASIS, MODE, Producer>;
+  auto kern = kan_tc_kernel<BASIS, MODE, Producer, WIDE>;
+  constexpr int smem = Layout<WIDE>::kSmemAlloc;
   static bool configured = false;  // one per template instance
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_ALLOC);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_ALLOC;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1094,6 +1136,18 @@ static cudaError_t launch_kernel(const CUtensorMap& tw, const CUtensorMap& tx, i
   return cudaLaunchKernelEx(&cfg, kern, tw, tx, a, BN, nb, splits, use_x);
 }
 
+// BN = 512 runs the wide variant (never split: the plan only picks it for grids of >= 120 tiles)
+template <int BASIS, int MODE, class Producer>
+static cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
+                             const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
+                             cudaStream_t s) {
+  if (BN == 512) {
+    if (splits != 1) return cudaErrorInvalidValue;
+    return launch_kernel<BASIS, MODE, Producer, true>(tw, tx, x_tma, a, BN, nb, splits, grid, s);
+  }
+  return launch_kernel<BASIS, MODE, Producer, false>(tw, tx, x_tma, a, BN, nb, splits, grid, s);
+}
+
 // Compile-time-K producers for the shapes the BASELINE configs and common layers use; any other
 // K runs the runtime-K producer.
 template <int BASIS, int MODE>
@@ -1102,8 +1156,8 @@ static cudaError_t dispatch_k(const CUtensorMap& tw, const CUtensorMap& tx, int 
                               cudaStream_t s) {
 #define KAN_TC_CASE(KK, HBV)                                                              \
   if (a.K == KK && (a.has_base != 0) == HBV)                                              \
-    return launch_kernel<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, tx, x_tma, a, BN, \
-                                                                         nb, splits, grid, s);
+    return launch_bn<BASIS, MODE, RowProducer<BASIS, MODE, KK, HBV>>(tw, tx, x_tma, a, BN, nb,  \
+                                                                     splits, grid, s);
   if (BASIS == KAN_CHEBY) {
     KAN_TC_CASE(4, true) KAN_TC_CASE(4, false) KAN_TC_CASE(5, true) KAN_TC_CASE(5, false)
     KAN_TC_CASE(8, true) KAN_TC_CASE(8, false) KAN_TC_CASE(9, true) KAN_TC_CASE(9, false)
@@ -1115,8 +1169,8 @@ static cudaError_t dispatch_k(const CUtensorMap& tw, const CUtensorMap& tx, int 
     KAN_TC_CASE(6, true) KAN_TC_CASE(6, false) KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   }
 #undef KAN_TC_CASE
-  return launch_kernel<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, tx, x_tma, a, BN, nb, splits,
-                                                                   grid, s);
+  return launch_bn<BASIS, MODE, RowProducerAnyK<BASIS, MODE>>(tw, tx, x_tma, a, BN, nb, splits,
+                                                               grid, s);
 }
 
 }  // namespace tc

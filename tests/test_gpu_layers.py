@@ -202,3 +202,18 @@ def test_host_forward_chunked(mk, case):
     assert layer_err(y, layer, x, mode, basis) <= TOL[mode]
     y1 = layer.forward(x, path=PATHS["simt"])
     assert layer_err(y1, layer, x, mode, basis) <= TOL[mode]
+
+
+@pytest.mark.parametrize("case", [("cheby", 64, 1024, 9, 7680, "bf16"), ("rbf", 128, 640, 8, 7700, "f16"),
+                                  ("cheby", 96, 520, 5, 15400, "f16")],
+                         ids=lambda c: "-".join(map(str, c)))
+def test_wide_tiles(mk, case):
+    """Grids of >= 120 tiles of 512 outputs run the wide tensor-core variant (two N = 256
+    accumulators per basis block): ragged rows and ragged output tiles included."""
+    basis, d_in, d_out, K, B, mode = case
+    layer = set_mode(make_layer(basis, d_in, d_out, K, seed=5), mode)
+    randomize_bias(layer)
+    lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
+    x = np.random.default_rng(B).uniform(lo, hi, (B, d_in)).astype(np.float32)
+    y = layer.forward(x, path=PATHS["tc"])
+    assert layer_err(y, layer, x, mode, basis) <= TOL[mode]

@@ -161,15 +161,16 @@ def test_gated_int4_golden(mk):
     assert O.max_rel_err(y, r["y"]) <= 1e-5
 
 
-@pytest.mark.parametrize("case", [(256, 640, 4096, "bf16", False, "int4"),
-                                  (256, 600, 4200, "f16", True, None),
-                                  (128, 384, 5120, "bf16", True, "ternary")],
+@pytest.mark.parametrize("case", [(256, 640, 5120, "bf16", False, "int4"),
+                                  (256, 600, 5200, "f16", True, None),
+                                  (128, 384, 7680, "bf16", True, "ternary")],
                          ids=lambda c: "-".join(map(str, c)))
 def test_gated_pair_matches_separate_launches(mk, case):
     """Gate and up in one tensor-core launch (shared basis tiles, SwiGLU in the epilogue) give the
     same hidden activations and output, bit for bit, as the separate gate, up and SwiGLU
-    launches (at these shapes the separate launches do not split K either, so every output sums
-    its K blocks in the same order); the block output agrees with the oracle."""
+    launches (at these shapes the pair fills >= 120 wide tiles, so it takes the one launch, and
+    the separate launches do not split K either, so every output sums its K blocks in the same
+    order); the block output agrees with the oracle."""
     from metal_kans._engine import DeviceBuffer
 
     d_model, d_ffn, B, mode, bias, quant = case
@@ -191,6 +192,7 @@ def test_gated_pair_matches_separate_launches(mk, case):
     descs = [l._descriptor(keep) for l in blk._layers()]
     pair = blk._pair(descs[0], descs[1], keep)
     assert pair, "pair packing refused a compatible gate/up"
+    n0 = lib.kan_launch_count()
     dx = DeviceBuffer.from_array(x)
     outs = []
     for p in (pair, 0):  # one launch for gate + up, then the separate launches
@@ -203,6 +205,8 @@ def test_gated_pair_matches_separate_launches(mk, case):
         y = dy.download(np.empty((B, d_model), act))
         lib.kan_stream_synchronize(None)
         outs.append((h.view(np.uint16).copy(), y.view(np.uint16).copy()))
+        if p:  # gate + up as one launch, then down
+            assert lib.kan_launch_count() - n0 == 2
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
     # the public forward takes the fused launch; oracle of the block: each layer rounded to the
