@@ -121,14 +121,16 @@ TcPlan tc_plan(const LayerArgs& a) {
   p.nb = bl.NB;
   p.mtiles = (a.B + tc::BM - 1) / tc::BM;
   // wide tiles (two N = 256 accumulators per basis block) halve the basis work per output; taken
-  // when the grid of wide tiles still fills the GPU (no split-K for them), never for the staged
-  // LayerNorm input
+  // when the grid of wide tiles fills the GPU, or does with K split in two (the producers then
+  // build half the blocks per CTA: 64 wide tiles x 2 splits run in one wave where 128 narrow
+  // tiles each build every block), never for the staged LayerNorm input
   if (a.D_out >= 512 && a.input_map != KAN_MAP_LAYERNORM) {
     const long long wide_tiles = (long long)p.mtiles * ((a.D_out + 511) / 512);
-    if (wide_tiles >= 120) {
+    const int wide_splits = wide_tiles >= 120 ? 1 : (wide_tiles * 2 >= 120 && p.nb / 2 >= 32) ? 2 : 0;
+    if (wide_splits) {
       p.BN = 512;
       p.ntiles = (a.D_out + 511) / 512;
-      p.splits = 1;
+      p.splits = wide_splits;
       return p;
     }
   }

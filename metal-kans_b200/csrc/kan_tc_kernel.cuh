@@ -75,6 +75,12 @@ __host__ __device__ constexpr int red_bytes(int splits, int slice) {
 }
 static_assert(red_bytes(4, 64) <= OFF_BAR && red_bytes(2, 128) <= OFF_BAR,
               "split-K reduction slots must fit in the stage buffers");
+// Rounds of the reduction: the slice in 1, 2 or 4 column chunks so that the slots fit in `avail`
+// bytes of stage buffers (narrow tiles always take one round).
+__host__ __device__ constexpr int red_rounds(int splits, int slice, int avail) {
+  return red_bytes(splits, slice) <= avail ? 1 : (red_bytes(splits, slice / 2) <= avail ? 2 : 4);
+}
+static_assert(red_rounds(2, 256, 208 * 1024) == 2, "wide split-K reduction in two rounds");
 // LayerNorm input tile (rows of <= 256 features) staged over the A stages before the first block
 static_assert(BM * 256 * 2 <= STAGES * A_STAGE_BYTES, "x tile must fit in the A stages");
 
@@ -686,8 +692,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       bulk_g2s(s_base + OFF_A, (const T*)a.X + (size_t)m0 * a.D_in, bytes, bar_x);
     }
     // the other splits' slices arrive after the first cluster barrier, i.e. after this point
-    if (splits > 1)
-      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * BM * (slice + 4) * 4));
+    if (splits > 1) {
+      const int chunk0 = slice / red_rounds(splits, slice, OFF_BAR);
+      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * BM * (chunk0 + 4) * 4));
+    }
   }
   if (warp == MMA_WARP) tmem_alloc(s_base + OFF_TMEM, TMEM_COLS);
   tc_fence_before();
@@ -973,11 +981,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (splits > 1) {
     // Split-K reduction.  Slot k of a CTA's receive area [0, (S-1) slots) holds the slice sent by
     // the k-th other split; its staging area (the next S-1 slots) holds the slices it sends.
-    const int pitch = slice + 4;  // slot row pitch in floats
+    // When the slots of whole slices do not fit (wide tiles), the slice goes in `rounds` column
+    // chunks, each staged, copied, summed and stored before the next reuses the slots.
+    const int rounds = red_rounds(splits, slice, OFF_BAR);
+    const int chunk = slice / rounds;
+    const int pitch = chunk + 4;  // slot row pitch in floats
     const int slot_bytes = BM * pitch * 4;
     auto other = [&](int zz, int self) { return zz < self ? zz : zz - 1; };
-    const int half = slice >> 1;  // slice columns per producer warp (host: slice % 32 == 0)
+    const int half = chunk >> 1;  // chunk columns per producer warp (host: chunk % 32 == 0)
     bool ok = !producer_aborted && nj > 0;
+    for (int rd = 0; rd < rounds; ++rd) {
+    const int c0 = rd * chunk;  // first slice column of this round
+    if (rd > 0 && threadIdx.x == 0)
+      mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * slot_bytes));
     if (warp < NUM_PRODUCER_WARPS) {
       // 1. stage this CTA's slices of the other splits' columns (TMEM -> shared)
       const int q = warp & 3, h = warp >> 2;
@@ -992,7 +1008,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int cc = 0; cc < half; cc += 16) {
             const int cs = h * half + cc;  // column within the slice
             float v[16];
-            tmem_ld16(taddr0 + (uint32_t)(zz * slice + cs), v);
+            tmem_ld16(taddr0 + (uint32_t)(zz * slice + c0 + cs), v);
 #pragma unroll
             for (int u = 0; u < 4; ++u)
               *reinterpret_cast<float4*>(stage + cs + 4 * u) =
@@ -1021,7 +1037,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t taddr0 = tmem_d + ((uint32_t)(q * 32) << 16);
       // 3. the other splits' slices of this CTA's own columns have landed (always waited for:
       //    no copy may still target this CTA's shared memory when it exits)
-      if (!mbar_wait_warp(bar_red, 0)) {
+      if (!mbar_wait_warp(bar_red, (uint32_t)rd & 1u)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
         ok = false;
       }
@@ -1035,7 +1051,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int cc = 0; cc < half; cc += 16) {
           const int cs = h * half + cc;
           float own[16];
-          tmem_ld16(taddr0 + (uint32_t)(z * slice + cs), own);  // warp-collective
+          tmem_ld16(taddr0 + (uint32_t)(z * slice + c0 + cs), own);  // warp-collective
           float sum[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) sum[t] = 0.f;
@@ -1056,7 +1072,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               }
             }
           }
-          const int col0 = n0 + z * slice + cs;
+          const int col0 = n0 + z * slice + c0 + cs;
           if (row >= a.B || col0 >= a.D_out) continue;
           if (vec && col0 + 16 <= a.D_out) {
             if (a.has_bias) {
@@ -1095,9 +1111,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-    // every copy out of this CTA's staging slots has landed (its receiver waited for it)
+    // every copy out of this CTA's staging slots has landed (its receiver waited for it), so
+    // the next round may overwrite them, or the CTA may exit
     __syncwarp();
     cluster_sync_all();
+    }
   }
 
   tc_fence_before();
@@ -1136,13 +1154,13 @@ static cudaError_t launch_kernel(const CUtensorMap& tw, const CUtensorMap& tx, i
   return cudaLaunchKernelEx(&cfg, kern, tw, tx, a, BN, nb, splits, use_x);
 }
 
-// BN = 512 runs the wide variant (never split: the plan only picks it for grids of >= 120 tiles)
+// BN = 512 runs the wide variant (K split at most in two: its reduction slots fit in two rounds)
 template <int BASIS, int MODE, class Producer>
 static cudaError_t launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, int x_tma,
                              const LayerArgs& a, int BN, int nb, int splits, dim3 grid,
                              cudaStream_t s) {
   if (BN == 512) {
-    if (splits != 1) return cudaErrorInvalidValue;
+    if (splits > 2) return cudaErrorInvalidValue;
     return launch_kernel<BASIS, MODE, Producer, true>(tw, tx, x_tma, a, BN, nb, splits, grid, s);
   }
   return launch_kernel<BASIS, MODE, Producer, false>(tw, tx, x_tma, a, BN, nb, splits, grid, s);

@@ -205,11 +205,13 @@ def test_host_forward_chunked(mk, case):
 
 
 @pytest.mark.parametrize("case", [("cheby", 64, 1024, 9, 7680, "bf16"), ("rbf", 128, 640, 8, 7700, "f16"),
-                                  ("cheby", 96, 520, 5, 15400, "f16")],
+                                  ("cheby", 96, 520, 5, 15400, "f16"),
+                                  ("cheby", 400, 512, 9, 8000, "bf16"), ("rbf", 448, 520, 8, 7500, "f16")],
                          ids=lambda c: "-".join(map(str, c)))
 def test_wide_tiles(mk, case):
     """Grids of >= 120 tiles of 512 outputs run the wide tensor-core variant (two N = 256
-    accumulators per basis block): ragged rows and ragged output tiles included."""
+    accumulators per basis block); grids of 60-119 such tiles run it with K split in two (the
+    cluster reduction in two column rounds).  Ragged rows and ragged output tiles included."""
     basis, d_in, d_out, K, B, mode = case
     layer = set_mode(make_layer(basis, d_in, d_out, K, seed=5), mode)
     randomize_bias(layer)
