@@ -39,9 +39,10 @@ METRIC = "fused KAN layer rows/sec at 1/2/4/8 B200; % tensor-pipe or HBM rooflin
 
 # ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel, from the
 # `ncu --set full` captures summarised under profiles/ (one summary per kernel and workload);
-# None when the config was not captured at its own size (c3, c4 are captured on 2048 rows)
+# None when the config was not captured at its own size (c4 is captured on 2048 tokens); c3: the
+# first (largest) of its three launches
 TRAFFIC = {"c2": 3386368, "c1": 453632, "c5:ternary:4096": 470647552 + 23311616,
-           "c5:ternary:16": 53773568 + 152064}
+           "c5:ternary:16": 53773568 + 152064, "c3": 20276992}
 
 
 def peaks():
