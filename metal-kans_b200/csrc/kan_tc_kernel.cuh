@@ -14,16 +14,26 @@
 //              reads.  Phi never reaches HBM (the reference writes it to a scratch buffer and runs
 //              MPS GEMMs on it, metal_kan_bridge.mm:503-523).  After the K loop these warps run
 //              the epilogue: tcgen05.ld of the fp32 accumulator, + bias, round, store.
-//   warp 8     TMA producer: one cp.async.bulk.tensor.2d per stage for the BN x 64 weight tile.
+//   warp 8     TMA producer: one cp.async.bulk.tensor.2d per stage for the BN x 64 weight tile
+//              (two 256-row boxes for BN = 512).
 //   warp 9     TMEM allocator and MMA issuer: 4 x tcgen05.mma.cta_group::1.kind::f16
-//              (M=128, N=BN, K=16) per stage into the TMEM accumulator; tcgen05.commit frees the
-//              stage and finally signals the epilogue.
+//              (M=128, N=BN, K=16) per stage into the TMEM accumulator -- for BN = 512 ("wide")
+//              two N = 256 MMAs per K step into the two halves of TMEM, so each basis block the
+//              producers build feeds twice the tensor work; tcgen05.commit frees the stage and
+//              finally signals the epilogue.
+//   warp 10    TMA producer of the input tiles (64 features x 128 rows per stage).
+//
+// The grid runs M tiles fastest: the CTAs resident at one time share a few weight panels in L2.
 //
 // Split-K (grid.z = S > 1, launched as clusters of S CTAs along z) serves grids too small to fill
-// the 148 SMs without recomputing the basis per N tile: each CTA of the cluster parks its fp32
-// partial tile in its own shared memory, and CTA z then reduces column slice z of the tile over
-// the S partials read through distributed shared memory, always in split order (deterministic),
-// adds the bias and stores Y.  No global scratch is involved.
+// the 148 SMs without recomputing the basis per N tile: each CTA stages the other splits' column
+// slices of its fp32 partial tile in its own shared memory and bulk-copies them to their owners
+// (distributed shared memory, no multicast); CTA z sums column slice z over the S partials in
+// split order (deterministic), adds the bias and stores Y -- in column rounds when the slots of
+// whole slices do not fit.  No global scratch is involved.
+//
+// fuse_swiglu (GatedKAN): the packed weights interleave gate and up rows per 256 outputs and the
+// epilogue writes silu(gate) * up of the wide tile's two halves.
 //
 // Every mbarrier wait is bounded (about one second of SM clocks); on expiry the kernel records
 // the error in the device error word, skips its remaining work, still joins every CTA-wide and
