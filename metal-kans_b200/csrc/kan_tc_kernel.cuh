@@ -1031,8 +1031,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncwarp();
     // every CTA has finished its main loop (its receive area is free) and staged its slices
     cluster_sync_all();
-    // 2. one bulk copy per other split: staging slot -> that CTA's receive slot for this split
-    if (threadIdx.x == 0 && ok) {
+    // 2. one bulk copy per other split: staging slot -> that CTA's receive slot for this split.
+    //    Sent even after an abort (the data is then meaningless, the error word is set), so that
+    //    every receiver's phase of bar_red completes before it is armed for the next round.
+    if (threadIdx.x == 0) {
       for (int zz = 0; zz < splits; ++zz) {
         if (zz == z) continue;
         bulk_s2cluster(map_to_rank(s_base + OFF_A + other(z, zz) * slot_bytes, (uint32_t)zz),
