@@ -206,7 +206,8 @@ def test_host_forward_chunked(mk, case):
 
 @pytest.mark.parametrize("case", [("cheby", 64, 1024, 9, 7680, "bf16"), ("rbf", 128, 640, 8, 7700, "f16"),
                                   ("cheby", 96, 520, 5, 15400, "f16"),
-                                  ("cheby", 400, 512, 9, 8000, "bf16"), ("rbf", 448, 520, 8, 7500, "f16")],
+                                  ("cheby", 400, 512, 9, 8000, "bf16"), ("rbf", 448, 520, 8, 7500, "f16"),
+                                  ("cheby", 64, 517, 9, 15400, "bf16")],
                          ids=lambda c: "-".join(map(str, c)))
 def test_wide_tiles(mk, case):
     """Grids of >= 120 tiles of 512 outputs run the wide tensor-core variant (two N = 256

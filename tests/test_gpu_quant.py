@@ -163,7 +163,8 @@ def test_gated_int4_golden(mk):
 
 @pytest.mark.parametrize("case", [(256, 640, 5120, "bf16", False, "int4"),
                                   (256, 600, 5200, "f16", True, None),
-                                  (128, 384, 7680, "bf16", True, "ternary")],
+                                  (128, 384, 7680, "bf16", True, "ternary"),
+                                  (64, 601, 5120, "bf16", True, "int8")],
                          ids=lambda c: "-".join(map(str, c)))
 def test_gated_pair_matches_separate_launches(mk, case):
     """Gate and up in one tensor-core launch (shared basis tiles, SwiGLU in the epilogue) give the
@@ -184,6 +185,8 @@ def test_gated_pair_matches_separate_launches(mk, case):
         blk.to_int4(group_size=64)
     elif quant == "ternary":
         blk.to_ternary(group_size=64)
+    elif quant == "int8":
+        blk.to_int8(group_size=64)
     blk.bfloat16() if mode == "bf16" else blk.half()
     act = blk.gate_kan.dtype
     x = np.random.default_rng(B).normal(0, 1, (B, d_model)).astype(np.float32).astype(act)
