@@ -439,8 +439,13 @@ int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {
     KAN_CUDA_TRY(cudaMemcpyAsync((char*)Y + (size_t)r0 * yrow, yd, (size_t)rows * yrow,
                                  cudaMemcpyDeviceToHost, d->d2h));
   }
+  // the device error word rides on the same copy stream (after the last kernel, which the last
+  // result copy waited for): one synchronisation for the results and the error check
+  KAN_CUDA_TRY(cudaMemcpyAsync(d->err_host, d->err_word, sizeof(int), cudaMemcpyDeviceToHost,
+                               d->d2h));
   KAN_CUDA_TRY(cudaStreamSynchronize(d->d2h));
-  return check_device_error(d);
+  if (*d->err_host) return check_device_error(d);  // reads it again on the engine stream, clears it
+  return KAN_OK;
 }
 
 // Gate and up of a GatedKAN share their input and their basis (Chebyshev, same K, base branch and
