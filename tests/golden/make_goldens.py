@@ -192,8 +192,11 @@ def block_goldens(mk):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("KAN_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("KAN_REFERENCE"),
+                    help="the reference source tree (or set KAN_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <path to the reference tree> or set KAN_REFERENCE")
     sys.path.insert(0, args.reference)
     sys.path.insert(0, REPO)
     import metal_kans as mk  # the reference package
