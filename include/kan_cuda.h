@@ -228,6 +228,20 @@ int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* str
 /* Same with an explicit kernel path (tests, benchmarks). */
 int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int path,
                      void* stream);
+/* No counterpart in the reference.  The kernel plan kan_forward_path(layer, X, Y, B, path) would
+ * run, without running it: info[0] = the path taken (KAN_PATH_SIMT / TC / GEMV; `path` may be
+ * KAN_PATH_AUTO), and for the tensor-core path info[1] = tile width BN, info[2] = split-K factor
+ * (cluster size), info[3] = M tiles, info[4] = N tiles, info[5] = 64-column K blocks; for the
+ * small-batch path info[3] = 128-row blocks.  Tests and benchmarks use it to name the plan they
+ * check.  info must hold 6 ints. */
+int kan_forward_plan(const kan_layer* layer, int B, int path, int* info);
+/* No counterpart in the reference.  Limit of the tensor-core kernel's pipeline waits (a stage
+ * filled or freed by another warp role), in SM clock cycles, for the launches that follow on any
+ * device; 0 restores the default of about one second.  A short limit makes those waits expire,
+ * so that the abort path (error word set, remaining work skipped, every copy and MMA in flight
+ * still waited for with the full limit, TMEM released) can be driven by a test; the next call
+ * then reports KAN_ERR_DEVICE_TIMEOUT.  Not for production use. */
+int kan_set_wait_limit(long long cycles);
 /* No counterpart in the reference's device API; replaces the host-pointer convention of the
  * bridge's forwards (metal_kan_bridge.mm:1890-1971: copy in, compute, copy out, synchronous) for
  * any kan_layer.  X [B][D_in] and Y [B][D_out] are HOST memory (page-locked for overlap);

@@ -52,6 +52,10 @@ static std::atomic<long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(); }
 
+// kan_set_wait_limit(): 0 = the kernels' default (about one second of SM clocks)
+static std::atomic<long long> g_wait_limit{0};
+long long pipeline_wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
+
 // ------------------------------------------------------------------------------------------
 // per-device state
 // ------------------------------------------------------------------------------------------
@@ -306,6 +310,7 @@ static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceSt
   a->wb = L->wb;
   a->err = d->err_word;
   a->tc_weights = L->tc_weights;
+  a->wait_cycles = pipeline_wait_limit();
   return KAN_OK;
 }
 
@@ -326,6 +331,14 @@ static int run_tc(LayerArgs& a, int act_dtype, cudaStream_t s, DeviceState* d) {
   return KAN_OK;
 }
 
+// KAN_PATH_AUTO: the small-batch kernel where it applies, else the tensor cores for f16/bf16,
+// else the CUDA cores.
+static int auto_path(const LayerArgs& a, int act_dtype) {
+  if (gemv_supported(a, act_dtype)) return KAN_PATH_GEMV;
+  if (act_dtype != KAN_F32 && tc_supported(a, act_dtype)) return KAN_PATH_TC;
+  return KAN_PATH_SIMT;
+}
+
 static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int path,
                        cudaStream_t s, DeviceState* d) {
   LayerArgs a;
@@ -334,11 +347,7 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
   if (B == 0) return KAN_OK;
   cudaError_t e;
   const bool gemv_ok = gemv_supported(a, L->act_dtype);
-  if (path == KAN_PATH_AUTO) {
-    path = gemv_ok ? KAN_PATH_GEMV
-                   : (L->act_dtype != KAN_F32 && tc_supported(a, L->act_dtype)) ? KAN_PATH_TC
-                                                                                 : KAN_PATH_SIMT;
-  }
+  if (path == KAN_PATH_AUTO) path = auto_path(a, L->act_dtype);
   if (path == KAN_PATH_TC) {
     if (!tc_supported(a, L->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED,
@@ -388,6 +397,43 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
 
 int kan_forward(const kan_layer* layer, const void* X, void* Y, int B, void* stream) {
   return kan_forward_path(layer, X, Y, B, KAN_PATH_AUTO, stream);
+}
+
+int kan_forward_plan(const kan_layer* layer, int B, int path, int* info) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!info) return fail(KAN_ERR_ARG, "forward_plan: NULL info");
+  // any non-null pointers: the plan depends on shapes, formats and alignment of the weights only
+  static const uint8_t dummy[16] = {};
+  LayerArgs a;
+  if ((rc = make_args(layer, dummy, (void*)dummy, B, d, &a))) return rc;
+  if (path == KAN_PATH_AUTO) path = auto_path(a, layer->act_dtype);
+  for (int i = 0; i < 6; ++i) info[i] = 0;
+  info[0] = path;
+  if (path == KAN_PATH_TC) {
+    if (!tc_supported(a, layer->act_dtype))
+      return fail(KAN_ERR_UNSUPPORTED, "forward_plan: the layer does not fit the tensor cores");
+    const TcPlan p = tc_plan(a);
+    info[1] = p.BN;
+    info[2] = p.splits;
+    info[3] = p.mtiles;
+    info[4] = p.ntiles;
+    info[5] = p.nb;
+  } else if (path == KAN_PATH_GEMV) {
+    if (!gemv_supported(a, layer->act_dtype))
+      return fail(KAN_ERR_UNSUPPORTED, "forward_plan: the layer does not fit the small-batch path");
+    info[3] = (layer->D_out + 127) / 128;
+  } else if (path != KAN_PATH_SIMT) {
+    return fail(KAN_ERR_ARG, "forward_plan: unknown path %d", path);
+  }
+  return KAN_OK;
+}
+
+int kan_set_wait_limit(long long cycles) {
+  if (cycles < 0) return fail(KAN_ERR_ARG, "wait limit %lld < 0", cycles);
+  g_wait_limit.store(cycles, std::memory_order_relaxed);
+  return KAN_OK;
 }
 
 int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {

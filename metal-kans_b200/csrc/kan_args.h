@@ -31,6 +31,9 @@ struct LayerArgs {
   // has_bias2 to up
   int fuse_swiglu, h_cols, has_bias2;
   const void* bias2;
+  // limit of the tensor-core kernel's pipeline waits, in SM clock cycles (waits on copies and
+  // MMAs already in flight always use the default of about one second)
+  long long wait_cycles;
 };
 
 // Rows of a gate/up pair in the interleaved tensor-core layout: per 256 output columns, 256

@@ -43,6 +43,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "kan_tc_kernel.cuh"
 
@@ -711,6 +712,8 @@ static int max_clusters(Kern kern, int ki, const cudaLaunchConfig_t& q) {
   };
   static Entry cache[32];
   static int used = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
   const int S = (int)q.attrs[0].val.clusterDim.z, smem = (int)q.dynamicSmemBytes;
   for (int i = 0; i < used; ++i)
     if (cache[i].ki == ki && cache[i].S == S && cache[i].smem == smem) return cache[i].clusters;
@@ -766,12 +769,10 @@ cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream
       kan_gemv_kernel<MODE_BF16, KAN_W_INT2, false>, kan_gemv_kernel<MODE_BF16, KAN_W_INT2, true>};
   const int ki = (bf ? 4 : 0) + (tern ? 0 : 2) + (p.gs == 32 ? 1 : 0);
   const KernFn kern = kerns[ki];
-  static bool configured[8] = {false, false, false, false, false, false, false, false};
-  if (!configured[ki]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SMEM_LIMIT);
+  static std::atomic<unsigned long long> configured[8];  // per device, one per instance
+  {
+    cudaError_t e = ensure_smem_attr(kern, SMEM_LIMIT, configured[ki]);
     if (e != cudaSuccess) return e;
-    configured[ki] = true;
   }
   // K splits: the largest power of two (<= the plan's) whose whole grid of clusters the GPU holds
   // at once (clusters must fit inside one GPC; a second wave would double the time)

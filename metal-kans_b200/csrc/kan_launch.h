@@ -4,11 +4,36 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "kan_args.h"
 
 namespace kan {
 
 inline int BasisOf(const LayerArgs& a) { return a.basis; }
+
+// Dynamic shared-memory limit of `kern` on the current device, set once per device.
+// cudaFuncSetAttribute acts on the current device only, so the "done" state is one bit per
+// device in `done` (a static of the caller, one per kernel); the bit is set atomically, and two
+// host threads that race on a device's first launch both set the same attribute, which is
+// harmless.  Devices past the mask's width set it on every launch.
+template <class Kern>
+inline cudaError_t ensure_smem_attr(Kern kern, int smem_bytes,
+                                    std::atomic<unsigned long long>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// Limit of the tensor-core kernel's pipeline waits in SM clock cycles (0: the default of about
+// one second).  A short limit makes those waits expire so that tests can drive the abort path;
+// waits for copies and MMAs already in flight always keep the default (kan_abi.cpp).
+long long pipeline_wait_limit();
 
 void note_launch();
 long long launch_count();

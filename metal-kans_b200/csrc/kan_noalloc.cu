@@ -82,10 +82,18 @@ int kan_gated_forward_noalloc(const kan_layer* gate, const kan_layer* up, const 
     const bool lowp = layers[i]->act_dtype != KAN_F32;
     path[i] = (lowp && layers[i]->tc_weights) ? KAN_PATH_TC : KAN_PATH_SIMT;
   }
-  if ((rc = kan_forward_path(gate, X, g, B, path[0], stream))) return rc;
-  if ((rc = kan_forward_path(up, X, u, B, path[1], stream))) return rc;
+  // a layer the tensor cores cannot take (e.g. no tensor-map encoder in this driver) runs on the
+  // CUDA cores, as kan_gated_forward() would run it; neither path allocates
+  auto run = [&](const kan_layer* L, const void* in, void* out, int p) {
+    int r = kan_forward_path(L, in, out, B, p, stream);
+    if (r == KAN_ERR_UNSUPPORTED && p == KAN_PATH_TC)
+      r = kan_forward_path(L, in, out, B, KAN_PATH_SIMT, stream);
+    return r;
+  };
+  if ((rc = run(gate, X, g, path[0]))) return rc;
+  if ((rc = run(up, X, u, path[1]))) return rc;
   if ((rc = kan_swiglu(g, u, H, (long long)B * gate->D_out, gate->act_dtype, stream))) return rc;
-  return kan_forward_path(down, H, Y, B, path[2], stream);
+  return run(down, H, Y, path[2]);
 }
 
 }  // extern "C"

@@ -75,7 +75,8 @@ constexpr int NUM_BARS = 2 * STAGES + 2 * BSTAGES + 2 * XSTAGES + 3;
 constexpr int OFF_TMEM = OFF_BAR + NUM_BARS * 8;
 constexpr int OFF_FLAG = OFF_TMEM + 4;
 constexpr int OFF_EPI = OFF_FLAG + 4;
-constexpr int OFF_STATS = (OFF_EPI + 4 + 15) / 16 * 16;    // LayerNorm partial sums / stats
+constexpr int OFF_RED = OFF_EPI + 4;                       // split-K: a reduction wait expired
+constexpr int OFF_STATS = (OFF_RED + 4 + 15) / 16 * 16;    // LayerNorm partial sums / stats
 constexpr int SMEM_BYTES = OFF_STATS + 4 * BM * 4;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
 // Split-K reduction buffers, over the (finished) pipeline buffers: (splits - 1) receive slots and
@@ -112,7 +113,8 @@ struct Layout {
   static constexpr int kOffTmem = kOffBar + kNumBars * 8;
   static constexpr int kOffFlag = kOffTmem + 4;
   static constexpr int kOffEpi = kOffFlag + 4;
-  static constexpr int kOffStats = (kOffEpi + 4 + 15) / 16 * 16;
+  static constexpr int kOffRed = kOffEpi + 4;
+  static constexpr int kOffStats = (kOffRed + 4 + 15) / 16 * 16;
   static constexpr int kSmemAlloc = kOffStats + 4 * BM * 4 + 1024;
 };
 static_assert(Layout<false>::kSmemAlloc == SMEM_ALLOC, "narrow layout unchanged");
@@ -160,21 +162,26 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity`; false when the limit expired.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase of `parity`; false when `limit` SM cycles passed first.  The suspend
+// hint never exceeds about half the limit, so that a short limit (tests of the abort path) is
+// honoured instead of sleeping through it.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          long long limit = WAIT_LIMIT_CYCLES) {
   if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t hint = limit >= 40000LL ? 20000u : (uint32_t)(limit / 2 + 1);
   const long long t0 = clock64();
-  while (!mbar_try_wait_hint(bar, parity, 20000u))
-    if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+  while (!mbar_try_wait_hint(bar, parity, hint))
+    if (clock64() - t0 > limit) return false;
   return true;
 }
 // Warp-wide bounded wait: lane 0 polls, the outcome is broadcast, each lane then takes the
 // completed phase with one (immediately successful) try_wait for its own acquire ordering, and
 // the warp leaves reconverged -- per-lane polling would let the lanes leave the loop at different
 // iterations and run the following code (shuffles, the A-tile producer) diverged.
-__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity,
+                                               long long limit = WAIT_LIMIT_CYCLES) {
   uint32_t ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity) ? 1u : 0u;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, limit) ? 1u : 0u;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (ok) (void)mbar_try_wait(bar, parity);
   __syncwarp();
@@ -640,6 +647,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t TMEM_COLS = LY::kTmemCols;
   constexpr int OFF_B = LY::kOffB, OFF_X = LY::kOffX, OFF_BAR = LY::kOffBar;
   constexpr int OFF_TMEM = LY::kOffTmem, OFF_FLAG = LY::kOffFlag, OFF_EPI = LY::kOffEpi;
+  constexpr int OFF_RED = LY::kOffRed;
   constexpr int OFF_STATS = LY::kOffStats;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -656,6 +664,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_FLAG);
   volatile int* epi_flag = reinterpret_cast<volatile int*>(smem + OFF_EPI);
+  volatile int* red_expired = reinterpret_cast<volatile int*>(smem + OFF_RED);
   float* s_stats = reinterpret_cast<float*>(smem + OFF_STATS);  // [4][BM]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -670,6 +679,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const bool ln_staged = !WIDE && a.input_map == KAN_MAP_LAYERNORM && ln_smem_ok(a);
   const int rows_valid = min(BM, a.B - m0);
   const int slice = BN / splits;  // split-K: columns of the tile this CTA finishes
+  // Pipeline waits (a stage filled or freed by another role) take the call's limit; waits for
+  // copies or MMAs this CTA already has in flight (bar_x, the TMA drains, bar_accum, bar_red)
+  // always take the full limit, so that nothing still targets this CTA's shared memory or TMEM
+  // when it aborts and exits.
+  const long long plim = a.wait_cycles > 0 ? a.wait_cycles : WAIT_LIMIT_CYCLES;
 
   // input stages of this split: 64-feature tiles covering features [F*kb0, F*kb1)
   const TcBlocking blocking = tc_blocking(a.D_in, a.K, a.has_base);
@@ -694,6 +708,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(bar_red, 1);
     *abort_flag = 0;
     *epi_flag = 0;
+    *red_expired = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     if (ln_staged) {
       // the CTA's input rows are one contiguous block of X
@@ -768,7 +783,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         bool ok = true;
         for (int st = st_lo; st <= st_hi && ok; ++st) {
           const int u = st - xs_first;
-          ok = mbar_wait_warp(bar_full_x + 8 * (u % XSTAGES), (uint32_t)(u / XSTAGES) & 1u);
+          ok = mbar_wait_warp(bar_full_x + 8 * (u % XSTAGES), (uint32_t)(u / XSTAGES) & 1u,
+                              plim);
         }
         if (!ok) {
           raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
@@ -781,7 +797,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int f = 0; f < Producer::F; ++f) xs[f] = prod.xn[f];
         if (j + 2 < nj) prod.prefetch(xrow, valid, kb0 + j + 2, a.D_in);
       }
-      if (!mbar_wait_warp(bar_empty + 8 * s, (it & 1u) ^ 1u)) {
+      if (!mbar_wait_warp(bar_empty + 8 * s, (it & 1u) ^ 1u, plim)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
         *abort_flag = 1;
         break;
@@ -792,7 +808,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_full_a + 8 * s);
     }
-    if (x_tma) release_x_until(xs_last + 1);
+    // After an abort the input stages this warp did not get to are not released: a load may
+    // still be landing in them, and a release would let the input TMA warp reuse the slot with
+    // the earlier load in flight.  That warp's own wait then expires and it drains its loads.
+    const bool aborted_here = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+    if (x_tma && !aborted_here) release_x_until(xs_last + 1);
 
     // ------------------------------------------------------------------ epilogue
     if (!mbar_wait_warp(bar_accum, 0)) {
@@ -908,7 +928,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < nj; ++j) {
         const int s = j % BSTAGES;
         const uint32_t it = (uint32_t)(j / BSTAGES);
-        if (!mbar_wait(bar_empty_b + 8 * s, (it & 1u) ^ 1u)) {
+        if (!mbar_wait(bar_empty_b + 8 * s, (it & 1u) ^ 1u, plim)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
@@ -935,9 +955,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < nj; ++j) {
         const int s = j % STAGES, sb = j % BSTAGES;
         const uint32_t par = (uint32_t)(j / STAGES) & 1u;
-        bool ok = mbar_wait(bar_full_a + 8 * s, par);
+        bool ok = mbar_wait(bar_full_a + 8 * s, par, plim);
         if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
-        if (ok && !mbar_wait(bar_full_b + 8 * sb, (uint32_t)(j / BSTAGES) & 1u)) {
+        if (ok && !mbar_wait(bar_full_b + 8 * sb, (uint32_t)(j / BSTAGES) & 1u, plim)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
           ok = false;
         }
@@ -971,7 +991,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       int issued = 0;
       for (int st = xs_first; st <= xs_last; ++st) {
         const int u = st - xs_first, slot = u % XSTAGES;
-        if (!mbar_wait(bar_empty_x + 8 * slot, ((uint32_t)(u / XSTAGES) & 1u) ^ 1u)) {
+        if (!mbar_wait(bar_empty_x + 8 * slot, ((uint32_t)(u / XSTAGES) & 1u) ^ 1u, plim)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
@@ -1002,7 +1022,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = !producer_aborted && nj > 0;
     for (int rd = 0; rd < rounds; ++rd) {
     const int c0 = rd * chunk;  // first slice column of this round
-    if (rd > 0 && threadIdx.x == 0)
+    // A reduction wait that expired (a slice did not land within the limit) leaves bar_red's
+    // phase incomplete: it is then neither re-armed nor waited on again, and this CTA stops
+    // staging and summing; it still sends its copies (their contents then meaningless, the error
+    // word set) and joins every cluster barrier, so that the other CTAs of the cluster complete
+    // their rounds.  The flag is read after the cluster barrier that ends the previous round.
+    // This wait always has the full limit: it waits for copies already in flight.
+    const bool red_live = *red_expired == 0;
+    if (!red_live) ok = false;
+    if (rd > 0 && threadIdx.x == 0 && red_live)
       mbar_arrive_expect_tx(bar_red, (uint32_t)((splits - 1) * slot_bytes));
     if (warp < NUM_PRODUCER_WARPS) {
       // 1. stage this CTA's slices of the other splits' columns (TMEM -> shared)
@@ -1049,8 +1077,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t taddr0 = tmem_d + ((uint32_t)(q * 32) << 16);
       // 3. the other splits' slices of this CTA's own columns have landed (always waited for:
       //    no copy may still target this CTA's shared memory when it exits)
-      if (!mbar_wait_warp(bar_red, (uint32_t)rd & 1u)) {
+      if (red_live && !mbar_wait_warp(bar_red, (uint32_t)rd & 1u)) {
         raise_device_error(a.err, DEVERR_TIMEOUT_ACCUM);
+        *red_expired = 1;
         ok = false;
       }
       // 4. sum in split order (deterministic), bias, store 16 outputs at a time
@@ -1144,12 +1173,9 @@ static cudaError_t launch_kernel(const CUtensorMap& tw, const CUtensorMap& tx, i
                                  cudaStream_t s) {
   auto kern = kan_tc_kernel<BASIS, MODE, Producer, WIDE>;
   constexpr int smem = Layout<WIDE>::kSmemAlloc;
-  static bool configured = false;  // one per template instance
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static std::atomic<unsigned long long> configured{0};  // per device, one per template instance
+  cudaError_t e = ensure_smem_attr(kern, smem, configured);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(THREADS, 1, 1);

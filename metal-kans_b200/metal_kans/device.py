@@ -97,6 +97,8 @@ SIGNATURES = [
     ("benchmark_metal_wavkan", ctypes.c_double, [vp] * 7 + [i32] * 9),
     ("kan_forward", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, vp]),
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
+    ("kan_forward_plan", i32, [ctypes.POINTER(KanLayer), i32, i32, ctypes.POINTER(i32)]),
+    ("kan_set_wait_limit", i32, [i64]),
     ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
     ("kan_gated_forward_pair", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, vp, i32, vp]),

@@ -154,6 +154,22 @@ class Int2QuantizedWeight(_PackedMixin):
         w.data, w.scales, w.codebook = p.ptr, s.ptr, c.ptr
 
 
+def pack_codes(codes: np.ndarray) -> np.ndarray:
+    """2-bit codes [rows, cols] (values 0..3) in the packed layout of the ternary and INT2
+    weights: 16 codes per uint32, code k of a row at bits 2*(k % 16) of word k // 16, the row's
+    last word zero padded (quantization.py:191-286 of the reference)."""
+    c = np.asarray(codes)
+    rows, cols = c.shape
+    words = (cols + 15) // 16
+    padded = np.zeros((rows, words * 16), np.uint32)
+    padded[:, :cols] = c.astype(np.uint32) & 3
+    lanes = padded.reshape(rows, words, 16)
+    out = np.zeros((rows, words), np.uint32)
+    for j in range(16):
+        out |= lanes[:, :, j] << np.uint32(2 * j)
+    return out
+
+
 def packed_from_codes(kind: str, w_packed: np.ndarray, scales: np.ndarray, shape,
                       group_size: int, codebook=None):
     """Build a Ternary/Int2QuantizedWeight straight from its packed codes and scales (same

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from conftest import group, load_npz
-from kan_cases import TOL, make_layer, oracle_for_layer
+from kan_cases import TOL, layer_err, make_layer, oracle_for_layer
 from oracle import kan_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -95,6 +95,40 @@ def test_swiglu_and_benchmark_entry_points(mk):
     x = rng.uniform(-1, 1, (1024, 64)).astype(np.float32)
     ms = l.benchmark(x, warmup=2, iters=5)
     assert 0 < ms < 1000
+
+
+K_OF = {"cheby": 5, "rbf": 8, "bspline": 8, "wavelet": 6}
+
+
+@pytest.mark.parametrize("basis", ["cheby", "rbf", "bspline", "wavelet"])
+def test_benchmark_entry_points_all_bases(mk, basis):
+    """benchmark_metal_{cheby,fastkan,bspline,wavkan} (metal_kan_bridge.mm:1250-1371): a positive
+    mean of milliseconds per host-pointer forward, and the Y each leaves behind is the layer's
+    forward (fp32 path, 1e-5 against the oracle)."""
+    lib = mk.get_metal_bridge()
+    l = make_layer(basis, 48, 40, K_OF[basis], seed=6)
+    rng = np.random.default_rng(6)
+    l.bias = rng.normal(0, 0.1, 40).astype(np.float32)
+    x = rng.uniform(-1, 1, (300, 48)).astype(np.float32)
+    assert 0 < l.benchmark(x, warmup=1, iters=3) < 1000
+    y = np.empty((300, 40), np.float32)
+    W = getattr(l, l.MAIN)
+    if basis == "cheby":
+        ms = lib.benchmark_metal_cheby(P(x), P(W), P(l.w_base), P(l.bias), P(y), 300, 48, 40,
+                                       l._terms(), 1, 1, 1, 3)
+    elif basis == "rbf":
+        ms = lib.benchmark_metal_fastkan(P(x), P(W), P(l.w_base), P(l.grid), P(l.bias), P(y), 300,
+                                         48, 40, l.num_centers, l.inv_denominator, 1, 1, 1, 3)
+    elif basis == "bspline":
+        g = np.ascontiguousarray(l.grid, np.float32)
+        ms = lib.benchmark_metal_bspline(P(x), P(W), P(l.w_base), P(g), P(l.bias), P(y), 300, 48,
+                                         40, l.grid_size, l.spline_order, 1, 1, 1, 3)
+    else:
+        ms = lib.benchmark_metal_wavkan(P(x), P(W), P(l.w_base), P(l.translation),
+                                        P(l._inv_scale), P(l.bias), P(y), 300, 48, 40,
+                                        l.num_wavelets, l.wavelet_type, 1, 1, 1, 3)
+    assert 0 < ms < 1000
+    assert layer_err(y, l, x, "f32", basis) <= 1e-5
 
 
 @pytest.mark.parametrize("mode", ["f32", "f16"])
