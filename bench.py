@@ -474,7 +474,7 @@ def device_step(mk, obj, layers, B, x_ptr, y_ptr, keep):
 def plan_of(mk, layers, B):
     """The kernel plan of each layer's launch (kan_forward_plan): path, tile width, splits."""
     lib = mk.get_metal_bridge()
-    names = {1: "simt", 2: "tc", 3: "small-batch"}
+    names = {1: "simt", 2: "tc", 3: "small-batch tensor cores", 4: "small-batch CUDA cores"}
     out = []
     for l in layers:
         keep = []
@@ -486,6 +486,8 @@ def plan_of(mk, layers, B):
             e.update(BN=info[1], splits=info[2], grid=[info[3], info[4], info[2]])
         elif info[0] == 3:
             e.update(row_blocks=info[3])
+        elif info[0] == 4:
+            e.update(row_blocks=info[3], splits=info[2])
         out.append(e)
     return out
 

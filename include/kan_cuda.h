@@ -169,11 +169,19 @@ enum kan_wformat {
   KAN_W_TERNARY = 3, /* u32 [rows][ceil(cols/16)], fp32 scales [rows][ceil(cols/gs)]           */
   KAN_W_INT2 = 4     /* as ternary + fp32 codebook[4]                                          */
 };
-/* Kernel selection for kan_forward_path.  KAN_PATH_AUTO: the small-batch kernel (GEMV) when it
-   applies (f16/bf16 Chebyshev layer, ternary/INT2 weights, B <= 64, D_in >= 512, D_out >= 256),
-   else the tensor-core kernel (TC) for f16/bf16, else the CUDA-core kernel (SIMT).  An explicit
-   path a layer does not fit returns KAN_ERR_UNSUPPORTED. */
-enum kan_path { KAN_PATH_AUTO = 0, KAN_PATH_SIMT = 1, KAN_PATH_TC = 2, KAN_PATH_GEMV = 3 };
+/* Kernel selection for kan_forward_path.  KAN_PATH_AUTO: the CUDA-core small-batch kernel
+   (GEMV_CC) when it applies (f16/bf16 layer of any basis and input map, ternary/INT8/INT4 weights,
+   B <= 4), else the tensor-core small-batch kernel (GEMV: f16/bf16 Chebyshev layer, ternary/INT2
+   weights, B <= 64, D_in >= 512, D_out >= 128), else the tensor-core kernel (TC) for f16/bf16,
+   else the CUDA-core kernel (SIMT).  An explicit path a layer does not fit returns
+   KAN_ERR_UNSUPPORTED. */
+enum kan_path {
+  KAN_PATH_AUTO = 0,
+  KAN_PATH_SIMT = 1,
+  KAN_PATH_TC = 2,
+  KAN_PATH_GEMV = 3,
+  KAN_PATH_GEMV_CC = 4
+};
 
 /* One weight matrix with `rows` = D_out and `cols` = D_in*K (basis) or D_in (base branch). */
 typedef struct kan_weight {
@@ -232,7 +240,8 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
  * run, without running it: info[0] = the path taken (KAN_PATH_SIMT / TC / GEMV; `path` may be
  * KAN_PATH_AUTO), and for the tensor-core path info[1] = tile width BN, info[2] = split-K factor
  * (cluster size), info[3] = M tiles, info[4] = N tiles, info[5] = 64-column K blocks; for the
- * small-batch path info[3] = 128-row blocks.  Tests and benchmarks use it to name the plan they
+ * tensor-core small-batch path info[3] = 128-row blocks; for the CUDA-core small-batch path
+ * info[2] = K splits, info[3] = 32-row blocks.  Tests and benchmarks use it to name the plan they
  * check.  info must hold 6 ints. */
 int kan_forward_plan(const kan_layer* layer, int B, int path, int* info);
 /* No counterpart in the reference.  Limit of the tensor-core kernel's pipeline waits (a stage

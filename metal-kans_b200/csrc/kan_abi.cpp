@@ -72,7 +72,7 @@ struct PendingCopy {
 // Engine scratch of one stream: packed tensor-core weights (when the caller passes none) and the
 // GatedKAN gate/up activations.  Kept per stream so that work queued on different streams never
 // shares a buffer.
-enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, SC_HX, SC_HY, NUM_SCRATCH };
+enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, SC_HX, SC_HY, SC_CC, NUM_SCRATCH };
 struct Scratch {
   cudaStream_t stream = nullptr;
   void* ptr[NUM_SCRATCH] = {};
@@ -334,6 +334,7 @@ static int run_tc(LayerArgs& a, int act_dtype, cudaStream_t s, DeviceState* d) {
 // KAN_PATH_AUTO: the small-batch kernel where it applies, else the tensor cores for f16/bf16,
 // else the CUDA cores.
 static int auto_path(const LayerArgs& a, int act_dtype) {
+  if (gemv_cc_supported(a, act_dtype)) return KAN_PATH_GEMV_CC;
   if (gemv_supported(a, act_dtype)) return KAN_PATH_GEMV;
   if (act_dtype != KAN_F32 && tc_supported(a, act_dtype)) return KAN_PATH_TC;
   return KAN_PATH_SIMT;
@@ -361,6 +362,15 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
     void* phi;
     if ((rc = scratch_buf(d, s, SC_PHI, gemv_phi_bytes(a), false, &phi))) return rc;
     e = launch_gemv(a, L->act_dtype, phi, s);
+  } else if (path == KAN_PATH_GEMV_CC) {
+    if (!gemv_cc_supported(a, L->act_dtype))
+      return fail(KAN_ERR_UNSUPPORTED,
+                  "CUDA-core small-batch path needs an f16/bf16 layer with ternary/INT8/INT4 "
+                  "weights (group a multiple of 16), B <= 4, and code rows of >= 128 bytes");
+    void* scratch;
+    // zeroed when first allocated: the split counters start at zero (the pre-pass resets them)
+    if ((rc = scratch_buf(d, s, SC_CC, gemv_cc_scratch_bytes(a), true, &scratch))) return rc;
+    e = launch_gemv_cc(a, L->act_dtype, scratch, s);
   } else if (path == KAN_PATH_SIMT) {
     e = launch_simt(a, L->act_dtype, s);
   } else {
@@ -424,6 +434,12 @@ int kan_forward_plan(const kan_layer* layer, int B, int path, int* info) {
     if (!gemv_supported(a, layer->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED, "forward_plan: the layer does not fit the small-batch path");
     info[3] = (layer->D_out + 127) / 128;
+  } else if (path == KAN_PATH_GEMV_CC) {
+    if (!gemv_cc_supported(a, layer->act_dtype))
+      return fail(KAN_ERR_UNSUPPORTED,
+                  "forward_plan: the layer does not fit the CUDA-core small-batch path");
+    info[2] = gemv_cc_splits(a);
+    info[3] = (layer->D_out + 31) / 32;
   } else if (path != KAN_PATH_SIMT) {
     return fail(KAN_ERR_ARG, "forward_plan: unknown path %d", path);
   }

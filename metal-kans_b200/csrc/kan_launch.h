@@ -58,6 +58,16 @@ cudaError_t launch_tc_pack(const LayerArgs& a, int act_dtype, void* out, cudaStr
 // interleaved in blocks of PAIR_BLOCK (the layout a.fuse_swiglu launches read).
 cudaError_t launch_tc_pack_pair(const LayerArgs& gate, const LayerArgs& up, int act_dtype,
                                 void* out, cudaStream_t s);
+// cuTensorMapEncodeTiled of the driver, looked up once (thread-safe); nullptr if unavailable
+// (kan_tc.cu).
+void* tensor_map_encoder();
+// kan_gemv_cc.cu: small-batch path on the CUDA cores (B <= 4; ternary / INT8 / INT4 weights decoded
+// on chip, integer dot products against a fixed-point basis matrix).  launch_gemv_cc also runs the
+// basis pre-pass; `scratch` holds gemv_cc_scratch_bytes() of device memory, zeroed when allocated.
+bool gemv_cc_supported(const LayerArgs& a, int act_dtype);
+size_t gemv_cc_scratch_bytes(const LayerArgs& a);
+int gemv_cc_splits(const LayerArgs& a);
+cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s);
 // kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
 // from the packed codes into TMEM; no dense copy)
 // launch_gemv also runs the basis pre-pass into `phi` (gemv_phi_bytes() of device scratch).

@@ -3,6 +3,8 @@
 // and the kernel that packs weights into the feature-blocked layout (kan_tc_pack).
 #include <cuda.h>
 
+#include <mutex>
+
 #include "kan_device.cuh"
 #include "kan_launch.h"
 #include "kan_tc_dispatch.h"
@@ -49,20 +51,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-static EncodeTiledFn get_encode() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)p;
-  }
-  return fn;
-}
+static EncodeTiledFn get_encode() { return (EncodeTiledFn)tensor_map_encoder(); }
 
 // 2-D tensor map over the packed [rows][cols] 16-bit matrix, box = 64 columns x box_rows,
 // 128-byte swizzle, zero fill out of range (rows beyond D_out).  cols is a multiple of 64, so the
@@ -106,6 +95,20 @@ static const DispatchFn kDispatch[3][4] = {
     {dispatch_2_0, dispatch_2_1, dispatch_2_2, dispatch_2_3}};
 
 }  // namespace tc
+
+void* tensor_map_encoder() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = p;
+  });
+  return fn;
+}
 
 bool tc_supported(const LayerArgs& a, int act_dtype) {
   if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;

@@ -59,7 +59,7 @@ KAN_F32, KAN_F16, KAN_BF16 = 0, 1, 2
 KAN_CHEBY, KAN_RBF, KAN_BSPLINE, KAN_WAVELET = 0, 1, 2, 3
 KAN_MAP_NONE, KAN_MAP_TANH, KAN_MAP_LAYERNORM = 0, 1, 2
 KAN_W_DENSE, KAN_W_INT8, KAN_W_INT4, KAN_W_TERNARY, KAN_W_INT2 = 0, 1, 2, 3, 4
-KAN_PATH_AUTO, KAN_PATH_SIMT, KAN_PATH_TC, KAN_PATH_GEMV = 0, 1, 2, 3
+KAN_PATH_AUTO, KAN_PATH_SIMT, KAN_PATH_TC, KAN_PATH_GEMV, KAN_PATH_GEMV_CC = 0, 1, 2, 3, 4
 
 # (name, restype, argtypes) of every exported symbol
 SIGNATURES = [

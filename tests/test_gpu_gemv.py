@@ -99,8 +99,17 @@ def test_c5_layer_small_batch(fmt, B):
         attach_packed(l, nm, packed_from_codes(fmt, O._pack2(codes), s, (D, cols), gs, cb))
     l.bfloat16()
     x = rng.uniform(-1, 1, (B, D)).astype(O.act_dtype("bf16"))
+    # the automatic path: the CUDA-core small-batch kernel for ternary weights at B <= 4, this
+    # kernel otherwise
+    import ctypes
+
+    keep = []
+    info = (ctypes.c_int * 6)()
+    mk.get_metal_bridge().kan_forward_plan(ctypes.byref(l._descriptor(keep)), B, 0, info)
+    auto = 4 if (fmt == "ternary" and B <= 4) else GEMV
+    assert info[0] == auto
     y_auto = l.forward(x)
+    np.testing.assert_array_equal(y_auto.view(np.uint16), l.forward(x, path=auto).view(np.uint16))
     y = l.forward(x, path=GEMV)
-    np.testing.assert_array_equal(y_auto.view(np.uint16), y.view(np.uint16))
     err = layer_err(y, l, x, "bf16", "cheby")
     assert err <= TOL["bf16"], f"max rel err {err:.3g}"

@@ -1,0 +1,128 @@
+"""GPU: the CUDA-core small-batch path (B <= 4) for ternary / INT8 / INT4 weights.
+
+The kernel never expands the packed codes: it decodes them on chip into bytes and takes integer
+dot products against a fixed-point copy of the basis values (two signed bytes per value, exact
+for every operand-dtype value of magnitude >= 2^-6), scaling each 16-code sum by its group's
+scale.  Its outputs are compared with the oracle (tolerance of the fp16/bf16 path), with the
+tensor-core path on the same layer, and a second call must be bit-identical (the split-K partials
+are summed in a fixed order).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from kan_cases import TOL, layer_err, make_layer, randomize_bias, set_mode
+from oracle import kan_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CC, TC = 4, 2
+
+
+def _quantize(mk, layer, q, gs):
+    {"ternary": mk.to_ternary, "int8": mk.to_int8, "int4": mk.to_int4}[q](layer, group_size=gs)
+
+
+def _plan(mk, layer, B, path=0):
+    keep = []
+    info = (ctypes.c_int * 6)()
+    mk.get_metal_bridge().kan_forward_plan(ctypes.byref(layer._descriptor(keep)), B, path, info)
+    return list(info)
+
+
+# (format, mode, basis, K, D_in, D_out, B, group, base, bias, input map)
+CASES = [
+    ("ternary", "bf16", "cheby", 9, 1024, 256, 1, 64, True, True, "none"),
+    ("ternary", "bf16", "cheby", 9, 1024, 100, 4, 64, True, True, "tanh"),       # ragged rows
+    ("ternary", "f16", "rbf", 8, 1024, 192, 3, 32, True, False, "layernorm"),
+    ("ternary", "bf16", "bspline", 8, 1024, 160, 2, 128, True, True, "none"),
+    ("ternary", "bf16", "wavelet", 6, 1024, 96, 1, 64, False, True, "none"),
+    ("ternary", "f16", "cheby", 5, 1536, 224, 4, 64, True, True, "none"),
+    ("int8", "bf16", "cheby", 9, 512, 256, 1, 64, True, True, "none"),
+    ("int8", "f16", "rbf", 8, 512, 200, 4, 32, True, True, "layernorm"),
+    ("int8", "bf16", "wavelet", 6, 1024, 128, 2, 128, True, False, "tanh"),
+    ("int4", "bf16", "cheby", 5, 512, 256, 4, 64, True, True, "none"),
+    ("int4", "f16", "bspline", 8, 1024, 96, 1, 32, True, True, "none"),
+    ("int4", "bf16", "cheby", 9, 1024, 130, 3, 128, False, True, "tanh"),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(map(str, c)))
+def test_cc_matches_oracle_and_tc(case):
+    import metal_kans as mk
+
+    fmt, mode, basis, K, d_in, d_out, B, gs, base, bias, imap = case
+    layer = make_layer(basis, d_in, d_out, K, bias=bias, use_base=base, input_map=imap,
+                       seed=B + K + d_out)
+    if bias:
+        randomize_bias(layer)
+    _quantize(mk, layer, fmt, gs)
+    set_mode(layer, mode)
+    assert _plan(mk, layer, B)[0] == CC  # the automatic choice for B <= 4
+    x = np.random.default_rng(d_out).normal(0, 1, (B, d_in)).astype(O.act_dtype(mode))
+    y = layer.forward(x, path=CC)
+    err = layer_err(y, layer, x, mode, basis)
+    assert err <= TOL[mode], f"max rel err {err:.3g}"
+    y_tc = layer.forward(x, path=TC)
+    ref = np.abs(y_tc.astype(np.float64)).max()
+    assert np.abs(y.astype(np.float64) - y_tc.astype(np.float64)).max() <= 2 * TOL[mode] * ref
+    np.testing.assert_array_equal(layer.forward(x, path=CC).view(np.uint16), y.view(np.uint16))
+
+
+@pytest.fixture(scope="module", params=["ternary", "int8", "int4"])
+def c5_layer(request):
+    """BASELINE config 5's layer (4096 -> 4096, T_0..T_8 + base, group 64, bf16) with the
+    format's weights: ternary from the benchmark's codes, INT8/INT4 quantised from N(0, 0.02)."""
+    import metal_kans as mk
+
+    fmt = request.param
+    if fmt == "ternary":
+        import bench
+
+        _, layers = bench.get_spec("c5:ternary:1").build(mk)
+        return fmt, layers[0]
+    np.random.seed(5)
+    l = mk.ChebyKAN(4096, 4096, degree=9, bias=False, use_base=True)
+    rng = np.random.default_rng(5)
+    l.w_cheby = rng.normal(0, 0.02, l.w_cheby.shape).astype(np.float32)
+    l.w_base = rng.normal(0, 0.02, l.w_base.shape).astype(np.float32)
+    _quantize(mk, l, fmt, 64)
+    return fmt, l.bfloat16()
+
+
+@pytest.mark.parametrize("B", [1, 2, 4])
+def test_cc_c5_layer(c5_layer, B):
+    """The C5 layer at B <= 4 on the CUDA-core path (K split over several CTAs per row block,
+    partials summed by the last one): oracle, tensor-core agreement, determinism."""
+    import metal_kans as mk
+
+    fmt, l = c5_layer
+    plan = _plan(mk, l, B)
+    assert plan[0] == CC and plan[2] > 1, plan
+    x = np.random.default_rng(B).uniform(-1, 1, (B, 4096)).astype(O.act_dtype("bf16"))
+    y = l.forward(x)
+    err = layer_err(y, l, x, "bf16", "cheby")
+    assert err <= TOL["bf16"], f"{fmt} B={B}: max rel err {err:.3g}"
+    np.testing.assert_array_equal(l.forward(x, path=CC).view(np.uint16), y.view(np.uint16))
+
+
+def test_cc_rejects_unsupported():
+    import metal_kans as mk
+    from metal_kans.device import KanError
+
+    l = make_layer("cheby", 1024, 256, 9, seed=2)
+    mk.to_ternary(l, group_size=64)
+    l.bfloat16()
+    x = np.zeros((5, 1024), O.act_dtype("bf16"))  # B > 4
+    with pytest.raises(KanError):
+        l.forward(x, path=CC)
+    m = make_layer("cheby", 1024, 256, 9, seed=3)
+    mk.to_int2(m, group_size=64)  # INT2 codebook: the tensor-core small-batch kernel's
+    m.bfloat16()
+    with pytest.raises(KanError):
+        m.forward(x[:2], path=CC)
+    f = make_layer("cheby", 1024, 256, 9, seed=4)
+    mk.to_ternary(f, group_size=64)  # fp32 layers keep the exact path
+    with pytest.raises(KanError):
+        f.forward(np.zeros((2, 1024), np.float32), path=CC)
