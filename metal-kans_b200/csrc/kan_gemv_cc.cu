@@ -72,7 +72,9 @@ struct Params {
   int sbox;                  // floats per row of a scale (and minimum) tile
   int units_w, units_b;      // 16-code units per batch row of the basis matrix, per segment
   int phi_pitch;             // bytes of one batch row of the hi (or lo) matrix
-  int tile_bytes;            // one ring stage: codes, scales (, minima)
+  int ups;                   // 16-code units per stage
+  int tile_bytes;            // one ring stage: codes, scales (, minima), basis slice, unit data
+  int off_phi, off_aux;      // offsets inside a stage of the basis slice and the unit data
   int off_red, off_bar, smem;
   int rowblocks;
   // scratch (device pointers into one buffer)
@@ -307,8 +309,35 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
   if (warp == WARP_TMA) {
     // ------------------------------------------------------------------ weight TMA
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(CODE_TILE + scale_floats * 4 * (AFFINE ? 2 : 1));
-      int issued = 0;
+      const int ups = p.ups, units = p.units_w + p.units_b;
+      // A stage is the weight tiles (independent of the pre-pass, so the first ring's worth is
+      // requested before waiting for it) plus the stage's slice of the basis matrix and unit data
+      // (written by the pre-pass: requested once it has completed).
+      auto stage_bytes = [&](bool seg) {
+        return (uint32_t)(CODE_TILE + scale_floats * 4 * (AFFINE ? 2 : 1) +
+                          B * (2 * ups * 16 + ((AFFINE ? 1 : 0) + (seg ? 1 : 0)) * ups * 4));
+      };
+      auto issue_basis = [&](int i) {
+        const int gst = st0 + i, slot = i % STAGES;
+        const bool seg = gst >= p.stages_w;
+        const int u0 = (seg ? p.units_w + (gst - p.stages_w) * ups : gst * ups);
+        const uint32_t bar = bar_full + 8 * slot;
+        const uint32_t dst = s_base + slot * p.tile_bytes;
+        for (int n = 0; n < B; ++n) {
+          tc::bulk_g2s(dst + p.off_phi + (2 * n) * ups * 16,
+                       p.phi_hi + (size_t)n * p.phi_pitch + (size_t)u0 * 16, ups * 16, bar);
+          tc::bulk_g2s(dst + p.off_phi + (2 * n + 1) * ups * 16,
+                       p.phi_lo + (size_t)n * p.phi_pitch + (size_t)u0 * 16, ups * 16, bar);
+          if (AFFINE)
+            tc::bulk_g2s(dst + p.off_aux + (2 * n) * ups * 4, p.sumphi + (size_t)n * units + u0,
+                         ups * 4, bar);
+          if (seg)
+            tc::bulk_g2s(dst + p.off_aux + (2 * n + 1) * ups * 4,
+                         p.p2b + (size_t)n * p.units_b + (u0 - p.units_w), ups * 4, bar);
+        }
+      };
+      const int first = nmine < STAGES ? nmine : STAGES;
+      int issued = 0, basis_issued = 0;
       for (int i = 0; i < nmine; ++i) {
         const int slot = i % STAGES;
         if (!mbar_wait(bar_empty + 8 * slot, ((uint32_t)(i / STAGES) & 1u) ^ 1u)) {
@@ -322,13 +351,26 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
         const int sis = seg ? gst - p.stages_w : gst;
         const int gal = ((sis * ROW_BYTES * p.cpb) / p.gs) & ~3;
         const uint32_t dst = s_base + slot * p.tile_bytes;
-        mbar_arrive_expect_tx(bar_full + 8 * slot, bytes);
+        mbar_arrive_expect_tx(bar_full + 8 * slot, stage_bytes(seg));
         tma_load_2d(dst, seg ? &tm_cb : &tm_cw, bar_full + 8 * slot, sis * ROW_BYTES, rb * ROWS);
         tma_load_2d(dst + CODE_TILE, seg ? &tm_sb : &tm_sw, bar_full + 8 * slot, gal, rb * ROWS);
         if (AFFINE)
           tma_load_2d(dst + CODE_TILE + scale_floats * 4, seg ? &tm_mb : &tm_mw,
                       bar_full + 8 * slot, gal, rb * ROWS);
         ++issued;
+        if (i + 1 == first) {
+          // the basis matrix is written by the pre-pass kernel this launch depends on
+          asm volatile("griddepcontrol.wait;" ::: "memory");
+          for (; basis_issued <= i; ++basis_issued) issue_basis(basis_issued);
+        } else if (i >= first) {
+          issue_basis(i);
+          basis_issued = i + 1;
+        }
+      }
+      // stages whose basis slice was deferred still get it, so that every issued stage completes
+      if (basis_issued < issued) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (; basis_issued < issued; ++basis_issued) issue_basis(basis_issued);
       }
       // every load issued lands before the CTA may exit (the consumers waited for all of them
       // unless they aborted)
@@ -340,10 +382,8 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
   }
 
   // ------------------------------------------------------------------ compute warps
-  // the basis matrix is written by the pre-pass kernel this launch depends on
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = lane;
-  const int units = p.units_w + p.units_b;
+  const int ups = p.ups;
   float accw[MAXB], accr[MAXB];
 #pragma unroll
   for (int n = 0; n < MAXB; ++n) accw[n] = accr[n] = 0.f;
@@ -362,7 +402,8 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
     const uint8_t* tile = smem + slot * p.tile_bytes;
     const float* stile = reinterpret_cast<const float*>(tile + CODE_TILE) + r * p.sbox;
     const float* mtile = stile + scale_floats;
-    const int ubase = seg ? p.units_w : 0;
+    const uint8_t* ptile = tile + p.off_phi;                                  // [B][hi, lo][ups][16]
+    const float* atile = reinterpret_cast<const float*>(tile + p.off_aux);  // [B][sum, p2b][ups]
 #pragma unroll
     for (int cc = 0; cc < CHUNKS_PER_WARP; ++cc) {
       const int c = warp * CHUNKS_PER_WARP + cc;
@@ -375,7 +416,7 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
         else if (j == 2) decode_unit<FMT, (UPC > 2 ? 2 : 0)>(q, d);
         else decode_unit<FMT, (UPC > 3 ? 3 : 0)>(q, d);
         const int code0 = (sis * ROW_BYTES + c * 16) * p.cpb + j * 16;  // within the segment
-        const int U = ubase + code0 / 16;
+        const int ul = c * UPC + j;                                      // unit within the stage
         const int g = code0 / p.gs - gal;
         float s = stile[g];
         if (!AFFINE) s = Act<MODE>::round(s);  // act(+-s) = +-act(s): the dequantised weight
@@ -383,8 +424,8 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
 #pragma unroll
         for (int n = 0; n < MAXB; ++n) {
           if (n >= B) break;
-          const uint4 h = __ldg(reinterpret_cast<const uint4*>(p.phi_hi + (size_t)n * p.phi_pitch) + U);
-          const uint4 l = __ldg(reinterpret_cast<const uint4*>(p.phi_lo + (size_t)n * p.phi_pitch) + U);
+          const uint4 h = *reinterpret_cast<const uint4*>(ptile + ((2 * n) * ups + ul) * 16);
+          const uint4 l = *reinterpret_cast<const uint4*>(ptile + ((2 * n + 1) * ups + ul) * 16);
           int t;
           if (AFFINE) {
             t = dp4a_us(d[0], h.x, 0);
@@ -410,10 +451,9 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
           if (!seg) {
             accw[n] = fmaf((float)t, s, accw[n]);
           } else {
-            accr[n] = fmaf((float)t, s * __ldg(p.p2b + (size_t)n * p.units_b + (U - p.units_w)),
-                           accr[n]);
+            accr[n] = fmaf((float)t, s * atile[(2 * n + 1) * ups + ul], accr[n]);
           }
-          if (AFFINE) accr[n] = fmaf(mn, __ldg(p.sumphi + (size_t)n * units + U), accr[n]);
+          if (AFFINE) accr[n] = fmaf(mn, atile[(2 * n) * ups + ul], accr[n]);
         }
       }
     }
@@ -447,6 +487,8 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
     if (n < B && row < a.D_out) p.part[((size_t)z * B + n) * a.D_out + row] = v[n];
   __threadfence();
   __syncwarp();
+  // the counters are reset by the pre-pass (long finished: its basis matrix has been consumed)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   int prev = 0;
   if (lane == 0) prev = atomicAdd(p.counters + rb, 1);
   prev = __shfl_sync(0xffffffffu, prev, 0);
@@ -533,8 +575,15 @@ static MainFn main_kernel(int mode, int fmt) {
   return kan_gemv_cc_kernel<MODE_BF16, KAN_W_INT4>;
 }
 
-// Resident CTAs per SM of a main-kernel instance (cached per device and instance).
+static std::atomic<unsigned long long> g_configured[6];  // per device: shared-memory limit set
+
+// Resident CTAs per SM of a main-kernel instance (cached per device and instance); raises the
+// instance's dynamic shared-memory limit on this device first.
 static int occupancy(MainFn k, int ki, int smem) {
+  if (ensure_smem_attr(k, smem, g_configured[ki]) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 1;
+  }
   static int cache[64][6] = {};
   static std::mutex mu;
   int dev = 0;
@@ -573,7 +622,11 @@ static size_t plan(const LayerArgs& a, int act_dtype, Params& p, void* scratch) 
   const int gps = std::max(1, ROW_BYTES * p.cpb / std::max(1, p.gs));  // groups per stage
   p.sbox = (gps + 3) / 4 * 4 + 4;
   const bool affine = p.fmt != KAN_W_TERNARY;
-  p.tile_bytes = CODE_TILE + ROWS * p.sbox * 4 * (affine ? 2 : 1);
+  p.ups = ups;
+  const int Bs = std::max(1, a.B);
+  p.off_phi = CODE_TILE + ROWS * p.sbox * 4 * (affine ? 2 : 1);            // multiple of 128
+  p.off_aux = p.off_phi + Bs * 2 * ups * 16;
+  p.tile_bytes = p.off_aux + Bs * 2 * ups * 4;
   p.tile_bytes = (p.tile_bytes + 1023) / 1024 * 1024;  // 128-byte swizzle: 1 KB aligned stages
   p.off_red = STAGES * p.tile_bytes;
   p.off_bar = p.off_red + NWARPS * MAXB * ROWS * 4;
@@ -700,9 +753,8 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
   if (e != cudaSuccess) return e;
 
   const MainFn kern = main_kernel(mode, fmt);
-  static std::atomic<unsigned long long> configured[6];
   const int ki = (mode == MODE_F16 ? 0 : 3) + (fmt == KAN_W_TERNARY ? 0 : (fmt == KAN_W_INT8 ? 1 : 2));
-  if ((e = ensure_smem_attr(kern, p.smem, configured[ki])) != cudaSuccess) return e;
+  if ((e = ensure_smem_attr(kern, p.smem, g_configured[ki])) != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.rowblocks, (unsigned)p.S, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);

@@ -195,8 +195,208 @@ static cudaError_t launch_simt_mode(const LayerArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// Dense fp32 weights: the CTA's weight panel streamed through a ring of cp.async stages.
+//
+// A CTA computes an 8-row x BN-column tile (BN = 64, or 32 when the grid of 64-wide tiles would
+// not cover the SMs).  K runs in chunks of 64 columns -- the basis segment (W, basis values) then
+// the base segment (W_base, silu values) -- and each chunk of the panel, [BN][64] fp32, is copied
+// by 16-byte cp.async into stage t % 4 three chunks ahead of its use, so the L2 round trips of
+// several chunks overlap each other and the FMAs.  While a chunk's copies are in flight the
+// threads evaluate that chunk's 8 x 64 basis values into its A stage.  The four warps split each
+// chunk's columns (16 each); a lane owns one or two output columns for all 8 rows, reads its
+// weights as float4 (row pitch 68 floats: conflict-free) and the basis values as float4
+// broadcasts, and the warps' partial tiles are summed in warp order at the end.
+// ---------------------------------------------------------------------------------------------
+constexpr int DN_BM = 8;
+constexpr int DN_KC = 64;
+constexpr int DN_PITCH = DN_KC + 4;
+constexpr int DN_STAGES = 4;
+constexpr int DN_THREADS = 128;
+
+template <int BN>
+struct DnSmem {
+  float W[DN_STAGES][BN][DN_PITCH];
+  float A[DN_STAGES][DN_BM][DN_PITCH];
+  float red[DN_THREADS / 32][DN_BM][BN];
+  float mean[DN_BM], rstd[DN_BM];
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+template <int BASIS, int BN>
+__global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a) {
+  using Gen = typename GenFor<BASIS, MODE_F32>::type;
+  extern __shared__ __align__(16) uint8_t dn_raw[];
+  DnSmem<BN>& sm = *reinterpret_cast<DnSmem<BN>*>(dn_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col0 = blockIdx.x * BN, row0 = blockIdx.y * DN_BM;
+  const int Kw = a.D_in * a.K;
+  const int Tw = (Kw + DN_KC - 1) / DN_KC;
+  const int T = Tw + (a.has_base ? (a.D_in + DN_KC - 1) / DN_KC : 0);
+  const float* X = (const float*)a.X;
+  const float* W = (const float*)a.w.data;
+  const float* Wb = (const float*)a.wb.data;
+
+  if (a.input_map == KAN_MAP_LAYERNORM) row_stats<MODE_F32>(a, row0, DN_BM, sm.mean, sm.rstd);
+  __syncthreads();
+
+  // issue the copies of chunk t's weight panel and build its basis tile
+  auto prepare = [&](int t) {
+    const int st = t % DN_STAGES;
+    const bool seg = t >= Tw;
+    const int c0 = (seg ? t - Tw : t) * DN_KC;
+    const int cols = seg ? a.D_in : Kw;
+    const float* M = seg ? Wb : W;
+    for (int q = tid; q < BN * (DN_KC / 4); q += DN_THREADS) {
+      const int n = q / (DN_KC / 4), c = (q % (DN_KC / 4)) * 4;
+      const int row = col0 + n, col = c0 + c;
+      const bool ok = row < a.D_out && col < cols;
+      cp_async16((uint32_t)__cvta_generic_to_shared(&sm.W[st][n][c]),
+                 ok ? (const void*)(M + (size_t)row * cols + col) : (const void*)M, ok ? 16 : 0);
+    }
+    if (!seg) {
+      // (row, feature) items overlapping the chunk; features >= D_in and rows >= B give zeros
+      const int i0 = c0 / a.K, i1 = (c0 + DN_KC - 1) / a.K;
+      const int nf = i1 - i0 + 1;
+      for (int it = tid; it < DN_BM * nf; it += DN_THREADS) {
+        const int r = it / nf, i = i0 + it % nf;
+        const int row = row0 + r;
+        const bool ok = row < a.B && i < a.D_in;
+        Gen g;
+        if (ok) {
+          const float xm = map_input<MODE_F32>(X[(size_t)row * a.D_in + i], a.input_map,
+                                               sm.mean[r], sm.rstd[r]);
+          g.init(xm, i, a);
+        }
+        for (int k = 0; k < a.K; ++k) {
+          const float v = ok ? g.next() : 0.f;
+          const int c = i * a.K + k - c0;
+          if (c >= 0 && c < DN_KC) sm.A[st][r][c] = v;
+        }
+      }
+    } else {
+      for (int it = tid; it < DN_BM * DN_KC; it += DN_THREADS) {
+        const int r = it / DN_KC, c = it % DN_KC;
+        const int row = row0 + r, i = c0 + c;
+        float v = 0.f;
+        if (row < a.B && i < a.D_in)
+          v = silu_value<MODE_F32>(map_input<MODE_F32>(X[(size_t)row * a.D_in + i], a.input_map,
+                                                       sm.mean[r], sm.rstd[r]));
+        sm.A[st][r][c] = v;
+      }
+    }
+  };
+
+  constexpr int NJ = BN / 32;
+  float acc[DN_BM][NJ];
+#pragma unroll
+  for (int r = 0; r < DN_BM; ++r)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) acc[r][j] = 0.f;
+
+#pragma unroll 1
+  for (int t = 0; t < DN_STAGES - 1; ++t) {
+    if (t < T) prepare(t);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+#pragma unroll 1
+  for (int i = 0; i < T; ++i) {
+    if (i + DN_STAGES - 1 < T) prepare(i + DN_STAGES - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // chunk i's copies (group i) have landed; its basis tile was written before the barrier
+    asm volatile("cp.async.wait_group %0;" ::"n"(DN_STAGES - 1) : "memory");
+    __syncthreads();
+    const int st = i % DN_STAGES;
+#pragma unroll
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const int c = warp * 16 + s4 * 4;
+      float4 wv[NJ];
+#pragma unroll
+      for (int j = 0; j < NJ; ++j) wv[j] = *reinterpret_cast<const float4*>(&sm.W[st][lane + 32 * j][c]);
+#pragma unroll
+      for (int r = 0; r < DN_BM; ++r) {
+        const float4 av = *reinterpret_cast<const float4*>(&sm.A[st][r][c]);
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          acc[r][j] = fmaf(av.x, wv[j].x, acc[r][j]);
+          acc[r][j] = fmaf(av.y, wv[j].y, acc[r][j]);
+          acc[r][j] = fmaf(av.z, wv[j].z, acc[r][j]);
+          acc[r][j] = fmaf(av.w, wv[j].w, acc[r][j]);
+        }
+      }
+    }
+    __syncthreads();  // stage st is refilled by the next iteration's prepare()
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+
+#pragma unroll
+  for (int r = 0; r < DN_BM; ++r)
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) sm.red[warp][r][lane + 32 * j] = acc[r][j];
+  __syncthreads();
+  float* Y = (float*)a.Y;
+  const float* bias = (const float*)a.bias;
+  for (int o = tid; o < DN_BM * BN; o += DN_THREADS) {
+    const int r = o / BN, n = o % BN;
+    const int row = row0 + r, col = col0 + n;
+    if (row >= a.B || col >= a.D_out) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < DN_THREADS / 32; ++w) v += sm.red[w][r][n];
+    if (a.has_bias) v += bias[col];
+    Y[(size_t)row * a.D_out + col] = v;
+  }
+}
+
+template <int BN>
+static cudaError_t launch_dense_bn(const LayerArgs& a, cudaStream_t s) {
+  const dim3 grid((a.D_out + BN - 1) / BN, (a.B + DN_BM - 1) / DN_BM);
+  const int smem = (int)sizeof(DnSmem<BN>);
+  static std::atomic<unsigned long long> configured[4];
+  cudaError_t e;
+  switch (BasisOf(a)) {
+    case KAN_CHEBY:
+      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_CHEBY, BN>, smem, configured[0]))) return e;
+      kan_simt_dense_kernel<KAN_CHEBY, BN><<<grid, DN_THREADS, smem, s>>>(a);
+      break;
+    case KAN_RBF:
+      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_RBF, BN>, smem, configured[1]))) return e;
+      kan_simt_dense_kernel<KAN_RBF, BN><<<grid, DN_THREADS, smem, s>>>(a);
+      break;
+    case KAN_BSPLINE:
+      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_BSPLINE, BN>, smem, configured[2])))
+        return e;
+      kan_simt_dense_kernel<KAN_BSPLINE, BN><<<grid, DN_THREADS, smem, s>>>(a);
+      break;
+    default:
+      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_WAVELET, BN>, smem, configured[3])))
+        return e;
+      kan_simt_dense_kernel<KAN_WAVELET, BN><<<grid, DN_THREADS, smem, s>>>(a);
+      break;
+  }
+  return cudaGetLastError();
+}
+
+// The streamed-panel kernel takes dense fp32 layers whose weight rows start on 16-byte
+// boundaries (D_in * K and D_in multiples of 4, aligned base pointers).
+static bool dense_f32_ok(const LayerArgs& a) {
+  auto al = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  if (a.w.format != KAN_W_DENSE || (a.D_in * a.K) % 4 || !al(a.w.data)) return false;
+  if (a.has_base && (a.wb.format != KAN_W_DENSE || a.D_in % 4 || !al(a.wb.data))) return false;
+  return true;
+}
+
 cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s) {
   note_launch();
+  if (act_dtype == KAN_F32 && dense_f32_ok(a)) {
+    const long long wide = (long long)((a.D_out + 63) / 64) * ((a.B + DN_BM - 1) / DN_BM);
+    return wide < 148 ? launch_dense_bn<32>(a, s) : launch_dense_bn<64>(a, s);
+  }
   if (act_dtype == KAN_F32) return launch_simt_mode<MODE_F32>(a, s);
   if (act_dtype == KAN_F16) return launch_simt_mode<MODE_F16>(a, s);
   return launch_simt_mode<MODE_BF16>(a, s);

@@ -270,15 +270,19 @@ def _w64(w, mode):
 
 
 def project(phi64: np.ndarray, W, x_base64, W_base, bias, mode: str,
-            out_round: bool = True) -> np.ndarray:
+            out_round: bool = True, round_weights: bool = True) -> np.ndarray:
     """Y = bias + silu(x) W_base^T + Phi W^T, accumulated in float64 and rounded once.
 
     Stand-in for the two MPS GEMMs of ``metal_kan_bridge.mm:489-523`` (accumulation order and
-    precision of MPS are not published).
+    precision of MPS are not published).  ``round_weights=False`` keeps W and W_base at their
+    fp32 values instead of rounding them to the operand dtype (the engine's CUDA-core small-batch
+    path multiplies by the exact dequantised INT8/INT4 weight).
     """
-    y = phi64 @ _w64(W, mode).T
+    wr = (lambda w: _w64(w, mode)) if round_weights else (
+        lambda w: np.asarray(w).astype(np.float32).astype(np.float64))
+    y = phi64 @ wr(W).T
     if x_base64 is not None:
-        y = y + x_base64 @ _w64(W_base, mode).T
+        y = y + x_base64 @ wr(W_base).T
     if bias is not None:
         y = y + _w64(bias, mode)[None, :]
     if not out_round:
@@ -288,7 +292,8 @@ def project(phi64: np.ndarray, W, x_base64, W_base, bias, mode: str,
 
 def kan_layer(x, basis: str, mode: str, W, W_base=None, bias=None, *, K=None, grid=None,
               inv_den=None, grid_size=None, grid_min=None, inv_h=None, translation=None,
-              inv_scale=None, wavelet_type=0, input_map="none", out_round=True):
+              inv_scale=None, wavelet_type=0, input_map="none", out_round=True,
+              round_weights=True):
     """One KAN layer forward (reference call stack A of the bridge, any basis).
 
     ``x`` is rounded to the activation dtype first (the reference casts x to the weight dtype,
@@ -308,7 +313,8 @@ def kan_layer(x, basis: str, mode: str, W, W_base=None, bias=None, *, K=None, gr
     else:
         raise ValueError(basis)
     xb = silu(xm, mode) if W_base is not None else None
-    return project(phi, W, xb, W_base, bias, mode, out_round=out_round)
+    return project(phi, W, xb, W_base, bias, mode, out_round=out_round,
+                   round_weights=round_weights)
 
 
 def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:

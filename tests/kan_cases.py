@@ -18,12 +18,16 @@ def set_mode(layer, mode):
     return layer
 
 
-def oracle_for_layer(layer, x, mode, basis, out_round=True):
-    """Oracle output for an engine layer object (reads its current weights)."""
+def oracle_for_layer(layer, x, mode, basis, out_round=True, exact_weights=False):
+    """Oracle output for an engine layer object (reads its current weights).  exact_weights:
+    the packed weights' exact fp32 dequantised values, not rounded to the operand dtype."""
     import metal_kans as mk  # noqa: F401
 
     W = np.asarray(getattr(layer, layer.MAIN)).astype(np.float32)
     wb = np.asarray(layer.w_base).astype(np.float32) if layer.has_base else None
+    if exact_weights:
+        W = layer._packed(layer.MAIN).dequantize()
+        wb = layer._packed("w_base").dequantize() if layer.has_base else None
     b = np.asarray(layer.bias).astype(np.float32) if layer.has_bias else None
     kw = {}
     if basis == "rbf":
@@ -35,12 +39,13 @@ def oracle_for_layer(layer, x, mode, basis, out_round=True):
                   inv_scale=np.asarray(layer._inv_scale).astype(np.float32),
                   wavelet_type=layer.wavelet_type)
     return O.kan_layer(x, basis, mode, W, wb, b, K=layer._terms(),
-                       input_map=getattr(layer, "input_map", "none"), out_round=out_round, **kw)
+                       input_map=getattr(layer, "input_map", "none"), out_round=out_round,
+                       round_weights=not exact_weights, **kw)
 
 
-def layer_err(y, layer, x, mode, basis):
+def layer_err(y, layer, x, mode, basis, exact_weights=False):
     """Engine output vs the unrounded oracle, final output rounding allowed (half an ulp)."""
-    ref = oracle_for_layer(layer, x, mode, basis, out_round=False)
+    ref = oracle_for_layer(layer, x, mode, basis, out_round=False, exact_weights=exact_weights)
     return O.max_rel_err_rounded(np.asarray(y).astype(np.float64), ref, mode)
 
 

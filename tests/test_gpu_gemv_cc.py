@@ -3,7 +3,9 @@
 The kernel never expands the packed codes: it decodes them on chip into bytes and takes integer
 dot products against a fixed-point copy of the basis values (two signed bytes per value, exact
 for every operand-dtype value of magnitude >= 2^-6), scaling each 16-code sum by its group's
-scale.  Its outputs are compared with the oracle (tolerance of the fp16/bf16 path), with the
+scale.  Ternary weights come out exactly as the reference's dequantiser rounded to the operand
+dtype; INT8/INT4 weights enter as their exact fp32 dequantised values (q * scale + minimum), so
+those cases are checked against the oracle fed the same exact weights.  Its outputs are compared with the oracle (tolerance of the fp16/bf16 path), with the
 tensor-core path on the same layer, and a second call must be bit-identical (the split-K partials
 are summed in a fixed order).
 """
@@ -62,7 +64,9 @@ def test_cc_matches_oracle_and_tc(case):
     assert _plan(mk, layer, B)[0] == CC  # the automatic choice for B <= 4
     x = np.random.default_rng(d_out).normal(0, 1, (B, d_in)).astype(O.act_dtype(mode))
     y = layer.forward(x, path=CC)
-    err = layer_err(y, layer, x, mode, basis)
+    # INT8/INT4: this path multiplies by the exact fp32 dequantised weight (q * scale + minimum),
+    # not its rounding to the operand dtype; ternary weights are exact either way
+    err = layer_err(y, layer, x, mode, basis, exact_weights=fmt != "ternary")
     assert err <= TOL[mode], f"max rel err {err:.3g}"
     y_tc = layer.forward(x, path=TC)
     ref = np.abs(y_tc.astype(np.float64)).max()
@@ -102,7 +106,7 @@ def test_cc_c5_layer(c5_layer, B):
     assert plan[0] == CC and plan[2] > 1, plan
     x = np.random.default_rng(B).uniform(-1, 1, (B, 4096)).astype(O.act_dtype("bf16"))
     y = l.forward(x)
-    err = layer_err(y, l, x, "bf16", "cheby")
+    err = layer_err(y, l, x, "bf16", "cheby", exact_weights=fmt != "ternary")
     assert err <= TOL["bf16"], f"{fmt} B={B}: max rel err {err:.3g}"
     np.testing.assert_array_equal(l.forward(x, path=CC).view(np.uint16), y.view(np.uint16))
 
