@@ -137,6 +137,37 @@ int metal_kan_forward_int2_cheby(const float* X, const uint32_t* W_packed, const
                                  const float* codebook, const float* bias, float* Y, int B,
                                  int D_in, int D_out, int degree, int group_size, int has_bias);
 
+/* Backward of one fp32 layer, host pointers, synchronous (the reference's training path).
+ * dY [B][D_out], X [B][D_in] (the forward's input), W / Wb the layer's weights; outputs dW
+ * [D_out][D_in*K], dW_base [D_out][D_in] (if has_base), dbias [D_out] (if has_bias), dX
+ * [B][D_in].  Same math as the reference: dW = dY^T Phi, dX = the basis derivatives contracted
+ * with dY W (Chebyshev derivative zero outside [-1, 1]), silu' for the base branch. */
+/* metal_kan_bridge.mm:2715 */
+int metal_kan_cheby_backward(const float* dY, const float* X, const float* W_cheby,
+                             const float* W_base, float* dW_cheby, float* dW_base, float* dbias,
+                             float* dX, int B, int D_in, int D_out, int degree, int has_base,
+                             int has_bias);
+/* metal_kan_bridge.mm:4532 (same results as metal_kan_cheby_backward here: neither materialises
+ * the basis matrix) */
+int metal_kan_cheby_backward_fused(const float* dY, const float* X, const float* W_cheby,
+                                   const float* W_base, float* dW_cheby, float* dW_base,
+                                   float* dbias, float* dX, int B, int D_in, int D_out, int degree,
+                                   int has_base, int has_bias);
+/* metal_kan_bridge.mm:2847 */
+int metal_kan_fastkan_backward(const float* dY, const float* X, const float* W_rbf,
+                               const float* W_base, const float* grid, float* dW_rbf,
+                               float* dW_base, float* dbias, float* dX, int B, int D_in, int D_out,
+                               int num_centers, float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm:3121 */
+int metal_kan_bspline_backward(const float* dY, const float* X, const float* W_spline,
+                               const float* W_base, float* dW_spline, float* dW_base, float* dbias,
+                               float* dX, int B, int D_in, int D_out, int grid_size,
+                               float grid_min, float inv_h, int has_base, int has_bias);
+/* metal_kan_bridge.mm:4877 -- d_gate, d_up of hidden = silu(gate) * up (SiLU argument clamped to
+ * +-20 in the sigmoid, fused_kan.metal:2298-2316) */
+int metal_kan_swiglu_backward(const float* d_hidden, const float* gate, const float* up,
+                              float* d_gate, float* d_up, int n_elems);
+
 /* metal_kan_bridge.mm:1250-1371 -- mean milliseconds per full host-pointer forward (stage +
  * kernel + copy back), after `warmup` untimed calls; negative on error. */
 double benchmark_metal_cheby(const float* X, const float* W_cheby, const float* W_base,
@@ -290,6 +321,17 @@ int kan_gated_forward_pair(const kan_layer* gate, const kan_layer* up, const kan
  * path, which needs no scratch. */
 int kan_gated_forward_noalloc(const kan_layer* gate, const kan_layer* up, const kan_layer* down,
                               const void* X, void* H, void* Y, int B, void* stream);
+
+/* No counterpart in the reference's device API (its backward is the host-pointer functions
+ * above, which call this).  Backward of a dense fp32 layer with raw inputs (Chebyshev, RBF or
+ * B-spline basis) on device pointers: X is the forward's input, dY [B][D_out]; writes dX
+ * [B][D_in], dW [D_out][D_in*K], dWb [D_out][D_in] and dbias [D_out] -- any of them may be NULL
+ * to skip it (dWb / dbias are ignored without a base branch / bias).  Enqueued on `stream`. */
+int kan_backward(const kan_layer* layer, const void* X, const void* dY, void* dX, void* dW,
+                 void* dWb, void* dbias, int B, void* stream);
+/* Elementwise SwiGLU backward on device pointers (fp32, n elements). */
+int kan_swiglu_backward(const void* d_hidden, const void* gate, const void* up, void* d_gate,
+                        void* d_up, long long n, void* stream);
 
 /* Dequantise any weight format to a dense matrix of `out_dtype` ([rows][cols]); the fp32 value
  * is bit-identical to the reference dequantiser, then rounded (RNE) for f16/bf16 outputs. */

@@ -61,7 +61,7 @@ long long pipeline_wait_limit() { return g_wait_limit.load(std::memory_order_rel
 // ------------------------------------------------------------------------------------------
 constexpr int MAX_DEVICES = 16;
 enum Slot { S_X, S_W, S_WB, S_BIAS, S_Y, S_GRID, S_TRANS, S_ISC, S_SC, S_BI, S_CB, S_T0, S_T1,
-            NUM_SLOTS };
+            S_DY, S_DW, S_DWB, S_DBIAS, S_DX, NUM_SLOTS };
 
 struct PendingCopy {
   void* pinned;
@@ -1242,6 +1242,184 @@ double benchmark_metal_wavkan(const float* X, const float* W, const float* Wb, c
   return bench_loop([&] {
     return metal_kan_wavkan_forward(X, W, Wb, tr, isc, bias, Y, B, D_in, D_out, nw, wt, hb, hbi);
   }, warmup, iters);
+}
+
+}  // extern "C"
+
+// ==========================================================================================
+// backward (fp32): device entry points and the reference's host-pointer functions
+// ==========================================================================================
+namespace kan {
+
+static int make_backward_args(const kan_layer* L, const void* X, const void* dY, void* dX,
+                              void* dW, void* dWb, void* dbias, int B, BackwardArgs* a) {
+  if (!L) return fail(KAN_ERR_ARG, "backward: NULL layer");
+  if (B < 0) return fail(KAN_ERR_ARG, "backward: B < 0");
+  if (L->act_dtype != KAN_F32)
+    return fail(KAN_ERR_UNSUPPORTED, "backward: fp32 layers only (the reference trains in fp32)");
+  if (L->w.format != KAN_W_DENSE || !L->w.data || (L->has_base && (L->wb.format != KAN_W_DENSE ||
+                                                                   !L->wb.data)))
+    return fail(KAN_ERR_UNSUPPORTED, "backward: dense weights only");
+  if (L->input_map != KAN_MAP_NONE)
+    return fail(KAN_ERR_UNSUPPORTED, "backward: raw inputs only (no tanh / LayerNorm map)");
+  if (B > 0 && (!X || !dY)) return fail(KAN_ERR_ARG, "backward: NULL X or dY");
+  std::memset(a, 0, sizeof(*a));
+  a->basis = L->basis;
+  a->B = B;
+  a->D_in = L->D_in;
+  a->D_out = L->D_out;
+  a->K = L->K;
+  a->has_base = L->has_base ? 1 : 0;
+  a->grid_size = L->grid_size;
+  a->inv_den = L->inv_den;
+  a->grid_min = L->grid_min;
+  a->inv_h = L->inv_h;
+  a->grid = L->grid;
+  a->X = (const float*)X;
+  a->dY = (const float*)dY;
+  a->W = (const float*)L->w.data;
+  a->Wb = (const float*)L->wb.data;
+  a->dW = (float*)dW;
+  a->dWb = L->has_base ? (float*)dWb : nullptr;
+  a->dbias = (float*)dbias;
+  a->dX = (float*)dX;
+  if (!backward_supported(*a))
+    return fail(KAN_ERR_UNSUPPORTED,
+                "backward: Chebyshev, RBF or B-spline layers with K + has_base <= 64");
+  return KAN_OK;
+}
+
+// Host-pointer backward: stage dY, X and the weights, run, copy the requested gradients back.
+static int run_host_backward(kan_layer L, const float* dY, const float* X, const float* W,
+                             const float* Wb, const float* grid, float* dW, float* dWb,
+                             float* dbias, float* dX, int B) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (B <= 0 || L.D_in <= 0 || L.D_out <= 0 || L.K <= 0 || !dY || !X || !W || !dX)
+    return fail(KAN_ERR_ARG, "backward: bad sizes or NULL dY / X / W / dX");
+  if (L.has_base && !Wb) return fail(KAN_ERR_ARG, "backward: has_base with NULL W_base");
+  const size_t kw = (size_t)L.D_in * L.K;
+  void *ddY, *dXin, *dWt, *dWbt = nullptr, *dG = nullptr, *oW = nullptr, *oWb = nullptr,
+             *oB = nullptr, *oX;
+  if ((rc = stage_in(d, S_DY, dY, (size_t)B * L.D_out * 4, &ddY))) return rc;
+  if ((rc = stage_in(d, S_X, X, (size_t)B * L.D_in * 4, &dXin))) return rc;
+  if ((rc = stage_in(d, S_W, W, (size_t)L.D_out * kw * 4, &dWt))) return rc;
+  if (L.has_base && (rc = stage_in(d, S_WB, Wb, (size_t)L.D_out * L.D_in * 4, &dWbt))) return rc;
+  if (grid && (rc = stage_in(d, S_GRID, grid, (size_t)L.K * 4, &dG))) return rc;
+  if (dW && (rc = slot(d, S_DW, (size_t)L.D_out * kw * 4, &oW))) return rc;
+  if (L.has_base && dWb && (rc = slot(d, S_DWB, (size_t)L.D_out * L.D_in * 4, &oWb))) return rc;
+  if (L.has_bias && dbias && (rc = slot(d, S_DBIAS, (size_t)L.D_out * 4, &oB))) return rc;
+  if ((rc = slot(d, S_DX, (size_t)B * L.D_in * 4, &oX))) return rc;
+  L.w.format = KAN_W_DENSE;
+  L.w.data = dWt;
+  L.wb.format = KAN_W_DENSE;
+  L.wb.data = dWbt;
+  L.grid = (const float*)dG;
+  BackwardArgs a;
+  if ((rc = make_backward_args(&L, dXin, ddY, oX, oW, oWb, oB, B, &a))) return rc;
+  cudaError_t e = launch_backward(a, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "backward launch: %s", cudaGetErrorString(e));
+  if (oW) KAN_CUDA_TRY(cudaMemcpyAsync(dW, oW, (size_t)L.D_out * kw * 4, cudaMemcpyDeviceToHost,
+                                       d->stream));
+  if (oWb) KAN_CUDA_TRY(cudaMemcpyAsync(dWb, oWb, (size_t)L.D_out * L.D_in * 4,
+                                        cudaMemcpyDeviceToHost, d->stream));
+  if (oB) KAN_CUDA_TRY(cudaMemcpyAsync(dbias, oB, (size_t)L.D_out * 4, cudaMemcpyDeviceToHost,
+                                       d->stream));
+  KAN_CUDA_TRY(cudaMemcpyAsync(dX, oX, (size_t)B * L.D_in * 4, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return check_device_error(d);
+}
+
+}  // namespace kan
+
+extern "C" {
+
+int kan_backward(const kan_layer* layer, const void* X, const void* dY, void* dX, void* dW,
+                 void* dWb, void* dbias, int B, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  BackwardArgs a;
+  if ((rc = make_backward_args(layer, X, dY, dX, dW, dWb, layer && layer->has_bias ? dbias : nullptr,
+                               B, &a)))
+    return rc;
+  cudaError_t e = launch_backward(a, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "backward launch: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_swiglu_backward(const void* d_hidden, const void* gate, const void* up, void* d_gate,
+                        void* d_up, long long n, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (!d_hidden || !gate || !up || !d_gate || !d_up)))
+    return fail(KAN_ERR_ARG, "swiglu_backward: bad arguments");
+  cudaError_t e = launch_swiglu_backward((const float*)d_hidden, (const float*)gate,
+                                         (const float*)up, (float*)d_gate, (float*)d_up, n,
+                                         pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu_backward: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int metal_kan_cheby_backward(const float* dY, const float* X, const float* W, const float* Wb,
+                             float* dW, float* dWb, float* dbias, float* dX, int B, int D_in,
+                             int D_out, int degree, int has_base, int has_bias) {
+  return run_host_backward(base_layer(KAN_CHEBY, KAN_F32, D_in, D_out, degree, has_base, has_bias),
+                           dY, X, W, Wb, nullptr, dW, dWb, dbias, dX, B);
+}
+
+int metal_kan_cheby_backward_fused(const float* dY, const float* X, const float* W,
+                                   const float* Wb, float* dW, float* dWb, float* dbias, float* dX,
+                                   int B, int D_in, int D_out, int degree, int has_base,
+                                   int has_bias) {
+  // one implementation: neither backward materialises the basis matrix here
+  return metal_kan_cheby_backward(dY, X, W, Wb, dW, dWb, dbias, dX, B, D_in, D_out, degree,
+                                  has_base, has_bias);
+}
+
+int metal_kan_fastkan_backward(const float* dY, const float* X, const float* W, const float* Wb,
+                               const float* grid, float* dW, float* dWb, float* dbias, float* dX,
+                               int B, int D_in, int D_out, int num_centers, float inv_den,
+                               int has_base, int has_bias) {
+  if (!grid) return fail(KAN_ERR_ARG, "fastkan_backward: NULL grid");
+  kan_layer L = base_layer(KAN_RBF, KAN_F32, D_in, D_out, num_centers, has_base, has_bias);
+  L.inv_den = inv_den;
+  return run_host_backward(L, dY, X, W, Wb, grid, dW, dWb, dbias, dX, B);
+}
+
+int metal_kan_bspline_backward(const float* dY, const float* X, const float* W, const float* Wb,
+                               float* dW, float* dWb, float* dbias, float* dX, int B, int D_in,
+                               int D_out, int grid_size, float grid_min, float inv_h,
+                               int has_base, int has_bias) {
+  kan_layer L = base_layer(KAN_BSPLINE, KAN_F32, D_in, D_out, grid_size + 3, has_base, has_bias);
+  L.grid_size = grid_size;
+  L.grid_min = grid_min;
+  L.inv_h = inv_h;
+  return run_host_backward(L, dY, X, W, Wb, nullptr, dW, dWb, dbias, dX, B);
+}
+
+int metal_kan_swiglu_backward(const float* d_hidden, const float* gate, const float* up,
+                              float* d_gate, float* d_up, int n) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!d_hidden || !gate || !up || !d_gate || !d_up || n <= 0)
+    return fail(KAN_ERR_ARG, "swiglu_backward: bad arguments");
+  void *dh, *g, *u, *dg, *du;
+  if ((rc = stage_in(d, S_DY, d_hidden, (size_t)n * 4, &dh))) return rc;
+  if ((rc = stage_in(d, S_X, gate, (size_t)n * 4, &g))) return rc;
+  if ((rc = stage_in(d, S_W, up, (size_t)n * 4, &u))) return rc;
+  if ((rc = slot(d, S_DW, (size_t)n * 4, &dg))) return rc;
+  if ((rc = slot(d, S_DX, (size_t)n * 4, &du))) return rc;
+  cudaError_t e = launch_swiglu_backward((const float*)dh, (const float*)g, (const float*)u,
+                                         (float*)dg, (float*)du, n, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu_backward: %s", cudaGetErrorString(e));
+  KAN_CUDA_TRY(cudaMemcpyAsync(d_gate, dg, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaMemcpyAsync(d_up, du, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return check_device_error(d);
 }
 
 }  // extern "C"

@@ -36,6 +36,22 @@ struct LayerArgs {
   long long wait_cycles;
 };
 
+// One fp32 layer backward (kan_backward.cu): device pointers; dW / dWb / dbias / dX may be null
+// (not computed).
+struct BackwardArgs {
+  int basis, B, D_in, D_out, K, has_base, grid_size;
+  float inv_den, grid_min, inv_h;
+  const float* grid;  // RBF centres
+  const float* X;     // [B][D_in]
+  const float* dY;    // [B][D_out]
+  const float* W;     // [D_out][D_in * K]
+  const float* Wb;    // [D_out][D_in]
+  float* dW;
+  float* dWb;
+  float* dbias;
+  float* dX;
+};
+
 // Rows of a gate/up pair in the interleaved tensor-core layout: per 256 output columns, 256
 // gate rows then 256 up rows (one wide tile of the tensor-core kernel).
 constexpr int PAIR_BLOCK = 256;

@@ -576,11 +576,14 @@ static MainFn main_kernel(int mode, int fmt) {
 }
 
 static std::atomic<unsigned long long> g_configured[6];  // per device: shared-memory limit set
+// The dynamic shared-memory limit every instance is given (once per device): the CTA maximum,
+// so that a launch of any batch size (the stage size grows with B) stays within it.
+constexpr int SMEM_MAX = 227 * 1024;
 
 // Resident CTAs per SM of a main-kernel instance (cached per device and instance); raises the
 // instance's dynamic shared-memory limit on this device first.
 static int occupancy(MainFn k, int ki, int smem) {
-  if (ensure_smem_attr(k, smem, g_configured[ki]) != cudaSuccess) {
+  if (ensure_smem_attr(k, SMEM_MAX, g_configured[ki]) != cudaSuccess) {
     (void)cudaGetLastError();
     return 1;
   }
@@ -754,7 +757,8 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
 
   const MainFn kern = main_kernel(mode, fmt);
   const int ki = (mode == MODE_F16 ? 0 : 3) + (fmt == KAN_W_TERNARY ? 0 : (fmt == KAN_W_INT8 ? 1 : 2));
-  if ((e = ensure_smem_attr(kern, p.smem, g_configured[ki])) != cudaSuccess) return e;
+  if ((e = ensure_smem_attr(kern, SMEM_MAX, g_configured[ki])) != cudaSuccess) return e;
+  if (p.smem > SMEM_MAX) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.rowblocks, (unsigned)p.S, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);

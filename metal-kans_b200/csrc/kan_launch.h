@@ -12,7 +12,8 @@ namespace kan {
 
 inline int BasisOf(const LayerArgs& a) { return a.basis; }
 
-// Dynamic shared-memory limit of `kern` on the current device, set once per device.
+// Dynamic shared-memory limit of `kern` on the current device, set once per device: callers pass
+// the largest size any launch of `kern` uses (a later, larger request would not be applied).
 // cudaFuncSetAttribute acts on the current device only, so the "done" state is one bit per
 // device in `done` (a static of the caller, one per kernel); the bit is set atomically, and two
 // host threads that race on a device's first launch both set the same attribute, which is
@@ -74,6 +75,11 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
 bool gemv_supported(const LayerArgs& a, int act_dtype);
 size_t gemv_phi_bytes(const LayerArgs& a);
 cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream_t s);
+// kan_backward.cu: fp32 layer backward (Chebyshev, RBF, B-spline bases; raw input)
+bool backward_supported(const BackwardArgs& a);
+cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s);
+cudaError_t launch_swiglu_backward(const float* dh, const float* g, const float* u, float* dg,
+                                   float* du, long long n, cudaStream_t s);
 // kan_misc.cu
 cudaError_t launch_dequantize(const kan_weight& w, int rows, int cols, void* out, int out_dtype,
                               cudaStream_t s);

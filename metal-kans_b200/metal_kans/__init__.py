@@ -23,10 +23,11 @@ from .quantization import (Int2QuantizedWeight, QuantizedWeight, TernaryQuantize
 from .utils import count_parameters, get_model_size
 
 try:
-    from .torch_module import TorchMetalKAN, TorchMetalKANLinear
+    from .torch_module import TorchGatedKAN, TorchMetalKAN, TorchMetalKANLinear
 except ImportError:  # torch is optional for the NumPy API
     TorchMetalKANLinear = None
     TorchMetalKAN = None
+    TorchGatedKAN = None
 
 __version__ = "0.6.0+b200"
 
@@ -38,5 +39,5 @@ __all__ = [
     "QuantizedWeight", "TernaryQuantizedWeight", "Int2QuantizedWeight",
     "quantize", "to_int8", "to_int4", "to_ternary", "to_int2",
     "count_parameters", "get_model_size",
-    "TorchMetalKANLinear", "TorchMetalKAN",
+    "TorchMetalKANLinear", "TorchMetalKAN", "TorchGatedKAN",
 ]

@@ -171,6 +171,9 @@ class KANLayerBase(E.DeviceLayerMixin):
         """Fused CUDA forward: x [..., in_features] -> [..., out_features] in the layer dtype."""
         act = self.dtype
         x2, orig = E.as_activation(x, act, self.in_features)
+        # kept for backward(), as the reference's layers do (cheby_kan.py:109)
+        self.__dict__["_saved_x"] = x2
+        self.__dict__["_saved_shape"] = orig
         B = x2.shape[0]
         y = E.pinned_empty((B, self.out_features), act)
         if B and not path and not D.async_enabled():
@@ -190,11 +193,59 @@ class KANLayerBase(E.DeviceLayerMixin):
 
     __call__ = forward
 
-    def backward(self, *args, **kwargs):
-        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+    # ---- training: fp32 backward like the reference's layers (cheby_kan.py:145-231) --------
+    def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
+        """The bridge's host-pointer backward for this basis (subclasses)."""
+        raise NotImplementedError(f"{type(self).__name__} has no backward in the reference")
+
+    def backward(self, dY: np.ndarray, fused: bool = True) -> np.ndarray:
+        """GPU backward of the last forward: fills ``grad_<weight>``, ``grad_w_base`` and
+        ``grad_bias`` (fp32, overwritten, not accumulated -- as the reference) and returns dX in
+        the shape of the forward's input.  fp32 layers with the raw input only."""
+        x = self.__dict__.get("_saved_x")
+        if x is None:
+            raise RuntimeError("Cannot run backward before forward() has been called.")
+        if self.dtype != np.float32:
+            raise RuntimeError("backward runs on fp32 layers (the reference trains in fp32); "
+                               "call .float() first")
+        if getattr(self, "input_map", "none") not in (None, "none", "clamp"):
+            raise NotImplementedError("backward takes the raw input (no tanh / LayerNorm map)")
+        x = np.ascontiguousarray(x, np.float32)
+        B = x.shape[0]
+        dY = np.ascontiguousarray(np.asarray(dY, np.float32).reshape(B, self.out_features))
+        d = self.__dict__
+        main = getattr(self, self.MAIN)
+        d["grad_" + self.MAIN] = np.zeros(main.shape, np.float32)
+        d["grad_w_base"] = (np.zeros(self.w_base.shape, np.float32) if self.has_base
+                            else np.zeros((1,), np.float32))
+        d["grad_bias"] = (np.zeros(self.bias.shape, np.float32) if self.has_bias
+                          else np.zeros((1,), np.float32))
+        dX = np.empty((B, self.in_features), np.float32)
+        self._backward_call(E.lib(), dY, x, d["grad_" + self.MAIN],
+                            d["grad_w_base"] if self.has_base else None,
+                            d["grad_bias"] if self.has_bias else None, dX, fused)
+        shape = d.get("_saved_shape")
+        return dX.reshape(shape) if shape is not None and len(shape) > 2 else dX
+
+    def zero_grad(self) -> None:
+        """Zeros the stored parameter gradients."""
+        for name in ("grad_" + self.MAIN, "grad_w_base", "grad_bias"):
+            g = self.__dict__.get(name)
+            if g is not None:
+                g.fill(0)
+
+    def parameters(self):
+        """(param, grad) pairs of the trainable arrays (fast_kan.py:80-87)."""
+        d = self.__dict__
+        params = [(getattr(self, self.MAIN), d.get("grad_" + self.MAIN))]
+        if self.has_base and d.get("grad_w_base") is not None:
+            params.append((self.w_base, d["grad_w_base"]))
+        if self.has_bias and d.get("grad_bias") is not None:
+            params.append((self.bias, d["grad_bias"]))
+        return params
 
     def train_step(self, *args, **kwargs):
-        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+        raise NotImplementedError("the fused training step is not built in this engine")
 
     def _benchmark_fallback(self, x, warmup, iters):
         import time

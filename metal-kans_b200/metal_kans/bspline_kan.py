@@ -53,6 +53,14 @@ class BSplineKAN(KANLayerBase):
     def _terms(self) -> int:
         return int(self.grid_size) + 3
 
+    def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
+        P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+        g = np.asarray(self.grid, np.float32)
+        lib.metal_kan_bspline_backward(
+            P(dY), P(x), P(self.w_spline), P(self.w_base) if self.has_base else None, P(dW),
+            P(dWb), P(dbias), P(dX), x.shape[0], self.in_features, self.out_features,
+            self.grid_size, float(g[0]), float(g[1]), self.has_base, self.has_bias)
+
     def _basis_params(self, L, keep):
         g = np.asarray(self.grid, dtype=np.float32)
         L.grid_size = int(self.grid_size)

@@ -52,6 +52,13 @@ class ChebyKAN(KANLayerBase):
     def _terms(self) -> int:
         return int(self.degree)
 
+    def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
+        fn = lib.metal_kan_cheby_backward_fused if fused else lib.metal_kan_cheby_backward
+        P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+        fn(P(dY), P(x), P(self.w_cheby), P(self.w_base) if self.has_base else None, P(dW), P(dWb),
+           P(dbias), P(dX), x.shape[0], self.in_features, self.out_features, self.degree,
+           self.has_base, self.has_bias)
+
     def benchmark(self, x: np.ndarray, warmup: int = 10, iters: int = 50) -> float:
         """Mean milliseconds of one host-pointer forward (cheby_kan.py:233-256 semantics:
         x cast to fp32, timed through ``benchmark_metal_cheby``)."""

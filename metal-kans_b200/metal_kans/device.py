@@ -98,6 +98,13 @@ SIGNATURES = [
     ("kan_forward", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, vp]),
     ("kan_forward_path", i32, [ctypes.POINTER(KanLayer), vp, vp, i32, i32, vp]),
     ("kan_forward_plan", i32, [ctypes.POINTER(KanLayer), i32, i32, ctypes.POINTER(i32)]),
+    ("kan_backward", i32, [ctypes.POINTER(KanLayer), vp, vp, vp, vp, vp, vp, i32, vp]),
+    ("kan_swiglu_backward", i32, [vp, vp, vp, vp, vp, i64, vp]),
+    ("metal_kan_cheby_backward", i32, [vp] * 8 + [i32] * 6),
+    ("metal_kan_cheby_backward_fused", i32, [vp] * 8 + [i32] * 6),
+    ("metal_kan_fastkan_backward", i32, [vp] * 9 + [i32] * 4 + [f32] + [i32] * 2),
+    ("metal_kan_bspline_backward", i32, [vp] * 8 + [i32] * 4 + [f32, f32] + [i32] * 2),
+    ("metal_kan_swiglu_backward", i32, [vp] * 5 + [i32]),
     ("kan_set_wait_limit", i32, [i64]),
     ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),

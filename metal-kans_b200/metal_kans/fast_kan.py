@@ -55,6 +55,14 @@ class FastKAN(KANLayerBase):
                      else np.zeros((1,), dtype=np.float32))
         self._bridge = D.get_metal_bridge()
 
+    def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
+        P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
+        grid = np.ascontiguousarray(self.grid, np.float32)
+        lib.metal_kan_fastkan_backward(
+            P(dY), P(x), P(self.w_rbf), P(self.w_base) if self.has_base else None, P(grid), P(dW),
+            P(dWb), P(dbias), P(dX), x.shape[0], self.in_features, self.out_features,
+            self.num_centers, self.inv_denominator, self.has_base, self.has_bias)
+
     def bfloat16(self):
         # the grid stays fp32 in bf16 mode (basis math is fp32 there)
         from ._engine import BFLOAT16

@@ -109,6 +109,7 @@ class GatedKAN:
         if self.up_kan.dtype != act or self.down_kan.dtype != act:
             raise TypeError("gate/up/down layers must share one dtype")
         x2, orig = E.as_activation(x, act, self.d_model)
+        self.__dict__["_saved_x"] = x2
         B = x2.shape[0]
         y = E.pinned_empty((B, self.d_model), act)
         if B:
@@ -122,8 +123,43 @@ class GatedKAN:
 
     __call__ = forward
 
-    def backward(self, *a, **k):
-        raise NotImplementedError("training (backward) is outside this inference engine")
+    def backward(self, dY: np.ndarray, fused: bool = True) -> np.ndarray:
+        """Backward through down, the SwiGLU gating and gate/up (gated_kan.py:145-219): fills
+        every layer's gradients, returns dX.  fp32 blocks.  The forward runs on the device and
+        keeps only x; gate and up are recomputed here (their saved inputs are x)."""
+        x = self.__dict__.get("_saved_x")
+        if x is None:
+            raise RuntimeError("Cannot run backward before forward() has been called.")
+        if self.gate_kan.dtype != np.float32:
+            raise RuntimeError("backward runs on fp32 blocks; call .float() first")
+        orig = np.shape(dY)
+        dY2 = np.asarray(dY, np.float32).reshape(-1, self.d_model)
+        lib = E.lib()
+        gate = np.ascontiguousarray(self.gate_kan.forward(x), np.float32)
+        up = np.ascontiguousarray(self.up_kan.forward(x), np.float32)
+        hidden = np.empty_like(gate)
+        lib.metal_kan_swiglu_forward(gate.ctypes.data, up.ctypes.data, hidden.ctypes.data,
+                                     gate.size)
+        self.down_kan.forward(hidden)  # the down layer's saved input
+        d_hidden = np.ascontiguousarray(self.down_kan.backward(dY2, fused=fused), np.float32)
+        d_gate = np.empty_like(gate)
+        d_up = np.empty_like(up)
+        lib.metal_kan_swiglu_backward(d_hidden.ctypes.data, gate.ctypes.data, up.ctypes.data,
+                                      d_gate.ctypes.data, d_up.ctypes.data, gate.size)
+        dX = self.gate_kan.backward(d_gate, fused=fused) + self.up_kan.backward(d_up, fused=fused)
+        return dX.reshape(orig[:-1] + (self.d_model,)) if len(orig) > 2 else dX
+
+    def zero_grad(self) -> None:
+        """Zeros stored parameter gradients across all KAN layers."""
+        for l in self._layers():
+            l.zero_grad()
+
+    def get_trainable_params(self):
+        """(param, grad) pairs of the three layers (gated_kan.py:226-237)."""
+        out = []
+        for l in self._layers():
+            out.extend(l.parameters())
+        return out
 
     def to_int8(self, group_size: int = 64) -> "GatedKAN":
         for l in self._layers():

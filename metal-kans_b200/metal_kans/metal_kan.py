@@ -104,6 +104,7 @@ class MetalKAN:
                 x = l(x)
             return x
         x2, orig = E.as_activation(x, act, self.layers_hidden[0])
+        self.__dict__["_saved_x"] = x2  # the layers' own inputs are recomputed by backward()
         B = x2.shape[0]
         out_dim = self.layers_hidden[-1]
         if self.pipeline and len(self.layers) > 1 and act == np.float32:
@@ -132,8 +133,32 @@ class MetalKAN:
     def __call__(self, x: np.ndarray) -> np.ndarray:
         return self.forward(x)
 
-    def backward(self, *a, **k):
-        raise NotImplementedError("training (backward/train_step) is outside this inference engine")
+    def backward(self, dY: np.ndarray) -> np.ndarray:
+        """Backward in reverse layer order (metal_kan.py:175-186), returning dX.  The forward
+        keeps only the net's input on the host; each layer's input is recomputed here, layer by
+        layer, before the reverse sweep fills every layer's gradients."""
+        x = self.__dict__.get("_saved_x")
+        if x is None:
+            raise RuntimeError("Cannot run backward before forward() has been called.")
+        h = x
+        for layer in self.layers:
+            h = layer.forward(h)  # sets the layer's saved input
+        grad = dY
+        for layer in reversed(self.layers):
+            grad = layer.backward(grad)
+        return grad
+
+    def zero_grad(self) -> None:
+        """Zeros gradients across all layers."""
+        for layer in self.layers:
+            layer.zero_grad()
+
+    def parameters(self):
+        """(param, grad) pairs of every layer (metal_kan.py:194-225)."""
+        out = []
+        for layer in self.layers:
+            out.extend((p, g) for p, g in layer.parameters() if g is not None)
+        return out
 
     def __repr__(self) -> str:
         return f"MetalKAN(layers={self.layers_hidden}, basis={self.basis_type!r})"

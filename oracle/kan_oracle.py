@@ -552,6 +552,86 @@ def kan_layer_cpu_f32(x, basis: str, W, W_base=None, bias=None, *, K=None, grid=
 
 
 # --------------------------------------------------------------------------------------------
+# Backward (fp32 training path of the reference)
+# --------------------------------------------------------------------------------------------
+
+def _basis_and_grad64(x, basis, K, grid=None, inv_den=None, grid_size=None, grid_min=None,
+                      inv_h=None):
+    """phi_k(x) and d phi_k / dx in float64, [..., K], with the reference kernels' conventions:
+    Chebyshev on clamp(x, -1, 1) with the basis derivative zero outside [-1, 1]
+    (fused_kan.metal:1679-1741); Gaussian -2 (x - c) inv_den phi (:1745-1783); cubic B-spline
+    pieces differentiated in u and scaled by inv_h on the clamped span/u (:1830-1882)."""
+    x = np.asarray(x, np.float64)
+    if basis == "cheby":
+        xc = np.clip(x, -1.0, 1.0)
+        T = np.zeros(x.shape + (K,))
+        dT = np.zeros(x.shape + (K,))
+        T[..., 0] = 1.0
+        if K > 1:
+            T[..., 1] = xc
+            dT[..., 1] = 1.0
+        for k in range(2, K):
+            T[..., k] = 2.0 * xc * T[..., k - 1] - T[..., k - 2]
+            dT[..., k] = 2.0 * T[..., k - 1] + 2.0 * xc * dT[..., k - 1] - dT[..., k - 2]
+        dT[(x < -1.0) | (x > 1.0)] = 0.0
+        return T, dT
+    if basis == "rbf":
+        d = x[..., None] - np.asarray(grid, np.float64)
+        phi = np.exp(-(d * d) * float(inv_den))
+        return phi, -2.0 * d * float(inv_den) * phi
+    if basis == "bspline":
+        pos = (x - float(grid_min)) * float(inv_h)
+        span = np.clip(np.floor(pos), 0, grid_size - 1).astype(np.int64)
+        u = np.clip(pos - span, 0.0, 1.0)
+        om = 1.0 - u
+        vals = (om ** 3 / 6, (3 * u ** 3 - 6 * u ** 2 + 4) / 6, (-3 * u ** 3 + 3 * u ** 2 + 3 * u + 1) / 6,
+                u ** 3 / 6)
+        ders = (-0.5 * om ** 2, 1.5 * u ** 2 - 2 * u, -1.5 * u ** 2 + u + 0.5, 0.5 * u ** 2)
+        phi = np.zeros(x.shape + (grid_size + 3,))
+        dphi = np.zeros_like(phi)
+        idx = np.indices(x.shape)
+        for j in range(4):
+            phi[tuple(idx) + (span + j,)] = vals[j]
+            dphi[tuple(idx) + (span + j,)] = ders[j] * float(inv_h)
+        return phi, dphi
+    raise ValueError(basis)
+
+
+def kan_layer_backward(x, dY, basis, W, W_base=None, *, K, grid=None, inv_den=None,
+                       grid_size=None, grid_min=None, inv_h=None):
+    """Gradients of one fp32 layer (raw input) in float64: (dX, dW, dW_base, dbias).
+
+    Restates the reference's backward (metal_kan_bridge.mm:2715-2846 and :2847, :3121): Phi and
+    silu(x) re-evaluated, dW = dY^T Phi, dW_base = dY^T silu(x), dbias = sum_b dY,
+    dX = sum_k (dY W)[.., i*K + k] phi_k'(x) + (dY W_base) silu'(x) with
+    silu'(x) = sigma (1 + x (1 - sigma)) of the raw input."""
+    x = np.asarray(x, np.float64)
+    dY = np.asarray(dY, np.float64)
+    B, D_in = x.shape
+    phi, dphi = _basis_and_grad64(x, basis, K, grid, inv_den, grid_size, grid_min, inv_h)
+    W = np.asarray(W, np.float64)
+    dW = dY.T @ phi.reshape(B, D_in * K)
+    dPhi = (dY @ W).reshape(B, D_in, K)
+    dX = (dPhi * dphi).sum(-1)
+    dWb = None
+    if W_base is not None:
+        sig = 1.0 / (1.0 + np.exp(-x))
+        dWb = dY.T @ (x * sig)
+        dX = dX + (dY @ np.asarray(W_base, np.float64)) * (sig * (1.0 + x * (1.0 - sig)))
+    return dX, dW, dWb, dY.sum(0)
+
+
+def swiglu_backward(d_hidden, gate, up):
+    """(d_gate, d_up) of hidden = silu(gate) * up, sigma of the clamped gate
+    (fused_kan.metal:2298-2316), float64."""
+    g = np.asarray(gate, np.float64)
+    u = np.asarray(up, np.float64)
+    dh = np.asarray(d_hidden, np.float64)
+    s = 1.0 / (1.0 + np.exp(-np.clip(g, -20.0, 20.0)))
+    return dh * u * (s * (1.0 + g * (1.0 - s))), dh * g * s
+
+
+# --------------------------------------------------------------------------------------------
 # Error metric
 # --------------------------------------------------------------------------------------------
 

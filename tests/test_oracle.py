@@ -175,3 +175,59 @@ def test_blocks_gated_int4_dequant_matches_reference():
             got = O.dequantize_affine_matrix(BLOCKS[pre + ".qweight"], BLOCKS[pre + ".scales"],
                                              BLOCKS[pre + ".biases"], 4, 64, deq.shape, pin)
             np.testing.assert_array_equal(got, deq)
+
+
+@pytest.mark.parametrize("basis,K", [("cheby", 6), ("rbf", 8), ("bspline", 8)])
+def test_backward_oracle_matches_finite_differences(basis, K):
+    """The backward restatement is the derivative of the forward restatement: central finite
+    differences of the float64 forward (f32 mode evaluates the basis exactly) agree with dX, dW,
+    dW_base and dbias.  Inputs stay away from the Chebyshev clamp and the B-spline knots, where
+    the reference's derivative conventions (zero / one-sided) apply."""
+    rng = np.random.default_rng(11)
+    B, D_in, D_out = 5, 4, 3
+    if basis == "bspline":
+        x = (rng.integers(0, 5, (B, D_in)) + rng.uniform(0.2, 0.8, (B, D_in))) * 0.4 - 1.0
+        kw = dict(grid_size=5, grid_min=-1.0, inv_h=2.5)
+    else:
+        x = rng.uniform(-0.9, 0.9, (B, D_in))
+        kw = dict(grid=np.linspace(-2, 2, K), inv_den=1.5) if basis == "rbf" else {}
+    W = rng.normal(0, 0.3, (D_out, D_in * K))
+    Wb = rng.normal(0, 0.3, (D_out, D_in))
+    bias = rng.normal(0, 0.1, D_out)
+    dY = rng.normal(0, 1, (B, D_out))
+
+    def loss(x_, W_, Wb_, b_):
+        y = O.kan_layer(x_, basis, "f32", W_, Wb_, b_, K=K, out_round=False,
+                        round_weights=False, **kw)
+        return float((np.asarray(y, np.float64) * dY).sum())
+
+    # the f32 mode rounds x to float32: finite differences are taken in float64 on the
+    # restatement evaluated through the same exact-basis path
+    def loss64(x_, W_, Wb_, b_):
+        phi, _ = O._basis_and_grad64(x_, basis, K, **kw)
+        s = 1.0 / (1.0 + np.exp(-x_))
+        y = phi.reshape(B, -1) @ W_.T + (x_ * s) @ Wb_.T + b_
+        return float((y * dY).sum())
+
+    dX, dW, dWb, db = O.kan_layer_backward(x, dY, basis, W, Wb, K=K, **kw)
+    h = 1e-6
+    num = np.zeros_like(x)
+    for idx in np.ndindex(*x.shape):
+        e = np.zeros_like(x)
+        e[idx] = h
+        num[idx] = (loss64(x + e, W, Wb, bias) - loss64(x - e, W, Wb, bias)) / (2 * h)
+    np.testing.assert_allclose(dX, num, rtol=1e-6, atol=1e-8)
+    for arr, grad, args in ((W, dW, 1), (Wb, dWb, 2), (bias, db, 3)):
+        num = np.zeros_like(arr)
+        for idx in np.ndindex(*arr.shape):
+            e = np.zeros_like(arr)
+            e[idx] = h
+            p = [x, W, Wb, bias]
+            m = [x, W, Wb, bias]
+            p[args] = arr + e
+            m[args] = arr - e
+            num[idx] = (loss64(*p) - loss64(*m)) / (2 * h)
+        np.testing.assert_allclose(grad, num, rtol=1e-6, atol=1e-8)
+    # and the float64 restatement of the forward is the f32-mode oracle up to its input rounding
+    assert abs(loss(x, W, Wb, bias) - loss64(x.astype(np.float32).astype(np.float64), W, Wb,
+                                             bias)) < 1e-6
