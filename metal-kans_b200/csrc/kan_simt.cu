@@ -213,11 +213,13 @@ constexpr int DN_KC = 64;
 constexpr int DN_PITCH = DN_KC + 4;
 constexpr int DN_STAGES = 4;
 constexpr int DN_THREADS = 128;
+constexpr int DN_ACHUNKS = 16;  // basis-tile chunks kept: all of them when the layer has <= 16
 
 template <int BN>
 struct DnSmem {
   float W[DN_STAGES][BN][DN_PITCH];
-  float A[DN_STAGES][DN_BM][DN_PITCH];
+  // the whole basis tile (T <= 16 chunks: built once, before the K loop) or a ring of 4 chunks
+  float A[DN_ACHUNKS][DN_BM][DN_PITCH];
   float red[DN_THREADS / 32][DN_BM][BN];
   float mean[DN_BM], rstd[DN_BM];
 };
@@ -243,9 +245,31 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
   const float* Wb = (const float*)a.wb.data;
 
   if (a.input_map == KAN_MAP_LAYERNORM) row_stats<MODE_F32>(a, row0, DN_BM, sm.mean, sm.rstd);
+  // whole basis tile at once when it fits: every input load of the CTA is in flight together
+  // (one memory latency) instead of one dependent round trip per chunk
+  const bool whole_a = T <= DN_ACHUNKS;
+  if (whole_a) {
+    for (int e = tid; e < T * DN_BM * DN_PITCH; e += DN_THREADS) (&sm.A[0][0][0])[e] = 0.f;
+  }
   __syncthreads();
+  if (whole_a) {
+    for (int it = tid; it < DN_BM * a.D_in; it += DN_THREADS) {
+      const int r = it / a.D_in, i = it % a.D_in;
+      const int row = row0 + r;
+      if (row >= a.B) continue;
+      const float xm = map_input<MODE_F32>(X[(size_t)row * a.D_in + i], a.input_map, sm.mean[r],
+                                           sm.rstd[r]);
+      Gen g;
+      g.init(xm, i, a);
+      for (int k = 0; k < a.K; ++k) {
+        const int c = i * a.K + k;
+        sm.A[c / DN_KC][r][c % DN_KC] = g.next();
+      }
+      if (a.has_base) sm.A[Tw + i / DN_KC][r][i % DN_KC] = silu_value<MODE_F32>(xm);
+    }
+  }
 
-  // issue the copies of chunk t's weight panel and build its basis tile
+  // issue the copies of chunk t's weight panel and (ring mode) build its basis tile
   auto prepare = [&](int t) {
     const int st = t % DN_STAGES;
     const bool seg = t >= Tw;
@@ -259,6 +283,7 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
       cp_async16((uint32_t)__cvta_generic_to_shared(&sm.W[st][n][c]),
                  ok ? (const void*)(M + (size_t)row * cols + col) : (const void*)M, ok ? 16 : 0);
     }
+    if (whole_a) return;
     if (!seg) {
       // (row, feature) items overlapping the chunk; features >= D_in and rows >= B give zeros
       const int i0 = c0 / a.K, i1 = (c0 + DN_KC - 1) / a.K;
@@ -312,6 +337,7 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
     asm volatile("cp.async.wait_group %0;" ::"n"(DN_STAGES - 1) : "memory");
     __syncthreads();
     const int st = i % DN_STAGES;
+    const int sa = whole_a ? i : st;  // basis-tile chunk
 #pragma unroll
     for (int s4 = 0; s4 < 4; ++s4) {
       const int c = warp * 16 + s4 * 4;
@@ -320,7 +346,7 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
       for (int j = 0; j < NJ; ++j) wv[j] = *reinterpret_cast<const float4*>(&sm.W[st][lane + 32 * j][c]);
 #pragma unroll
       for (int r = 0; r < DN_BM; ++r) {
-        const float4 av = *reinterpret_cast<const float4*>(&sm.A[st][r][c]);
+        const float4 av = *reinterpret_cast<const float4*>(&sm.A[sa][r][c]);
 #pragma unroll
         for (int j = 0; j < NJ; ++j) {
           acc[r][j] = fmaf(av.x, wv[j].x, acc[r][j]);
