@@ -137,6 +137,34 @@ int metal_kan_forward_int2_cheby(const float* X, const uint32_t* W_packed, const
                                  const float* codebook, const float* bias, float* Y, int B,
                                  int D_in, int D_out, int degree, int group_size, int has_bias);
 
+/* metal_kan_bridge.mm:627 -- ReLUKAN (tent basis), grid [num_grids] */
+int metal_kan_relu_forward(const float* X, const float* W_relu, const float* W_base,
+                           const float* grid, const float* bias, float* Y, int B, int D_in,
+                           int D_out, int num_grids, float inv_h, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2359 (grid is fp16 here, like the reference) */
+int metal_kan_relu_forward_fp16(const uint16_t* X, const uint16_t* W_relu, const uint16_t* W_base,
+                                const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                int D_in, int D_out, int num_grids, float inv_h, int has_base,
+                                int has_bias);
+/* metal_kan_bridge.mm:820 -- FourierKAN, 2 * num_frequencies + 1 bases per feature */
+int metal_kan_fourier_forward(const float* X, const float* W_fourier, const float* W_base,
+                              const float* bias, float* Y, int B, int D_in, int D_out,
+                              int num_frequencies, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2539 */
+int metal_kan_fourier_forward_fp16(const uint16_t* X, const uint16_t* W_fourier,
+                                   const uint16_t* W_base, const uint16_t* bias, uint16_t* Y,
+                                   int B, int D_in, int D_out, int num_frequencies, int has_base,
+                                   int has_bias);
+/* metal_kan_bridge.mm:910 -- JacobiKAN P_k^(alpha, beta), `degree` terms */
+int metal_kan_jacobi_forward(const float* X, const float* W_jacobi, const float* W_base,
+                             const float* bias, float* Y, int B, int D_in, int D_out, int degree,
+                             float alpha, float beta, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2624 */
+int metal_kan_jacobi_forward_fp16(const uint16_t* X, const uint16_t* W_jacobi,
+                                  const uint16_t* W_base, const uint16_t* bias, uint16_t* Y, int B,
+                                  int D_in, int D_out, int degree, float alpha, float beta,
+                                  int has_base, int has_bias);
+
 /* Backward of one fp32 layer, host pointers, synchronous (the reference's training path).
  * dY [B][D_out], X [B][D_in] (the forward's input), W / Wb the layer's weights; outputs dW
  * [D_out][D_in*K], dW_base [D_out][D_in] (if has_base), dbias [D_out] (if has_bias), dX
@@ -158,6 +186,12 @@ int metal_kan_fastkan_backward(const float* dY, const float* X, const float* W_r
                                const float* W_base, const float* grid, float* dW_rbf,
                                float* dW_base, float* dbias, float* dX, int B, int D_in, int D_out,
                                int num_centers, float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm (ReLUKAN backward, bound at device.py:296) -- tent derivative
+ * -sign(x - g) inv_h where the tent is positive (fused_kan.metal:1787-1826) */
+int metal_kan_relu_backward(const float* dY, const float* X, const float* W_relu,
+                            const float* W_base, const float* grid, float* dW_relu,
+                            float* dW_base, float* dbias, float* dX, int B, int D_in, int D_out,
+                            int num_grids, float inv_h, int has_base, int has_bias);
 /* metal_kan_bridge.mm:3121 */
 int metal_kan_bspline_backward(const float* dY, const float* X, const float* W_spline,
                                const float* W_base, float* dW_spline, float* dW_base, float* dbias,
@@ -185,13 +219,33 @@ double benchmark_metal_wavkan(const float* X, const float* W_wav, const float* W
                               const float* translation, const float* inv_scale, const float* bias,
                               float* Y, int B, int D_in, int D_out, int num_wavelets,
                               int wavelet_type, int has_base, int has_bias, int warmup, int iters);
+double benchmark_metal_relu(const float* X, const float* W_relu, const float* W_base,
+                            const float* grid, const float* bias, float* Y, int B, int D_in,
+                            int D_out, int num_grids, float inv_h, int has_base, int has_bias,
+                            int warmup, int iters);
+double benchmark_metal_fourier(const float* X, const float* W_fourier, const float* W_base,
+                               const float* bias, float* Y, int B, int D_in, int D_out,
+                               int num_frequencies, int has_base, int has_bias, int warmup,
+                               int iters);
+double benchmark_metal_jacobi(const float* X, const float* W_jacobi, const float* W_base,
+                              const float* bias, float* Y, int B, int D_in, int D_out, int degree,
+                              float alpha, float beta, int has_base, int has_bias, int warmup,
+                              int iters);
 
 /* ------------------------------------------------------------------------------------------ */
 /* tier 2: device-resident engine (new)                                                       */
 /* ------------------------------------------------------------------------------------------ */
 
 enum kan_dtype { KAN_F32 = 0, KAN_F16 = 1, KAN_BF16 = 2 };
-enum kan_basis { KAN_CHEBY = 0, KAN_RBF = 1, KAN_BSPLINE = 2, KAN_WAVELET = 3 };
+enum kan_basis {
+  KAN_CHEBY = 0,   /* T_k(clamp(x, -1, 1))                                                       */
+  KAN_RBF = 1,     /* exp(-(x - c_k)^2 inv_den), centres in grid[K]                             */
+  KAN_BSPLINE = 2, /* uniform cubic B-spline, G + 3 bases                                       */
+  KAN_WAVELET = 3, /* mexican hat / morlet / DoG of (x - t) inv_s                               */
+  KAN_RELU = 4,    /* tent max(0, 1 - |x - g_k| inv_h), grid points in grid[K]                  */
+  KAN_FOURIER = 5, /* 1, cos(pi x), sin(pi x), cos(2 pi x), ... (K = 2 F + 1)                   */
+  KAN_JACOBI = 6   /* Jacobi P_k^(alpha, beta)(clamp(x, -1, 1))                                 */
+};
 enum kan_input_map { KAN_MAP_NONE = 0, KAN_MAP_TANH = 1, KAN_MAP_LAYERNORM = 2 };
 enum kan_wformat {
   KAN_W_DENSE = 0,   /* act-dtype matrix [rows][cols]                                          */
@@ -200,6 +254,12 @@ enum kan_wformat {
   KAN_W_TERNARY = 3, /* u32 [rows][ceil(cols/16)], fp32 scales [rows][ceil(cols/gs)]           */
   KAN_W_INT2 = 4     /* as ternary + fp32 codebook[4]                                          */
 };
+/* kan_weight.flags.  KAN_WFLAG_TERNARY_NO3: a ternary matrix holds no code 3 (the quantiser
+   writes only 0, 1, 2; the dequantiser maps 3 to 0 like 1).  The CUDA-core small-batch kernel
+   then decodes codes in place as c - 1 (fewer instructions per code); without the flag it uses
+   the exact table decode.  A caller setting the flag on data that holds code 3 gets +1 instead
+   of 0 for those weights. */
+enum kan_wflags { KAN_WFLAG_TERNARY_NO3 = 1 };
 /* Kernel selection for kan_forward_path.  KAN_PATH_AUTO: the CUDA-core small-batch kernel
    (GEMV_CC) when it applies (f16/bf16 layer of any basis and input map, ternary/INT8/INT4 weights,
    B <= 4), else the tensor-core small-batch kernel (GEMV: f16/bf16 Chebyshev layer, ternary/INT2
@@ -219,7 +279,7 @@ typedef struct kan_weight {
   int32_t format;       /* enum kan_wformat */
   int32_t group_size;   /* quantised formats */
   int32_t padded_cols;  /* INT8/INT4: cols rounded up to a multiple of group_size */
-  int32_t reserved;
+  int32_t flags;        /* enum kan_wflags */
   const void* data;     /* device pointer */
   const float* scales;  /* device pointer or NULL */
   const float* biases;  /* device pointer or NULL (INT8/INT4 group minimum) */
@@ -253,6 +313,7 @@ typedef struct kan_layer {
    * pointer, act dtype).  When NULL the tensor-core path packs into library scratch on every
    * call; callers that keep weights resident should pack once and pass the buffer here. */
   const void* tc_weights;
+  float alpha, beta;    /* Jacobi parameters (ReLU uses grid + inv_h) */
 } kan_layer;
 
 /* Tensor-core weight layout: 64-column blocks of whole input features -- F = 64 / KT features

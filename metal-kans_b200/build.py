@@ -29,15 +29,18 @@ NVCC_COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", IN
 CXX_FLAGS = ["-Xcompiler", "-ffp-contract=off"]
 
 # (source, object name, extra defines): the tensor-core kernels are instantiated once per
-# (activation dtype, basis) in separate translation units so that they compile in parallel.
+# (activation dtype, basis), the CUDA-core small-batch kernels once per (activation dtype, batch
+# size), in separate translation units so that they compile in parallel.
 SOURCES = [("kan_abi.cpp", "kan_abi", []), ("kan_misc.cu", "kan_misc", []),
            ("kan_simt.cu", "kan_simt", []), ("kan_tc.cu", "kan_tc", []),
            ("kan_noalloc.cu", "kan_noalloc", []), ("kan_gemv.cu", "kan_gemv", []),
            ("kan_gemv_cc.cu", "kan_gemv_cc", []), ("kan_backward.cu", "kan_backward", [])] + [
     ("kan_tc_inst.cu", f"kan_tc_inst_{m}_{b}", [f"-DKAN_TC_MODE={m}", f"-DKAN_TC_BASIS={b}"])
-    for m in (1, 2) for b in (0, 1, 2, 3)]
+    for m in (1, 2) for b in range(7)] + [
+    ("kan_gemv_cc_inst.cu", f"kan_gemv_cc_inst_{m}_{n}", [f"-DKAN_CC_MODE={m}", f"-DKAN_CC_NB={n}"])
+    for m in (1, 2) for n in range(1, 5)]
 HEADERS = ["kan_device.cuh", "kan_launch.h", "kan_args.h", "kan_tc_kernel.cuh",
-           "kan_tc_dispatch.h"]
+           "kan_tc_dispatch.h", "kan_gemv_cc.cuh"]
 
 
 def nvcc() -> str:

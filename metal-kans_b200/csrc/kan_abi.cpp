@@ -269,9 +269,10 @@ static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceSt
   if (L->K > 64) return fail(KAN_ERR_UNSUPPORTED, "K=%d terms per feature (max 64)", L->K);
   if (L->act_dtype < KAN_F32 || L->act_dtype > KAN_BF16)
     return fail(KAN_ERR_ARG, "act_dtype %d", L->act_dtype);
-  if (L->basis < KAN_CHEBY || L->basis > KAN_WAVELET) return fail(KAN_ERR_ARG, "basis %d", L->basis);
+  if (L->basis < KAN_CHEBY || L->basis > KAN_JACOBI) return fail(KAN_ERR_ARG, "basis %d", L->basis);
   if (B > 0 && (!X || !Y)) return fail(KAN_ERR_ARG, "X or Y is NULL");
-  if (L->basis == KAN_RBF && !L->grid) return fail(KAN_ERR_ARG, "RBF layer without grid");
+  if ((L->basis == KAN_RBF || L->basis == KAN_RELU) && !L->grid)
+    return fail(KAN_ERR_ARG, "RBF / ReLU layer without grid");
   if (L->basis == KAN_WAVELET && (!L->translation || !L->inv_scale))
     return fail(KAN_ERR_ARG, "wavelet layer without translation/inv_scale");
   if (L->basis == KAN_BSPLINE && (L->grid_size <= 0 || L->K != L->grid_size + 3))
@@ -311,6 +312,8 @@ static int make_args(const kan_layer* L, const void* X, void* Y, int B, DeviceSt
   a->err = d->err_word;
   a->tc_weights = L->tc_weights;
   a->wait_cycles = pipeline_wait_limit();
+  a->alpha = L->alpha;
+  a->beta = L->beta;
   return KAN_OK;
 }
 
@@ -942,6 +945,62 @@ int metal_kan_wavkan_forward_fp16(const uint16_t* X, const uint16_t* W, const ui
   return run_host_layer(h);
 }
 
+int metal_kan_relu_forward(const float* X, const float* W, const float* Wb, const float* grid,
+                           const float* bias, float* Y, int B, int D_in, int D_out, int G,
+                           float inv_h, int hb, int hbi) {
+  if (!grid || G <= 0) return fail(KAN_ERR_ARG, "relu: NULL grid");
+  HostLayer h{base_layer(KAN_RELU, KAN_F32, D_in, D_out, G, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.inv_h = inv_h;
+  h.grid.assign(grid, grid + G);
+  return run_host_layer(h);
+}
+
+int metal_kan_relu_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                int D_in, int D_out, int G, float inv_h, int hb, int hbi) {
+  if (!grid || G <= 0) return fail(KAN_ERR_ARG, "relu_fp16: NULL grid");
+  HostLayer h{base_layer(KAN_RELU, KAN_F16, D_in, D_out, G, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.inv_h = inv_h;
+  h.grid = half_to_float(grid, (size_t)G);
+  return run_host_layer(h);
+}
+
+int metal_kan_fourier_forward(const float* X, const float* W, const float* Wb, const float* bias,
+                              float* Y, int B, int D_in, int D_out, int num_freqs, int hb,
+                              int hbi) {
+  if (num_freqs < 0) return fail(KAN_ERR_ARG, "fourier: num_frequencies < 0");
+  HostLayer h{base_layer(KAN_FOURIER, KAN_F32, D_in, D_out, 2 * num_freqs + 1, hb, hbi), X, Y, B,
+              W, Wb, bias};
+  return run_host_layer(h);
+}
+
+int metal_kan_fourier_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                   const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                   int num_freqs, int hb, int hbi) {
+  if (num_freqs < 0) return fail(KAN_ERR_ARG, "fourier_fp16: num_frequencies < 0");
+  HostLayer h{base_layer(KAN_FOURIER, KAN_F16, D_in, D_out, 2 * num_freqs + 1, hb, hbi), X, Y, B,
+              W, Wb, bias};
+  return run_host_layer(h);
+}
+
+int metal_kan_jacobi_forward(const float* X, const float* W, const float* Wb, const float* bias,
+                             float* Y, int B, int D_in, int D_out, int degree, float alpha,
+                             float beta, int hb, int hbi) {
+  HostLayer h{base_layer(KAN_JACOBI, KAN_F32, D_in, D_out, degree, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.alpha = alpha;
+  h.L.beta = beta;
+  return run_host_layer(h);
+}
+
+int metal_kan_jacobi_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                  const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                  int degree, float alpha, float beta, int hb, int hbi) {
+  HostLayer h{base_layer(KAN_JACOBI, KAN_F16, D_in, D_out, degree, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.alpha = alpha;
+  h.L.beta = beta;
+  return run_host_layer(h);
+}
+
 int metal_kan_chain_pipeline_cheby(const float* X, float* Y, int B, int num_layers,
                                    const int* dims, const int* degrees, const float** W,
                                    const float** Wb, const float** bias) {
@@ -1244,6 +1303,29 @@ double benchmark_metal_wavkan(const float* X, const float* W, const float* Wb, c
   }, warmup, iters);
 }
 
+double benchmark_metal_relu(const float* X, const float* W, const float* Wb, const float* grid,
+                            const float* bias, float* Y, int B, int D_in, int D_out, int G,
+                            float inv_h, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_relu_forward(X, W, Wb, grid, bias, Y, B, D_in, D_out, G, inv_h, hb, hbi);
+  }, warmup, iters);
+}
+double benchmark_metal_fourier(const float* X, const float* W, const float* Wb, const float* bias,
+                               float* Y, int B, int D_in, int D_out, int num_freqs, int hb,
+                               int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_fourier_forward(X, W, Wb, bias, Y, B, D_in, D_out, num_freqs, hb, hbi);
+  }, warmup, iters);
+}
+double benchmark_metal_jacobi(const float* X, const float* W, const float* Wb, const float* bias,
+                              float* Y, int B, int D_in, int D_out, int degree, float alpha,
+                              float beta, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_jacobi_forward(X, W, Wb, bias, Y, B, D_in, D_out, degree, alpha, beta, hb,
+                                    hbi);
+  }, warmup, iters);
+}
+
 }  // extern "C"
 
 // ==========================================================================================
@@ -1285,7 +1367,7 @@ static int make_backward_args(const kan_layer* L, const void* X, const void* dY,
   a->dX = (float*)dX;
   if (!backward_supported(*a))
     return fail(KAN_ERR_UNSUPPORTED,
-                "backward: Chebyshev, RBF or B-spline layers with K + has_base <= 64");
+                "backward: Chebyshev, RBF, B-spline or ReLU layers with K + has_base <= 64");
   return KAN_OK;
 }
 
@@ -1386,6 +1468,16 @@ int metal_kan_fastkan_backward(const float* dY, const float* X, const float* W, 
   if (!grid) return fail(KAN_ERR_ARG, "fastkan_backward: NULL grid");
   kan_layer L = base_layer(KAN_RBF, KAN_F32, D_in, D_out, num_centers, has_base, has_bias);
   L.inv_den = inv_den;
+  return run_host_backward(L, dY, X, W, Wb, grid, dW, dWb, dbias, dX, B);
+}
+
+int metal_kan_relu_backward(const float* dY, const float* X, const float* W, const float* Wb,
+                            const float* grid, float* dW, float* dWb, float* dbias, float* dX,
+                            int B, int D_in, int D_out, int num_grids, float inv_h, int has_base,
+                            int has_bias) {
+  if (!grid) return fail(KAN_ERR_ARG, "relu_backward: NULL grid");
+  kan_layer L = base_layer(KAN_RELU, KAN_F32, D_in, D_out, num_grids, has_base, has_bias);
+  L.inv_h = inv_h;
   return run_host_backward(L, dY, X, W, Wb, grid, dW, dWb, dbias, dX, B);
 }
 

@@ -34,6 +34,7 @@ struct LayerArgs {
   // limit of the tensor-core kernel's pipeline waits, in SM clock cycles (waits on copies and
   // MMAs already in flight always use the default of about one second)
   long long wait_cycles;
+  float alpha, beta;  // Jacobi parameters
 };
 
 // One fp32 layer backward (kan_backward.cu): device pointers; dW / dWb / dbias / dX may be null

@@ -22,7 +22,8 @@
 //   * dbias: column sums of dY.
 //
 // Derivatives follow the reference kernels (fused_kan.metal:1679-1882): Chebyshev on the clamped
-// input, with the basis part zero outside [-1, 1]; Gaussian -2 (x - c) inv_den phi; the cubic
+// input, with the basis part zero outside [-1, 1]; Gaussian -2 (x - c) inv_den phi; tents
+// -sign(x - g) inv_h where positive; the cubic
 // B-spline pieces differentiated in u times inv_h on the clamped span; silu'(x) =
 // sigma (1 + x (1 - sigma)) of the raw input.
 #include "kan_device.cuh"
@@ -71,6 +72,14 @@ __device__ __forceinline__ void basis_and_grad(const BackwardArgs& a, float x, f
       const float p = __expf(-(d * d) * a.inv_den);
       if (phi) phi[k] = p;
       if (dphi) dphi[k] = -2.0f * d * a.inv_den * p;
+    }
+  } else if (BASIS == KAN_RELU) {
+    // tent: derivative -sign(x - g) inv_h where the tent is positive (fused_kan.metal:1787-1826)
+    for (int k = 0; k < a.K; ++k) {
+      const float d = x - __ldg(a.grid + k);
+      const float v = 1.0f - fabsf(d) * a.inv_h;
+      if (phi) phi[k] = fmaxf(0.0f, v);
+      if (dphi) dphi[k] = v > 0.0f ? (d > 0.0f ? -a.inv_h : (d < 0.0f ? a.inv_h : 0.0f)) : 0.0f;
     }
   } else {  // cubic B-spline, G + 3 bases
     const float pos = (x - a.grid_min) * a.inv_h;
@@ -255,10 +264,11 @@ __global__ void swiglu_backward_kernel(const float* dh, const float* g, const fl
 }  // namespace bwd
 
 bool backward_supported(const BackwardArgs& a) {
-  if (a.basis != KAN_CHEBY && a.basis != KAN_RBF && a.basis != KAN_BSPLINE) return false;
+  if (a.basis != KAN_CHEBY && a.basis != KAN_RBF && a.basis != KAN_BSPLINE && a.basis != KAN_RELU)
+    return false;
   if (a.K < 1 || a.K + (a.has_base ? 1 : 0) > 64 || a.B < 0 || a.D_in < 1 || a.D_out < 1)
     return false;
-  if (a.basis == KAN_RBF && !a.grid) return false;
+  if ((a.basis == KAN_RBF || a.basis == KAN_RELU) && !a.grid) return false;
   if (a.basis == KAN_BSPLINE && (a.grid_size < 1 || a.K != a.grid_size + 3)) return false;
   return true;
 }
@@ -274,6 +284,7 @@ cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s) {
     note_launch();
     if (a.basis == KAN_CHEBY) bwd_dw_kernel<KAN_CHEBY><<<grid, THREADS, 0, s>>>(a);
     else if (a.basis == KAN_RBF) bwd_dw_kernel<KAN_RBF><<<grid, THREADS, 0, s>>>(a);
+    else if (a.basis == KAN_RELU) bwd_dw_kernel<KAN_RELU><<<grid, THREADS, 0, s>>>(a);
     else bwd_dw_kernel<KAN_BSPLINE><<<grid, THREADS, 0, s>>>(a);
   }
   if (a.dX) {
@@ -281,6 +292,7 @@ cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s) {
     note_launch();
     if (a.basis == KAN_CHEBY) bwd_dx_kernel<KAN_CHEBY><<<grid, THREADS, 0, s>>>(a);
     else if (a.basis == KAN_RBF) bwd_dx_kernel<KAN_RBF><<<grid, THREADS, 0, s>>>(a);
+    else if (a.basis == KAN_RELU) bwd_dx_kernel<KAN_RELU><<<grid, THREADS, 0, s>>>(a);
     else bwd_dx_kernel<KAN_BSPLINE><<<grid, THREADS, 0, s>>>(a);
   }
   if (a.dbias) {

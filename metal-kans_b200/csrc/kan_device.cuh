@@ -218,11 +218,107 @@ struct WaveletGen {
   }
 };
 
+// Tent (ReLUKAN) max(0, 1 - |x - g_k| inv_h) on the raw input (fused_kan.metal:278-303); fp16
+// (:1452-1474): the difference, its magnitude, the product by half(inv_h) and 1 - that in half.
+template <int MODE>
+struct ReluGen {
+  float x, inv_h;
+  const float* grid;
+  int k;
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+    x = xm;
+    grid = a.grid;
+    inv_h = a.inv_h;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    const float g = __ldg(grid + k);
+    ++k;
+    if (MODE == MODE_F16) {
+      const __half d = __habs(__hsub(__float2half_rn(x), __float2half_rn(g)));
+      const __half t = __hmul(d, __float2half_rn(inv_h));
+      return __half2float(__hmax(__float2half_rn(0.0f), __hsub(__float2half_rn(1.0f), t)));
+    }
+    return Act<MODE>::round(fmaxf(0.0f, 1.0f - fabsf(x - g) * inv_h));
+  }
+};
+
+// Fourier (FourierKAN) 1, cos(pi x), sin(pi x), ..., cos(F pi x), sin(F pi x) on the raw input
+// (fused_kan.metal:306-329: angle (f pi) x in fp32); fp16 (:1550-1576): pi x and f (pi x) in
+// half, the cosine and sine of that half angle stored as half.
+template <int MODE>
+struct FourierGen {
+  float x, s;
+  int k;
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs&) {
+    x = xm;
+    k = 0;
+    s = 0.0f;
+  }
+  __device__ __forceinline__ float next() {
+    const int kk = k++;
+    if (kk == 0) return 1.0f;
+    if ((kk & 1) == 0) return s;  // sin of the angle whose cos came just before
+    const int f = (kk + 1) >> 1;
+    float angle;
+    if (MODE == MODE_F16) {
+      const __half pix = __hmul(__float2half_rn(3.14159265358979f), __float2half_rn(x));
+      angle = __half2float(__hmul(__float2half_rn((float)f), pix));
+    } else {
+      angle = ((float)f * 3.14159265358979f) * x;
+    }
+    float c;
+    sincosf(angle, &s, &c);
+    s = Act<MODE>::round(s);
+    return Act<MODE>::round(c);
+  }
+};
+
+// Jacobi P_k^(alpha, beta)(clamp(x, -1, 1)) by the three-term recurrence (fused_kan.metal:331-366;
+// fp16 :1578-1613: the same fp32 recurrence, fma form, half store).
+template <int MODE>
+struct JacobiGen {
+  float x, alpha, beta, p0, p1;
+  int k;
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+    x = fminf(fmaxf(xm, -1.0f), 1.0f);
+    alpha = a.alpha;
+    beta = a.beta;
+    p0 = 1.0f;
+    p1 = 0.0f;
+    k = 0;
+  }
+  __device__ __forceinline__ float next() {
+    const int n = k++;
+    const float ab = alpha + beta;
+    if (n == 0) return Act<MODE>::round(1.0f);
+    if (n == 1) {
+      p1 = 0.5f * (alpha - beta + (ab + 2.0f) * x);
+      return Act<MODE>::round(p1);
+    }
+    const float fn = (float)n;
+    const float an = 2.0f * fn * (fn + ab) * (2.0f * fn + ab - 2.0f);
+    const float bn1 = (2.0f * fn + ab - 1.0f) * (2.0f * fn + ab) * (2.0f * fn + ab - 2.0f);
+    const float bn2 = (2.0f * fn + ab - 1.0f) * (alpha * alpha - beta * beta);
+    const float cn = 2.0f * (fn + alpha - 1.0f) * (fn + beta - 1.0f) * (2.0f * fn + ab);
+    const float p = fmaf(fmaf(bn1, x, bn2), p1, -cn * p0) / an;
+    p0 = p1;
+    p1 = p;
+    return Act<MODE>::round(p);
+  }
+};
+
 template <int BASIS, int MODE> struct GenFor;
 template <int MODE> struct GenFor<KAN_CHEBY, MODE> { using type = ChebyGen<MODE>; };
 template <int MODE> struct GenFor<KAN_RBF, MODE> { using type = RbfGen<MODE>; };
 template <int MODE> struct GenFor<KAN_BSPLINE, MODE> { using type = BsplineGen<MODE>; };
 template <int MODE> struct GenFor<KAN_WAVELET, MODE> { using type = WaveletGen<MODE>; };
+template <int MODE> struct GenFor<KAN_RELU, MODE> { using type = ReluGen<MODE>; };
+template <int MODE> struct GenFor<KAN_FOURIER, MODE> { using type = FourierGen<MODE>; };
+template <int MODE> struct GenFor<KAN_JACOBI, MODE> { using type = JacobiGen<MODE>; };
+
+// Number of basis kinds (kan_basis), for dispatch tables.
+constexpr int NUM_BASES = 7;
 
 // ------------------------------------------------------------------------------------------
 // weight decode: element (row, col) of a kan_weight as the exact fp32 value the reference's

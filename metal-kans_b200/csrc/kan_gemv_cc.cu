@@ -1,509 +1,17 @@
-// kan_gemv_cc.cu -- small-batch path on the CUDA cores (B <= 4): ternary, INT8 and INT4 weights.
-//
-// With a handful of rows the layer is a stream of packed weights: each weight is read once and
-// meets only B basis values.  The tensor cores cannot help there (an MMA needs N >= 16 batch
-// columns, so 15/16 of it would be padding), and expanding the codes to 16-bit operands costs more
-// CUDA-core work than the dot products themselves.  This path keeps the codes packed all the way:
-//
-//   * a pre-pass (one warp per 64 input features, launched as the main kernel's programmatic
-//     dependency) evaluates every basis term phi and silu(x) of the batch with the reference
-//     rounding points (kan_device.cuh), then writes each value in fixed point, v = rint(phi * 2^E)
-//     with |v| <= 8192, as two signed bytes v = 128 * hi + lo (hi in [-64, 64], lo in [-64, 63]).
-//     Basis terms are bounded by 1 in magnitude (Chebyshev on the clamped input, Gaussians,
-//     cubic B-splines, the three wavelets), so their E is 13: every operand-dtype value of
-//     magnitude >= 2^-6 is represented exactly, smaller ones to within 2^-14.  silu(x) is not
-//     bounded, so each 64-feature chunk of the base branch gets its own E from its largest value.
-//   * the main kernel streams [32 rows x 128 code bytes] tiles of the packed weights (and their
-//     per-group scales / minima) with TMA into a 4-stage ring; one lane per output row reads its
-//     16-byte chunks (128-byte swizzle: conflict-free), turns 16 codes into four words of signed
-//     (ternary: -1/0/+1, code 3 -> 0) or unsigned (INT8/INT4: q) bytes with byte permutes and
-//     masks, and accumulates 8 dp4a per batch row (4 against the hi bytes, 4 against the lo bytes)
-//     into an exact int32 sum 128 * H + L.  That sum is converted once per 16 codes and scaled by
-//     the group's fp32 scale (ternary: rounded to the operand dtype, which makes the product the
-//     reference's dequantised weight rounded to the operand dtype, exactly); INT8/INT4 add the
-//     group minimum times the (exact) basis sum of the 16 codes.
-//   * K is split over S CTAs per 32-row block (S from the occupancy, so the whole grid is resident
-//     at once); each split stores its fp32 partials, and the last CTA of a row block to finish
-//     (atomic counter) sums them in split order -- deterministic -- adds the bias, rounds, stores.
-//
-// The basis matrix keeps each 16-code unit in the order the decoder produces bytes in:
-// [0 2 4 6 | 1 3 5 7 | 8 10 12 14 | 9 11 13 15] (perm16 below), the same for all three formats.
-//
-// Every wait is bounded; on expiry the kernel records the device error word, stops consuming,
-// and the TMA warp still waits (full limit) for each load it issued before the CTA exits.
+// kan_gemv_cc.cu -- host side of the small-batch path on the CUDA cores (kan_gemv_cc.cuh): the
+// launch plan, tensor maps, the basis pre-pass instances and the launch.
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
+#include <map>
 #include <mutex>
+#include <tuple>
 
-#include "kan_tc_kernel.cuh"
+#include "kan_gemv_cc.cuh"
 
 namespace kan {
 namespace cc {
-
-using tc::mbar_arrive;
-using tc::mbar_arrive_expect_tx;
-using tc::mbar_init;
-using tc::mbar_wait;
-using tc::mbar_wait_warp;
-using tc::smem_u32;
-using tc::tma_load_2d;
-
-constexpr int ROWS = 32;                      // output rows per CTA: one per lane
-constexpr int ROW_BYTES = 128;                // code bytes of one row per stage
-constexpr int CODE_TILE = ROWS * ROW_BYTES;   // 4 KB
-constexpr int NWARPS = 4;                     // compute warps
-constexpr int CHUNKS_PER_WARP = ROW_BYTES / 16 / NWARPS;
-constexpr int WARP_TMA = NWARPS;
-constexpr int THREADS = (NWARPS + 1) * 32;
-constexpr int STAGES = 4;
-constexpr int MAXB = 4;
-constexpr int PHI_E = 13;                     // fixed-point exponent of the basis terms
-constexpr int PRE_THREADS = 128;              // pre-pass: 4 warps x 64 features
-constexpr int PRE_FEATURES = 256;
-
-struct Params {
-  int fmt;                   // KAN_W_TERNARY / KAN_W_INT8 / KAN_W_INT4
-  int cpb;                   // codes per byte: 4, 1, 2
-  int stages_w, stages_b;    // stages of the basis / base segment
-  int nst;                   // stages_w + stages_b
-  int S;                     // K splits (grid.y)
-  int gs;                    // group size in codes (multiple of 16)
-  int sbox;                  // floats per row of a scale (and minimum) tile
-  int units_w, units_b;      // 16-code units per batch row of the basis matrix, per segment
-  int phi_pitch;             // bytes of one batch row of the hi (or lo) matrix
-  int ups;                   // 16-code units per stage
-  int tile_bytes;            // one ring stage: codes, scales (, minima), basis slice, unit data
-  int off_phi, off_aux;      // offsets inside a stage of the basis slice and the unit data
-  int off_red, off_bar, smem;
-  int rowblocks;
-  // scratch (device pointers into one buffer)
-  int8_t* phi_hi;
-  int8_t* phi_lo;
-  float* sumphi;             // [B][units_w + units_b]: exact basis sum of each unit (INT8/INT4)
-  float* p2b;                // [B][units_b]: 2^-E of each base unit
-  float* part;               // [S][B][D_out] split partials
-  int* counters;             // [rowblocks]
-};
-
-// Position of code j (0..15) of a unit in the decoder's byte order.
-__host__ __device__ __forceinline__ int perm16(int j) {
-  return (j & 8) | ((j & 1) << 2) | ((j & 7) >> 1);
-}
-
-__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-// ---------------------------------------------------------------------------------------------
-// pre-pass: fixed-point basis matrix (hi / lo bytes), unit sums, base-chunk exponents
-// ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void put_fixed(int8_t* hi, int8_t* lo, int code, int q) {
-  const int h = (q + 64) >> 7;
-  const int pos = (code & ~15) | perm16(code & 15);
-  hi[pos] = (int8_t)h;
-  lo[pos] = (int8_t)(q - (h << 7));
-}
-
-// Exponent E <= 13 with max_abs * 2^E <= 8191 (so |rint(v * 2^E)| <= 8191).
-__device__ __forceinline__ int fixed_exponent(float max_abs) {
-  if (!(max_abs > 0.f)) return PHI_E;
-  int e = min(PHI_E, (int)floorf(log2f(8191.f / max_abs)));
-  while (max_abs * exp2f((float)e) > 8191.f) --e;
-  return e;
-}
-
-template <int MODE, int BASIS>
-__global__ void __launch_bounds__(PRE_THREADS) cc_phi_kernel(LayerArgs a, Params p) {
-  // the dependent main kernel may start streaming weights now
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  using T = typename Act<MODE>::T;
-  using Gen = typename GenFor<BASIS, MODE>::type;
-  const int n = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const T* xrow = (const T*)a.X + (size_t)n * a.D_in;
-  int8_t* hi = p.phi_hi + (size_t)n * p.phi_pitch;
-  int8_t* lo = p.phi_lo + (size_t)n * p.phi_pitch;
-  const int units = p.units_w + p.units_b;
-  float* sum = p.sumphi + (size_t)n * units;
-  const int K = a.K, kdim = a.D_in * K;
-  const bool need_sums = p.fmt != KAN_W_TERNARY;
-
-  if (blockIdx.x == 0 && n == 0)
-    for (int i = tid; i < p.rowblocks; i += PRE_THREADS) p.counters[i] = 0;
-
-  // LayerNorm statistics of the row (each CTA of the row computes them; rows are short here)
-  __shared__ float red[PRE_THREADS / 32];
-  float mean = 0.f, rstd = 1.f;
-  if (a.input_map == KAN_MAP_LAYERNORM) {
-    float s = 0.f;
-    for (int i = tid; i < a.D_in; i += PRE_THREADS) s += Act<MODE>::to_f(xrow[i]);
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    s = 0.f;
-    for (int w = 0; w < PRE_THREADS / 32; ++w) s += red[w];
-    mean = s / (float)a.D_in;
-    __syncthreads();
-    float v = 0.f;
-    for (int i = tid; i < a.D_in; i += PRE_THREADS) {
-      const float d = Act<MODE>::to_f(xrow[i]) - mean;
-      v = fmaf(d, d, v);
-    }
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    v = 0.f;
-    for (int w = 0; w < PRE_THREADS / 32; ++w) v += red[w];
-    rstd = rsqrtf(v / (float)a.D_in + a.ln_eps);
-  }
-
-  // padding codes of both segments (whole stages are streamed) are zero; block 0 of the row
-  // clears them every call, since the scratch is shared with other layers
-  if (blockIdx.x == 0) {
-    for (int c = kdim + tid; c < p.units_w * 16; c += PRE_THREADS) put_fixed(hi, lo, c, 0);
-    for (int c = a.D_in + tid; c < p.units_b * 16; c += PRE_THREADS)
-      put_fixed(hi + p.units_w * 16, lo + p.units_w * 16, c, 0);
-    for (int u = (kdim + 15) / 16 + tid; u < p.units_w; u += PRE_THREADS) sum[u] = 0.f;
-    for (int u = (a.D_in + 15) / 16 + tid; u < p.units_b; u += PRE_THREADS) {
-      sum[p.units_w + u] = 0.f;
-      p.p2b[(size_t)n * p.units_b + u] = 0.f;
-    }
-  }
-
-  // this warp's 64 features: basis terms (E = 13) and silu (E of the chunk)
-  const int f0 = blockIdx.x * PRE_FEATURES + warp * 64;
-  float sv[2];
-  float smax = 0.f;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int f = f0 + h * 32 + lane;
-    sv[h] = 0.f;
-    if (f < a.D_in) {
-      const float xm = map_input<MODE>(Act<MODE>::to_f(xrow[f]), a.input_map, mean, rstd);
-      Gen gen;
-      gen.init(xm, f, a);
-      for (int k = 0; k < K; ++k)
-        put_fixed(hi, lo, f * K + k, __float2int_rn(gen.next() * (float)(1 << PHI_E)));
-      if (a.has_base) sv[h] = silu_value<MODE>(xm);
-      smax = fmaxf(smax, fabsf(sv[h]));
-    }
-  }
-  if (a.has_base && f0 < a.D_in) {
-    for (int o = 16; o; o >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
-    const int e = fixed_exponent(smax);
-    const float sc = exp2f((float)e);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int f = f0 + h * 32 + lane;
-      if (f < a.D_in)
-        put_fixed(hi + p.units_w * 16, lo + p.units_w * 16, f, __float2int_rn(sv[h] * sc));
-    }
-    if (lane < 4 && f0 / 16 + lane < p.units_b)
-      p.p2b[(size_t)n * p.units_b + f0 / 16 + lane] = exp2f((float)-e);
-  }
-  if (!need_sums || f0 >= a.D_in) return;
-  // exact basis sum of each unit this warp wrote (its own global writes, ordered by the warp
-  // barrier); codes past the real ones are skipped, whatever the padding holds
-  __syncwarp();
-  const int ulo = f0 * K / 16, uhi = min((f0 + 64) * K, kdim + 15) / 16;
-  for (int u = ulo + lane; u < uhi && u < p.units_w; u += 32) {
-    int acc = 0;
-    for (int j = 0; j < 16; ++j) {
-      const int c = u * 16 + j;
-      if (c >= kdim) break;
-      const int pos = u * 16 + perm16(j);
-      acc += 128 * (int)hi[pos] + (int)lo[pos];
-    }
-    sum[u] = (float)acc * (1.0f / (float)(1 << PHI_E));
-  }
-  if (a.has_base && lane < 4) {
-    const int u = f0 / 16 + lane;
-    if (u < p.units_b && u * 16 < a.D_in) {
-      int acc = 0;
-      for (int j = 0; j < 16 && u * 16 + j < a.D_in; ++j) {
-        const int pos = p.units_w * 16 + u * 16 + perm16(j);
-        acc += 128 * (int)hi[pos] + (int)lo[pos];
-      }
-      sum[p.units_w + u] = (float)acc * p.p2b[(size_t)n * p.units_b + u];
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------------------------
-// main kernel
-// ---------------------------------------------------------------------------------------------
-// 32-bit word i (compile-time) of a 16-byte chunk.
-template <int I>
-__device__ __forceinline__ uint32_t word_of(const uint4& q) {
-  return I == 0 ? q.x : (I == 1 ? q.y : (I == 2 ? q.z : q.w));
-}
-
-// Unit J (16 codes) of a 16-byte chunk -> four words of bytes in perm16 order.
-template <int FMT, int J>
-__device__ __forceinline__ void decode_unit(const uint4& q, uint32_t (&d)[4]) {
-  if (FMT == KAN_W_TERNARY) {
-    // byte value per code: 0 -> -1, 1 -> 0, 2 -> +1, 3 -> 0 (the reference's dequantiser)
-    const uint32_t lut = 0x000100FFu;
-    const uint32_t x = word_of<J>(q);
-    d[0] = __byte_perm(lut, 0u, x & 0x3333u);
-    d[1] = __byte_perm(lut, 0u, (x >> 2) & 0x3333u);
-    d[2] = __byte_perm(lut, 0u, (x >> 16) & 0x3333u);
-    d[3] = __byte_perm(lut, 0u, (x >> 18) & 0x3333u);
-  } else if (FMT == KAN_W_INT4) {
-    // byte = q[2i] | q[2i+1] << 4
-    const uint32_t w0 = word_of<2 * J>(q), w1 = word_of<2 * J + 1>(q);
-    d[0] = w0 & 0x0F0F0F0Fu;
-    d[1] = (w0 >> 4) & 0x0F0F0F0Fu;
-    d[2] = w1 & 0x0F0F0F0Fu;
-    d[3] = (w1 >> 4) & 0x0F0F0F0Fu;
-  } else {
-    d[0] = __byte_perm(q.x, q.y, 0x6420);
-    d[1] = __byte_perm(q.x, q.y, 0x7531);
-    d[2] = __byte_perm(q.z, q.w, 0x6420);
-    d[3] = __byte_perm(q.z, q.w, 0x7531);
-  }
-}
-
-template <int MODE, int FMT>
-__global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
-    const __grid_constant__ CUtensorMap tm_cw, const __grid_constant__ CUtensorMap tm_sw,
-    const __grid_constant__ CUtensorMap tm_mw, const __grid_constant__ CUtensorMap tm_cb,
-    const __grid_constant__ CUtensorMap tm_sb, const __grid_constant__ CUtensorMap tm_mb,
-    LayerArgs a, Params p) {
-  using T = typename Act<MODE>::T;
-  constexpr bool AFFINE = FMT != KAN_W_TERNARY;
-  constexpr int UPC = FMT == KAN_W_TERNARY ? 4 : (FMT == KAN_W_INT4 ? 2 : 1);  // units/chunk
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const uint32_t s_base = smem_u32(smem);
-  const uint32_t bar_full = s_base + p.off_bar;
-  const uint32_t bar_empty = bar_full + STAGES * 8;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + p.off_bar + 2 * STAGES * 8);
-  float* red = reinterpret_cast<float*>(smem + p.off_red);  // [NWARPS][MAXB][ROWS]
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = blockIdx.x, z = blockIdx.y;
-  const int st0 = (int)((long long)p.nst * z / p.S), st1 = (int)((long long)p.nst * (z + 1) / p.S);
-  const int nmine = st1 - st0;
-  const int B = a.B;
-  const int scale_floats = ROWS * p.sbox;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, NWARPS);
-    }
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
-  if (warp == WARP_TMA) {
-    // ------------------------------------------------------------------ weight TMA
-    if (lane == 0) {
-      const int ups = p.ups, units = p.units_w + p.units_b;
-      // A stage is the weight tiles (independent of the pre-pass, so the first ring's worth is
-      // requested before waiting for it) plus the stage's slice of the basis matrix and unit data
-      // (written by the pre-pass: requested once it has completed).
-      auto stage_bytes = [&](bool seg) {
-        return (uint32_t)(CODE_TILE + scale_floats * 4 * (AFFINE ? 2 : 1) +
-                          B * (2 * ups * 16 + ((AFFINE ? 1 : 0) + (seg ? 1 : 0)) * ups * 4));
-      };
-      auto issue_basis = [&](int i) {
-        const int gst = st0 + i, slot = i % STAGES;
-        const bool seg = gst >= p.stages_w;
-        const int u0 = (seg ? p.units_w + (gst - p.stages_w) * ups : gst * ups);
-        const uint32_t bar = bar_full + 8 * slot;
-        const uint32_t dst = s_base + slot * p.tile_bytes;
-        for (int n = 0; n < B; ++n) {
-          tc::bulk_g2s(dst + p.off_phi + (2 * n) * ups * 16,
-                       p.phi_hi + (size_t)n * p.phi_pitch + (size_t)u0 * 16, ups * 16, bar);
-          tc::bulk_g2s(dst + p.off_phi + (2 * n + 1) * ups * 16,
-                       p.phi_lo + (size_t)n * p.phi_pitch + (size_t)u0 * 16, ups * 16, bar);
-          if (AFFINE)
-            tc::bulk_g2s(dst + p.off_aux + (2 * n) * ups * 4, p.sumphi + (size_t)n * units + u0,
-                         ups * 4, bar);
-          if (seg)
-            tc::bulk_g2s(dst + p.off_aux + (2 * n + 1) * ups * 4,
-                         p.p2b + (size_t)n * p.units_b + (u0 - p.units_w), ups * 4, bar);
-        }
-      };
-      const int first = nmine < STAGES ? nmine : STAGES;
-      int issued = 0, basis_issued = 0;
-      for (int i = 0; i < nmine; ++i) {
-        const int slot = i % STAGES;
-        if (!mbar_wait(bar_empty + 8 * slot, ((uint32_t)(i / STAGES) & 1u) ^ 1u)) {
-          raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
-          *abort_flag = 1;
-          break;
-        }
-        if (*abort_flag) break;
-        const int gst = st0 + i;
-        const bool seg = gst >= p.stages_w;
-        const int sis = seg ? gst - p.stages_w : gst;
-        const int gal = ((sis * ROW_BYTES * p.cpb) / p.gs) & ~3;
-        const uint32_t dst = s_base + slot * p.tile_bytes;
-        mbar_arrive_expect_tx(bar_full + 8 * slot, stage_bytes(seg));
-        tma_load_2d(dst, seg ? &tm_cb : &tm_cw, bar_full + 8 * slot, sis * ROW_BYTES, rb * ROWS);
-        tma_load_2d(dst + CODE_TILE, seg ? &tm_sb : &tm_sw, bar_full + 8 * slot, gal, rb * ROWS);
-        if (AFFINE)
-          tma_load_2d(dst + CODE_TILE + scale_floats * 4, seg ? &tm_mb : &tm_mw,
-                      bar_full + 8 * slot, gal, rb * ROWS);
-        ++issued;
-        if (i + 1 == first) {
-          // the basis matrix is written by the pre-pass kernel this launch depends on
-          asm volatile("griddepcontrol.wait;" ::: "memory");
-          for (; basis_issued <= i; ++basis_issued) issue_basis(basis_issued);
-        } else if (i >= first) {
-          issue_basis(i);
-          basis_issued = i + 1;
-        }
-      }
-      // stages whose basis slice was deferred still get it, so that every issued stage completes
-      if (basis_issued < issued) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        for (; basis_issued < issued; ++basis_issued) issue_basis(basis_issued);
-      }
-      // every load issued lands before the CTA may exit (the consumers waited for all of them
-      // unless they aborted)
-      for (int i = issued - 1; i >= 0 && i >= issued - STAGES; --i)
-        (void)mbar_wait(bar_full + 8 * (i % STAGES), (uint32_t)(i / STAGES) & 1u);
-    }
-    __syncwarp();
-    return;
-  }
-
-  // ------------------------------------------------------------------ compute warps
-  const int r = lane;
-  const int ups = p.ups;
-  float accw[MAXB], accr[MAXB];
-#pragma unroll
-  for (int n = 0; n < MAXB; ++n) accw[n] = accr[n] = 0.f;
-
-  for (int i = 0; i < nmine; ++i) {
-    const int slot = i % STAGES;
-    if (!mbar_wait_warp(bar_full + 8 * slot, (uint32_t)(i / STAGES) & 1u)) {
-      raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
-      *abort_flag = 1;
-      break;
-    }
-    const int gst = st0 + i;
-    const bool seg = gst >= p.stages_w;
-    const int sis = seg ? gst - p.stages_w : gst;
-    const int gal = ((sis * ROW_BYTES * p.cpb) / p.gs) & ~3;
-    const uint8_t* tile = smem + slot * p.tile_bytes;
-    const float* stile = reinterpret_cast<const float*>(tile + CODE_TILE) + r * p.sbox;
-    const float* mtile = stile + scale_floats;
-    const uint8_t* ptile = tile + p.off_phi;                                  // [B][hi, lo][ups][16]
-    const float* atile = reinterpret_cast<const float*>(tile + p.off_aux);  // [B][sum, p2b][ups]
-#pragma unroll
-    for (int cc = 0; cc < CHUNKS_PER_WARP; ++cc) {
-      const int c = warp * CHUNKS_PER_WARP + cc;
-      const uint4 q = *reinterpret_cast<const uint4*>(tile + r * ROW_BYTES + ((c ^ (r & 7)) << 4));
-#pragma unroll
-      for (int j = 0; j < UPC; ++j) {
-        uint32_t d[4];
-        if (j == 0) decode_unit<FMT, 0>(q, d);
-        else if (j == 1) decode_unit<FMT, (UPC > 1 ? 1 : 0)>(q, d);
-        else if (j == 2) decode_unit<FMT, (UPC > 2 ? 2 : 0)>(q, d);
-        else decode_unit<FMT, (UPC > 3 ? 3 : 0)>(q, d);
-        const int code0 = (sis * ROW_BYTES + c * 16) * p.cpb + j * 16;  // within the segment
-        const int ul = c * UPC + j;                                      // unit within the stage
-        const int g = code0 / p.gs - gal;
-        float s = stile[g];
-        if (!AFFINE) s = Act<MODE>::round(s);  // act(+-s) = +-act(s): the dequantised weight
-        const float mn = AFFINE ? mtile[g] : 0.f;
-#pragma unroll
-        for (int n = 0; n < MAXB; ++n) {
-          if (n >= B) break;
-          const uint4 h = *reinterpret_cast<const uint4*>(ptile + ((2 * n) * ups + ul) * 16);
-          const uint4 l = *reinterpret_cast<const uint4*>(ptile + ((2 * n + 1) * ups + ul) * 16);
-          int t;
-          if (AFFINE) {
-            t = dp4a_us(d[0], h.x, 0);
-            t = dp4a_us(d[1], h.y, t);
-            t = dp4a_us(d[2], h.z, t);
-            t = dp4a_us(d[3], h.w, t);
-            t <<= 7;
-            t = dp4a_us(d[0], l.x, t);
-            t = dp4a_us(d[1], l.y, t);
-            t = dp4a_us(d[2], l.z, t);
-            t = dp4a_us(d[3], l.w, t);
-          } else {
-            t = dp4a_ss(d[0], h.x, 0);
-            t = dp4a_ss(d[1], h.y, t);
-            t = dp4a_ss(d[2], h.z, t);
-            t = dp4a_ss(d[3], h.w, t);
-            t <<= 7;
-            t = dp4a_ss(d[0], l.x, t);
-            t = dp4a_ss(d[1], l.y, t);
-            t = dp4a_ss(d[2], l.z, t);
-            t = dp4a_ss(d[3], l.w, t);
-          }
-          if (!seg) {
-            accw[n] = fmaf((float)t, s, accw[n]);
-          } else {
-            accr[n] = fmaf((float)t, s * atile[(2 * n + 1) * ups + ul], accr[n]);
-          }
-          if (AFFINE) accr[n] = fmaf(mn, atile[(2 * n) * ups + ul], accr[n]);
-        }
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar_empty + 8 * slot);
-  }
-
-  // ------------------------------------------------------------------ reduction and store
-#pragma unroll
-  for (int n = 0; n < MAXB; ++n)
-    red[(warp * MAXB + n) * ROWS + r] = accw[n] * (1.0f / (float)(1 << PHI_E)) + accr[n];
-  asm volatile("bar.sync 1, %0;" ::"r"(NWARPS * 32) : "memory");
-  if (warp != 0) return;
-  const int row = rb * ROWS + r;
-  float v[MAXB];
-#pragma unroll
-  for (int n = 0; n < MAXB; ++n) {
-    v[n] = 0.f;
-    for (int w = 0; w < NWARPS; ++w) v[n] += red[(w * MAXB + n) * ROWS + r];
-  }
-  T* Y = (T*)a.Y;
-  const float b = (a.has_bias && row < a.D_out) ? Act<MODE>::to_f(((const T*)a.bias)[row]) : 0.f;
-  if (p.S == 1) {
-#pragma unroll
-    for (int n = 0; n < MAXB; ++n)
-      if (n < B && row < a.D_out) Y[(size_t)n * a.D_out + row] = Act<MODE>::from_f(v[n] + b);
-    return;
-  }
-#pragma unroll
-  for (int n = 0; n < MAXB; ++n)
-    if (n < B && row < a.D_out) p.part[((size_t)z * B + n) * a.D_out + row] = v[n];
-  __threadfence();
-  __syncwarp();
-  // the counters are reset by the pre-pass (long finished: its basis matrix has been consumed)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  int prev = 0;
-  if (lane == 0) prev = atomicAdd(p.counters + rb, 1);
-  prev = __shfl_sync(0xffffffffu, prev, 0);
-  if (prev != p.S - 1) return;
-  // the last split of this row block: sum the partials in split order (deterministic)
-  __threadfence();
-  if (row < a.D_out) {
-    for (int n = 0; n < B; ++n) {
-      float sum = 0.f;
-      for (int zz = 0; zz < p.S; ++zz) sum += __ldcg(p.part + ((size_t)zz * B + n) * a.D_out + row);
-      Y[(size_t)n * a.D_out + row] = Act<MODE>::from_f(sum + b);
-    }
-  }
-  if (lane == 0) p.counters[rb] = 0;
-}
 
 // ---------------------------------------------------------------------------------------------
 // host side
@@ -561,50 +69,68 @@ static int sm_count() {
   return n[dev];
 }
 
-using MainFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
-                        const CUtensorMap, const CUtensorMap, const CUtensorMap, LayerArgs,
-                        Params);
-static MainFn main_kernel(int mode, int fmt) {
+// The main-kernel instance for a launch (ternary flags and flush width from the plan).
+static MainFn main_kernel(int mode, int B, int fmt, bool fast, int fu) {
   if (mode == MODE_F16) {
-    if (fmt == KAN_W_TERNARY) return kan_gemv_cc_kernel<MODE_F16, KAN_W_TERNARY>;
-    if (fmt == KAN_W_INT8) return kan_gemv_cc_kernel<MODE_F16, KAN_W_INT8>;
-    return kan_gemv_cc_kernel<MODE_F16, KAN_W_INT4>;
+    switch (B) {
+      case 1: return select_main<MODE_F16, 1>(fmt, fast, fu);
+      case 2: return select_main<MODE_F16, 2>(fmt, fast, fu);
+      case 3: return select_main<MODE_F16, 3>(fmt, fast, fu);
+      default: return select_main<MODE_F16, 4>(fmt, fast, fu);
+    }
   }
-  if (fmt == KAN_W_TERNARY) return kan_gemv_cc_kernel<MODE_BF16, KAN_W_TERNARY>;
-  if (fmt == KAN_W_INT8) return kan_gemv_cc_kernel<MODE_BF16, KAN_W_INT8>;
-  return kan_gemv_cc_kernel<MODE_BF16, KAN_W_INT4>;
+  switch (B) {
+    case 1: return select_main<MODE_BF16, 1>(fmt, fast, fu);
+    case 2: return select_main<MODE_BF16, 2>(fmt, fast, fu);
+    case 3: return select_main<MODE_BF16, 3>(fmt, fast, fu);
+    default: return select_main<MODE_BF16, 4>(fmt, fast, fu);
+  }
 }
 
-static std::atomic<unsigned long long> g_configured[6];  // per device: shared-memory limit set
 // The dynamic shared-memory limit every instance is given (once per device): the CTA maximum,
-// so that a launch of any batch size (the stage size grows with B) stays within it.
+// so that a launch of any stage size stays within it.
 constexpr int SMEM_MAX = 227 * 1024;
 
-// Resident CTAs per SM of a main-kernel instance (cached per device and instance); raises the
-// instance's dynamic shared-memory limit on this device first.
-static int occupancy(MainFn k, int ki, int smem) {
-  if (ensure_smem_attr(k, SMEM_MAX, g_configured[ki]) != cudaSuccess) {
+// Per instance and device: the shared-memory limit has been raised (bit per device).
+static std::atomic<unsigned long long>& configured(MainFn k) {
+  static std::mutex mu;
+  static std::map<MainFn, std::atomic<unsigned long long>*> m;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = m.find(k);
+  if (it == m.end()) it = m.emplace(k, new std::atomic<unsigned long long>(0)).first;
+  return *it->second;
+}
+
+// Resident CTAs per SM of a main-kernel instance at `smem` bytes (cached per device, instance
+// and size); raises the instance's dynamic shared-memory limit on this device first.
+static int occupancy(MainFn k, int smem) {
+  if (ensure_smem_attr(k, SMEM_MAX, configured(k)) != cudaSuccess) {
     (void)cudaGetLastError();
     return 1;
   }
-  static int cache[64][6] = {};
   static std::mutex mu;
+  static std::map<std::tuple<int, MainFn, int>, int> cache;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
   std::lock_guard<std::mutex> lk(mu);
-  if (!cache[dev][ki]) {
-    int v = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, THREADS, smem) != cudaSuccess ||
-        v <= 0) {
-      (void)cudaGetLastError();
-      v = 1;
-    }
-    cache[dev][ki] = v;
+  const auto key = std::make_tuple(dev, k, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int v = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, THREADS, smem) != cudaSuccess ||
+      v <= 0) {
+    (void)cudaGetLastError();
+    v = 1;
   }
-  return cache[dev][ki];
+  cache.emplace(key, v);
+  return v;
 }
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Floats per row of the scale tile of a segment with `groups` groups per row: the groups one
+// stage touches, 4-aligned at both ends, at most the whole row.
+static int scale_box(int gps, int groups) { return std::min((gps + 3) / 4 * 4 + 4, groups); }
 
 // The launch plan; `scratch` (may be null) fills the scratch pointers.  Returns the scratch
 // bytes needed.
@@ -612,7 +138,13 @@ static size_t plan(const LayerArgs& a, int act_dtype, Params& p, void* scratch) 
   p = Params{};
   p.fmt = a.w.format;
   p.cpb = p.fmt == KAN_W_TERNARY ? 4 : (p.fmt == KAN_W_INT4 ? 2 : 1);
+  p.fast = p.fmt == KAN_W_TERNARY && (a.w.flags & KAN_WFLAG_TERNARY_NO3) &&
+           (!a.has_base || (a.wb.flags & KAN_WFLAG_TERNARY_NO3));
   p.gs = a.w.group_size;
+  p.lg = 0;
+  while ((16 << p.lg) < p.gs) ++p.lg;
+  const int upc = p.cpb;                       // 16-code units per 16-byte chunk
+  p.fu = std::min(upc, 1 << p.lg);             // a flush never crosses a group or a chunk
   const RowShape rw = row_shape(a.w, a.D_in * a.K);
   const RowShape rbs = a.has_base ? row_shape(a.wb, a.D_in) : RowShape{0, 0};
   p.stages_w = (int)((rw.bytes + ROW_BYTES - 1) / ROW_BYTES);
@@ -623,11 +155,15 @@ static size_t plan(const LayerArgs& a, int act_dtype, Params& p, void* scratch) 
   p.units_b = p.stages_b * ups;
   p.phi_pitch = (p.units_w + p.units_b) * 16;
   const int gps = std::max(1, ROW_BYTES * p.cpb / std::max(1, p.gs));  // groups per stage
-  p.sbox = (gps + 3) / 4 * 4 + 4;
+  p.groups_w = rw.groups;
+  p.groups_b = rbs.groups;
+  p.sbox_w = scale_box(gps, rw.groups);
+  p.sbox_b = a.has_base ? scale_box(gps, rbs.groups) : 4;
+  p.sbox_max = std::max(p.sbox_w, p.sbox_b);
   const bool affine = p.fmt != KAN_W_TERNARY;
   p.ups = ups;
-  const int Bs = std::max(1, a.B);
-  p.off_phi = CODE_TILE + ROWS * p.sbox * 4 * (affine ? 2 : 1);            // multiple of 128
+  const int Bs = std::min(MAXB, std::max(1, a.B));
+  p.off_phi = CODE_TILE + ROWS * p.sbox_max * 4 * (affine ? 2 : 1);        // multiple of 512
   p.off_aux = p.off_phi + Bs * 2 * ups * 16;
   p.tile_bytes = p.off_aux + Bs * 2 * ups * 4;
   p.tile_bytes = (p.tile_bytes + 1023) / 1024 * 1024;  // 128-byte swizzle: 1 KB aligned stages
@@ -636,8 +172,7 @@ static size_t plan(const LayerArgs& a, int act_dtype, Params& p, void* scratch) 
   p.smem = p.off_bar + 2 * STAGES * 8 + 16 + 1024;
   p.rowblocks = (a.D_out + ROWS - 1) / ROWS;
   const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;
-  const int ki = (mode == MODE_F16 ? 0 : 3) + (p.fmt == KAN_W_TERNARY ? 0 : (p.fmt == KAN_W_INT8 ? 1 : 2));
-  const int occ = occupancy(main_kernel(mode, p.fmt), ki, p.smem);
+  const int occ = occupancy(main_kernel(mode, Bs, p.fmt, p.fast != 0, p.fu), p.smem);
   // as many K splits as keep the whole grid resident at once (one wave), at least 2 stages each
   int S = std::max(1, sm_count() * occ / std::max(1, p.rowblocks));
   S = std::min(S, std::max(1, p.nst / 2));
@@ -674,16 +209,17 @@ bool gemv_cc_supported(const LayerArgs& a, int act_dtype) {
   using namespace cc;
   if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
   if (a.B < 1 || a.B > MAXB || a.D_in < 1 || a.D_out < 1 || a.K < 1) return false;
+  // the fixed-point basis matrix needs |phi| <= 1: every basis but Jacobi (whose polynomials
+  // exceed 1 for alpha or beta > 0)
+  if (a.basis == KAN_JACOBI) return false;
   const int fmt = a.w.format;
   if (fmt != KAN_W_TERNARY && fmt != KAN_W_INT8 && fmt != KAN_W_INT4) return false;
   const int gs = a.w.group_size;
-  if (gs < 16 || gs % 16 || gs > 4096) return false;
+  if (gs < 16 || (gs & (gs - 1)) || gs > 4096) return false;  // group index by shift
   if (a.has_base && (a.wb.format != fmt || a.wb.group_size != gs)) return false;
-  // TMA: rows of 16-byte multiples, at least one full stage and one scale tile wide
-  const int cpb = fmt == KAN_W_TERNARY ? 4 : (fmt == KAN_W_INT4 ? 2 : 1);
-  const int sbox = (std::max(1, ROW_BYTES * cpb / gs) + 3) / 4 * 4 + 4;
+  // TMA: rows of 16-byte multiples at least one box wide, whole 4-float groups of scales
   auto fits = [&](const RowShape& s) {
-    return s.bytes % 16 == 0 && s.bytes >= ROW_BYTES && s.groups % 4 == 0 && s.groups >= sbox;
+    return s.bytes % 16 == 0 && s.bytes >= BOX_BYTES && s.groups % 4 == 0 && s.groups >= 4;
   };
   if (!fits(row_shape(a.w, a.D_in * a.K))) return false;
   if (a.has_base && !fits(row_shape(a.wb, a.D_in))) return false;
@@ -720,7 +256,11 @@ static void launch_phi(const LayerArgs& a, const cc::Params& p, cudaStream_t s) 
     case KAN_BSPLINE:
       cc::cc_phi_kernel<MODE, KAN_BSPLINE><<<grid, cc::PRE_THREADS, 0, s>>>(a, p);
       break;
-    default: cc::cc_phi_kernel<MODE, KAN_WAVELET><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
+    case KAN_WAVELET:
+      cc::cc_phi_kernel<MODE, KAN_WAVELET><<<grid, cc::PRE_THREADS, 0, s>>>(a, p);
+      break;
+    case KAN_RELU: cc::cc_phi_kernel<MODE, KAN_RELU><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
+    default: cc::cc_phi_kernel<MODE, KAN_FOURIER><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
   }
 }
 
@@ -732,21 +272,21 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
   const int fmt = p.fmt;
   CUtensorMap cw, sw, mw, cb, sb, mb;
   const RowShape rw = row_shape(a.w, a.D_in * a.K);
-  if (!make_map(&cw, a.w.data, a.D_out, rw.bytes, ROW_BYTES, true) ||
-      !make_map(&sw, a.w.scales, a.D_out, rw.groups, p.sbox, false))
+  if (!make_map(&cw, a.w.data, a.D_out, rw.bytes, BOX_BYTES, true) ||
+      !make_map(&sw, a.w.scales, a.D_out, rw.groups, p.sbox_w, false))
     return cudaErrorInvalidValue;
   mw = sw;
-  if (fmt != KAN_W_TERNARY && !make_map(&mw, a.w.biases, a.D_out, rw.groups, p.sbox, false))
+  if (fmt != KAN_W_TERNARY && !make_map(&mw, a.w.biases, a.D_out, rw.groups, p.sbox_w, false))
     return cudaErrorInvalidValue;
   cb = cw;
   sb = sw;
   mb = mw;
   if (a.has_base) {
     const RowShape rbs = row_shape(a.wb, a.D_in);
-    if (!make_map(&cb, a.wb.data, a.D_out, rbs.bytes, ROW_BYTES, true) ||
-        !make_map(&sb, a.wb.scales, a.D_out, rbs.groups, p.sbox, false))
+    if (!make_map(&cb, a.wb.data, a.D_out, rbs.bytes, BOX_BYTES, true) ||
+        !make_map(&sb, a.wb.scales, a.D_out, rbs.groups, p.sbox_b, false))
       return cudaErrorInvalidValue;
-    if (fmt != KAN_W_TERNARY && !make_map(&mb, a.wb.biases, a.D_out, rbs.groups, p.sbox, false))
+    if (fmt != KAN_W_TERNARY && !make_map(&mb, a.wb.biases, a.D_out, rbs.groups, p.sbox_b, false))
       return cudaErrorInvalidValue;
   }
   if (mode == MODE_F16) launch_phi<MODE_F16>(a, p, s);
@@ -755,9 +295,8 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  const MainFn kern = main_kernel(mode, fmt);
-  const int ki = (mode == MODE_F16 ? 0 : 3) + (fmt == KAN_W_TERNARY ? 0 : (fmt == KAN_W_INT8 ? 1 : 2));
-  if ((e = ensure_smem_attr(kern, SMEM_MAX, g_configured[ki])) != cudaSuccess) return e;
+  const MainFn kern = main_kernel(mode, a.B, fmt, p.fast != 0, p.fu);
+  if ((e = ensure_smem_attr(kern, SMEM_MAX, configured(kern))) != cudaSuccess) return e;
   if (p.smem > SMEM_MAX) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.rowblocks, (unsigned)p.S, 1);

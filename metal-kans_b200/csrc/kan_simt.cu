@@ -181,7 +181,10 @@ static void launch_simt_tile(const LayerArgs& a, cudaStream_t s) {
     case KAN_CHEBY: kan_simt_kernel<KAN_CHEBY, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
     case KAN_RBF: kan_simt_kernel<KAN_RBF, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
     case KAN_BSPLINE: kan_simt_kernel<KAN_BSPLINE, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
-    default: kan_simt_kernel<KAN_WAVELET, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
+    case KAN_WAVELET: kan_simt_kernel<KAN_WAVELET, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
+    case KAN_RELU: kan_simt_kernel<KAN_RELU, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
+    case KAN_FOURIER: kan_simt_kernel<KAN_FOURIER, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
+    default: kan_simt_kernel<KAN_JACOBI, MODE, BM><<<grid, SIMT_THREADS, 0, s>>>(a); break;
   }
 }
 
@@ -379,33 +382,28 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
   }
 }
 
-template <int BN>
-static cudaError_t launch_dense_bn(const LayerArgs& a, cudaStream_t s) {
+template <int BASIS, int BN>
+static cudaError_t launch_dense_basis(const LayerArgs& a, cudaStream_t s) {
   const dim3 grid((a.D_out + BN - 1) / BN, (a.B + DN_BM - 1) / DN_BM);
   const int smem = (int)sizeof(DnSmem<BN>);
-  static std::atomic<unsigned long long> configured[4];
-  cudaError_t e;
-  switch (BasisOf(a)) {
-    case KAN_CHEBY:
-      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_CHEBY, BN>, smem, configured[0]))) return e;
-      kan_simt_dense_kernel<KAN_CHEBY, BN><<<grid, DN_THREADS, smem, s>>>(a);
-      break;
-    case KAN_RBF:
-      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_RBF, BN>, smem, configured[1]))) return e;
-      kan_simt_dense_kernel<KAN_RBF, BN><<<grid, DN_THREADS, smem, s>>>(a);
-      break;
-    case KAN_BSPLINE:
-      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_BSPLINE, BN>, smem, configured[2])))
-        return e;
-      kan_simt_dense_kernel<KAN_BSPLINE, BN><<<grid, DN_THREADS, smem, s>>>(a);
-      break;
-    default:
-      if ((e = ensure_smem_attr(kan_simt_dense_kernel<KAN_WAVELET, BN>, smem, configured[3])))
-        return e;
-      kan_simt_dense_kernel<KAN_WAVELET, BN><<<grid, DN_THREADS, smem, s>>>(a);
-      break;
-  }
+  static std::atomic<unsigned long long> configured{0};
+  cudaError_t e = ensure_smem_attr(kan_simt_dense_kernel<BASIS, BN>, smem, configured);
+  if (e != cudaSuccess) return e;
+  kan_simt_dense_kernel<BASIS, BN><<<grid, DN_THREADS, smem, s>>>(a);
   return cudaGetLastError();
+}
+
+template <int BN>
+static cudaError_t launch_dense_bn(const LayerArgs& a, cudaStream_t s) {
+  switch (BasisOf(a)) {
+    case KAN_CHEBY: return launch_dense_basis<KAN_CHEBY, BN>(a, s);
+    case KAN_RBF: return launch_dense_basis<KAN_RBF, BN>(a, s);
+    case KAN_BSPLINE: return launch_dense_basis<KAN_BSPLINE, BN>(a, s);
+    case KAN_WAVELET: return launch_dense_basis<KAN_WAVELET, BN>(a, s);
+    case KAN_RELU: return launch_dense_basis<KAN_RELU, BN>(a, s);
+    case KAN_FOURIER: return launch_dense_basis<KAN_FOURIER, BN>(a, s);
+    default: return launch_dense_basis<KAN_JACOBI, BN>(a, s);
+  }
 }
 
 // The streamed-panel kernel takes dense fp32 layers whose weight rows start on 16-byte

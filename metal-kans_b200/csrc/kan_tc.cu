@@ -89,10 +89,12 @@ static bool make_tmap_x(CUtensorMap* m, const void* base, int B, int D_in, int m
   return r == CUDA_SUCCESS;
 }
 
-static const DispatchFn kDispatch[3][4] = {
-    {nullptr, nullptr, nullptr, nullptr},
-    {dispatch_1_0, dispatch_1_1, dispatch_1_2, dispatch_1_3},
-    {dispatch_2_0, dispatch_2_1, dispatch_2_2, dispatch_2_3}};
+static const DispatchFn kDispatch[3][NUM_BASES] = {
+    {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr},
+    {dispatch_1_0, dispatch_1_1, dispatch_1_2, dispatch_1_3, dispatch_1_4, dispatch_1_5,
+     dispatch_1_6},
+    {dispatch_2_0, dispatch_2_1, dispatch_2_2, dispatch_2_3, dispatch_2_4, dispatch_2_5,
+     dispatch_2_6}};
 
 }  // namespace tc
 

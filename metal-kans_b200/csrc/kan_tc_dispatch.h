@@ -20,7 +20,9 @@ using DispatchFn = cudaError_t (*)(const CUtensorMap& tw, const CUtensorMap& tx,
                                         int x_tma, const LayerArgs& a, int BN, int nb,         \
                                         int splits, dim3 grid, cudaStream_t s);
 KAN_TC_DECL(1, 0) KAN_TC_DECL(1, 1) KAN_TC_DECL(1, 2) KAN_TC_DECL(1, 3)
+KAN_TC_DECL(1, 4) KAN_TC_DECL(1, 5) KAN_TC_DECL(1, 6)
 KAN_TC_DECL(2, 0) KAN_TC_DECL(2, 1) KAN_TC_DECL(2, 2) KAN_TC_DECL(2, 3)
+KAN_TC_DECL(2, 4) KAN_TC_DECL(2, 5) KAN_TC_DECL(2, 6)
 #undef KAN_TC_DECL
 
 }  // namespace tc

@@ -4,7 +4,7 @@
 #include "kan_tc_kernel.cuh"
 
 #if !defined(KAN_TC_MODE) || !defined(KAN_TC_BASIS)
-#error "build with -DKAN_TC_MODE=<1|2> -DKAN_TC_BASIS=<0..3>"
+#error "build with -DKAN_TC_MODE=<1|2> -DKAN_TC_BASIS=<0..6>"
 #endif
 
 #define KAN_CAT2(a, b, c) a##b##_##c

@@ -1221,7 +1221,7 @@ static cudaError_t dispatch_k(const CUtensorMap& tw, const CUtensorMap& tx, int 
     KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   } else if (BASIS == KAN_BSPLINE) {
     KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
-  } else {
+  } else if (BASIS == KAN_WAVELET) {
     KAN_TC_CASE(6, true) KAN_TC_CASE(6, false) KAN_TC_CASE(8, true) KAN_TC_CASE(8, false)
   }
 #undef KAN_TC_CASE

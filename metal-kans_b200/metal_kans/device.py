@@ -36,7 +36,7 @@ class KanWeight(ctypes.Structure):
     """``kan_weight`` of include/kan_cuda.h."""
 
     _fields_ = [("format", ctypes.c_int32), ("group_size", ctypes.c_int32),
-                ("padded_cols", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("padded_cols", ctypes.c_int32), ("flags", ctypes.c_int32),
                 ("data", vp), ("scales", vp), ("biases", vp), ("codebook", vp)]
 
 
@@ -51,14 +51,15 @@ class KanLayer(ctypes.Structure):
                 ("grid_min", ctypes.c_float), ("inv_h", ctypes.c_float),
                 ("ln_eps", ctypes.c_float), ("grid", vp), ("translation", vp),
                 ("inv_scale", vp), ("bias", vp), ("w", KanWeight), ("wb", KanWeight),
-                ("tc_weights", vp)]
+                ("tc_weights", vp), ("alpha", ctypes.c_float), ("beta", ctypes.c_float)]
 
 
 # enum values of include/kan_cuda.h
 KAN_F32, KAN_F16, KAN_BF16 = 0, 1, 2
-KAN_CHEBY, KAN_RBF, KAN_BSPLINE, KAN_WAVELET = 0, 1, 2, 3
+KAN_CHEBY, KAN_RBF, KAN_BSPLINE, KAN_WAVELET, KAN_RELU, KAN_FOURIER, KAN_JACOBI = range(7)
 KAN_MAP_NONE, KAN_MAP_TANH, KAN_MAP_LAYERNORM = 0, 1, 2
 KAN_W_DENSE, KAN_W_INT8, KAN_W_INT4, KAN_W_TERNARY, KAN_W_INT2 = 0, 1, 2, 3, 4
+KAN_WFLAG_TERNARY_NO3 = 1
 KAN_PATH_AUTO, KAN_PATH_SIMT, KAN_PATH_TC, KAN_PATH_GEMV, KAN_PATH_GEMV_CC = 0, 1, 2, 3, 4
 
 # (name, restype, argtypes) of every exported symbol
@@ -105,6 +106,16 @@ SIGNATURES = [
     ("metal_kan_fastkan_backward", i32, [vp] * 9 + [i32] * 4 + [f32] + [i32] * 2),
     ("metal_kan_bspline_backward", i32, [vp] * 8 + [i32] * 4 + [f32, f32] + [i32] * 2),
     ("metal_kan_swiglu_backward", i32, [vp] * 5 + [i32]),
+    ("metal_kan_relu_backward", i32, [vp] * 9 + [i32] * 4 + [f32] + [i32] * 2),
+    ("metal_kan_relu_forward", i32, [vp] * 6 + [i32] * 4 + [f32] + [i32] * 2),
+    ("metal_kan_relu_forward_fp16", i32, [vp] * 6 + [i32] * 4 + [f32] + [i32] * 2),
+    ("metal_kan_fourier_forward", i32, [vp] * 5 + [i32] * 6),
+    ("metal_kan_fourier_forward_fp16", i32, [vp] * 5 + [i32] * 6),
+    ("metal_kan_jacobi_forward", i32, [vp] * 5 + [i32] * 4 + [f32, f32] + [i32] * 2),
+    ("metal_kan_jacobi_forward_fp16", i32, [vp] * 5 + [i32] * 4 + [f32, f32] + [i32] * 2),
+    ("benchmark_metal_relu", ctypes.c_double, [vp] * 6 + [i32] * 4 + [f32] + [i32] * 4),
+    ("benchmark_metal_fourier", ctypes.c_double, [vp] * 5 + [i32] * 8),
+    ("benchmark_metal_jacobi", ctypes.c_double, [vp] * 5 + [i32] * 4 + [f32, f32] + [i32] * 4),
     ("kan_set_wait_limit", i32, [i64]),
     ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),

@@ -6,7 +6,8 @@ Activations stay on the device between layers (ping-pong buffers); only the inpu
 output cross PCIe.  ``pipeline=True`` on an fp32 Cheby net runs the reference's single-call chain
 entry point ``metal_kan_chain_pipeline_cheby``, which here honours each layer's degree (the
 reference hard-codes 4 terms, ``metal_kan_bridge.mm:1210``).
-Bases served by this engine: cheby, fastkan/rbf, bspline/spline/kan, wav/wavkan/wavelet.
+Bases served by this engine: cheby, fastkan/rbf, bspline/spline/kan, wav/wavkan/wavelet, relu,
+fourier, jacobi.
 """
 from __future__ import annotations
 
@@ -18,6 +19,9 @@ import numpy as np
 from . import _engine as E
 from .bspline_kan import BSplineKAN
 from .cheby_kan import ChebyKAN
+from .fourier_kan import FourierKAN
+from .jacobi_kan import JacobiKAN
+from .relu_kan import ReLUKAN
 from .fast_kan import FastKAN
 from .wav_kan import WavKAN
 
@@ -48,6 +52,13 @@ class MetalKAN:
                 layer = WavKAN(in_f, out_f, num_wavelets=degree, bias=bias, use_base=use_base)
             elif b in ("bspline", "spline", "kan"):
                 layer = BSplineKAN(in_f, out_f, grid_size=degree, bias=bias, use_base=use_base)
+            elif b in ("relukan", "relu", "tent"):
+                layer = ReLUKAN(in_f, out_f, num_grids=degree, bias=bias, use_base=use_base)
+            elif b in ("fourier", "fourierkan"):
+                layer = FourierKAN(in_f, out_f, num_frequencies=degree, bias=bias,
+                                   use_base=use_base)
+            elif b in ("jacobi", "jacobikan"):
+                layer = JacobiKAN(in_f, out_f, degree=degree, bias=bias, use_base=use_base)
             else:
                 raise ValueError(f"Unknown or unsupported basis_type for this engine: {basis_type}")
             self.layers.append(layer)

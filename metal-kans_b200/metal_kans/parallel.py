@@ -162,7 +162,10 @@ class OutputShardedLayer:
                 self._pad = pad
             pad[:, :w] = y_local
             src = pad
-        dist.all_gather_into_tensor(gathered, src, group=self.group)
+        # the output as [world * B, width]: NCCL takes any shape of the right size, gloo splits
+        # dim 0 into per-rank blocks of the input's shape
+        dist.all_gather_into_tensor(gathered.view(self.world * B, self.width), src,
+                                    group=self.group)
         if all(b - a == self.width for a, b in self.ranges):
             out.view(B, self.world, self.width).copy_(gathered.permute(1, 0, 2))
         else:

@@ -112,11 +112,20 @@ class TernaryQuantizedWeight(_PackedMixin):
             self.group_size)
         return out
 
+    def _no_code3(self) -> bool:
+        """True when no packed code is 3 (checked once, with the device copy it describes)."""
+        cache = self.__dict__.setdefault("_dev_bufs", {})
+        if "no_code3" not in cache:
+            a = np.ascontiguousarray(self.w_packed).view(np.uint32)
+            cache["no_code3"] = not np.any(a & (a >> 1) & np.uint32(0x55555555))
+        return cache["no_code3"]
+
     def _fill_struct(self, w: D.KanWeight, keep: list) -> None:
         p, s = self._device("w_packed"), self._device("scales")
         keep += [p, s]
         w.format = D.KAN_W_TERNARY
         w.group_size = self.group_size
+        w.flags = D.KAN_WFLAG_TERNARY_NO3 if self._no_code3() else 0
         w.data, w.scales = p.ptr, s.ptr
 
 

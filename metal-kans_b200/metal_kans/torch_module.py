@@ -23,6 +23,7 @@ from . import device as D
 from .bspline_kan import BSplineKAN
 from .cheby_kan import ChebyKAN
 from .fast_kan import FastKAN
+from .relu_kan import ReLUKAN
 
 _TORCH_KAN = {torch.float32: D.KAN_F32, torch.float16: D.KAN_F16, torch.bfloat16: D.KAN_BF16}
 
@@ -45,6 +46,8 @@ def _descriptor(basis: int, dtype, D_in: int, D_out: int, K: int, weight, base_w
         L.grid, L.inv_den = grid.data_ptr(), float(inv_den)
     elif basis == D.KAN_BSPLINE:
         L.grid_size, L.grid_min, L.inv_h = int(grid_size), float(grid_min), float(inv_h)
+    elif basis == D.KAN_RELU:
+        L.grid, L.inv_h = grid.data_ptr(), float(inv_h)
     return L
 
 
@@ -148,7 +151,7 @@ kan_linear.register_autograd(_backward, setup_context=_setup_context)
 
 
 class TorchMetalKANLinear(nn.Module):
-    """KAN layer as an ``nn.Module`` (bases: cheby, fastkan/rbf, bspline/kan)."""
+    """KAN layer as an ``nn.Module`` (bases: cheby, fastkan/rbf, bspline/kan, relu/relukan)."""
 
     def __init__(self, in_features: int, out_features: int, basis: str = "cheby",
                  degree: int = 4, bias: bool = True, use_base: bool = True):
@@ -168,6 +171,10 @@ class TorchMetalKANLinear(nn.Module):
         elif self.basis in ("bspline", "kan"):
             layer = BSplineKAN(in_features, out_features, grid_size=degree, bias=bias)
             w_main = layer.w_spline
+        elif self.basis in ("relu", "relukan"):
+            layer = ReLUKAN(in_features, out_features, num_grids=degree, bias=bias,
+                            use_base=use_base)
+            w_main = layer.w_relu
         else:
             raise ValueError(f"Unsupported basis type: {basis}")
         self.metal_layer = layer
@@ -176,7 +183,7 @@ class TorchMetalKANLinear(nn.Module):
                             if layer.has_base else None)
         self.bias_param = (nn.Parameter(torch.from_numpy(np.array(layer.bias, np.float32)))
                            if layer.has_bias else None)
-        if self.basis in ("fastkan", "rbf"):
+        if self.basis in ("fastkan", "rbf", "relu", "relukan"):
             self.register_buffer("grid", torch.from_numpy(np.array(layer.grid, np.float32)))
         else:
             self.grid = None
@@ -188,7 +195,7 @@ class TorchMetalKANLinear(nn.Module):
                           int(lay.BASIS), int(lay._terms()),
                           int(getattr(lay, "grid_size", 0)),
                           float(g[0]) if g is not None else 0.0,
-                          float(g[1]) if g is not None else 0.0,
+                          float(g[1]) if g is not None else float(getattr(lay, "inv_h", 0.0)),
                           float(getattr(lay, "inv_denominator", 0.0)))
 
 

@@ -47,7 +47,8 @@ class FakeBridge:
     def metal_kan_sync(self):
         return 0
 
-    # ---- forwards (metal_kan_bridge.mm:443, :532, :722, :1069 and the _fp16 twins) -----------
+    # ---- forwards (metal_kan_bridge.mm:443, :532, :722, :1069, relu / fourier / jacobi and the
+    # _fp16 twins) ------------------------------------------------------------------------------
     def _fwd(self, mode, basis, X, W, Wb, bias, Y, B, D_in, D_out, K, has_base, has_bias,
              **kw):
         dt = np.float16 if mode == "f16" else np.float32
@@ -101,6 +102,37 @@ class FakeBridge:
 
     def metal_kan_wavkan_forward_fp16(self, *a):
         return self._wav("f16", *a)
+
+    def _relu(self, mode, X, W, Wb, grid, bias, Y, B, D_in, D_out, G, inv_h, hb, hbi):
+        g = _arr(grid, (G,), np.float16 if mode == "f16" else np.float32).copy()
+        return self._fwd(mode, "relu", X, W, Wb, bias, Y, B, D_in, D_out, G, hb, hbi, grid=g,
+                         inv_h=inv_h)
+
+    def metal_kan_relu_forward(self, *a):
+        return self._relu("f32", *a)
+
+    def metal_kan_relu_forward_fp16(self, *a):
+        return self._relu("f16", *a)
+
+    def _fourier(self, mode, X, W, Wb, bias, Y, B, D_in, D_out, F, hb, hbi):
+        return self._fwd(mode, "fourier", X, W, Wb, bias, Y, B, D_in, D_out, 2 * F + 1, hb, hbi,
+                         num_freqs=F)
+
+    def metal_kan_fourier_forward(self, *a):
+        return self._fourier("f32", *a)
+
+    def metal_kan_fourier_forward_fp16(self, *a):
+        return self._fourier("f16", *a)
+
+    def _jacobi(self, mode, X, W, Wb, bias, Y, B, D_in, D_out, deg, alpha, beta, hb, hbi):
+        return self._fwd(mode, "jacobi", X, W, Wb, bias, Y, B, D_in, D_out, deg, hb, hbi,
+                         alpha=alpha, beta=beta)
+
+    def metal_kan_jacobi_forward(self, *a):
+        return self._jacobi("f32", *a)
+
+    def metal_kan_jacobi_forward_fp16(self, *a):
+        return self._jacobi("f16", *a)
 
     def metal_kan_chain_pipeline_cheby(self, X, Y, B, L, dims, degs, Ws, Wbs, biases):
         """``metal_kan_bridge.mm:1168-1248`` -- note the reference hard-codes degree 4 there

@@ -257,6 +257,119 @@ def wavelet_basis(x_act: np.ndarray, translation: np.ndarray, inv_scale: np.ndar
     return _round_mode(psi.reshape(B, D * W), mode)
 
 
+def relu_basis(x_act: np.ndarray, grid: np.ndarray, inv_h: float, mode: str) -> np.ndarray:
+    """Tent max(0, 1 - |x - g_k| inv_h) on the raw input (ReLUKAN).
+
+    fp32: ``fused_kan.metal:278-303`` -> |x - g| and the product in fp32 are near-exact; the
+    oracle evaluates in float64 with the fp32 grid and fp32 inv_h.
+    fp16 (``fused_kan.metal:1452-1474``): half arithmetic -- diff = x - g (half), |diff| * half(inv_h)
+    (half), 1 - that (half), max with 0.
+    """
+    B, D = x_act.shape
+    K = np.asarray(grid).shape[0]
+    if mode == "f16":
+        xh = x_act.astype(np.float16).astype(np.float64)[:, :, None]
+        gh = np.asarray(grid).astype(np.float16).astype(np.float64)[None, None, :]
+        ih = np.float64(np.float16(inv_h))
+        d = np.abs(_h(xh - gh).astype(np.float64))
+        t = _h(d * ih).astype(np.float64)
+        return np.maximum(0.0, _h(1.0 - t).astype(np.float64)).reshape(B, D * K)
+    x64 = x_act.astype(np.float64)[:, :, None]
+    g64 = np.asarray(grid, np.float32).astype(np.float64)[None, None, :]
+    ih = np.float64(np.float32(inv_h))
+    return _round_mode(np.maximum(0.0, 1.0 - np.abs(x64 - g64) * ih).reshape(B, D * K), mode)
+
+
+def fourier_basis(x_act: np.ndarray, num_freqs: int, mode: str) -> np.ndarray:
+    """1, cos(pi x), sin(pi x), ..., cos(F pi x), sin(F pi x) on the raw input (FourierKAN).
+
+    fp32 (``fused_kan.metal:306-329``): angle = fp32(fp32(f * pi) * x), then exact cos/sin.
+    fp16 (``fused_kan.metal:1550-1576``): pi_x = half(pi) * x and angle = half(f) * pi_x in half;
+    cos/sin of that half angle, stored as half.
+    """
+    B, D = x_act.shape
+    nb = 2 * num_freqs + 1
+    out = np.empty((B, D, nb), np.float64)
+    out[..., 0] = 1.0
+    if mode == "f16":
+        xh = x_act.astype(np.float16).astype(np.float64)
+        pix = _h(np.float64(np.float16(np.pi)) * xh).astype(np.float64)
+        for f in range(1, num_freqs + 1):
+            ang = _h(np.float64(f) * pix).astype(np.float64)
+            out[..., 2 * f - 1] = _h(np.cos(ang)).astype(np.float64)
+            out[..., 2 * f] = _h(np.sin(ang)).astype(np.float64)
+        return out.reshape(B, D * nb)
+    x32 = x_act.astype(np.float32)
+    for f in range(1, num_freqs + 1):
+        fr = np.float32(np.float32(f) * np.float32(np.pi))
+        ang = (fr * x32).astype(np.float32).astype(np.float64)
+        out[..., 2 * f - 1] = np.cos(ang)
+        out[..., 2 * f] = np.sin(ang)
+    return _round_mode(out.reshape(B, D * nb), mode)
+
+
+def _jacobi_coeffs(n: int, alpha: float, beta: float):
+    """The recurrence coefficients an, bn1, bn2, cn in fp32 arithmetic, in the reference's
+    order of operations (``fused_kan.metal:352-356``)."""
+    f = np.float32
+    fn, a, b = f(n), f(alpha), f(beta)
+    ab = f(a + b)
+    an = f(f(f(f(2.0) * fn) * f(fn + ab)) * f(f(f(2.0) * fn + ab) - f(2.0)))
+    t = f(f(2.0) * fn + ab)
+    bn1 = f(f(f(t - f(1.0)) * t) * f(t - f(2.0)))
+    bn2 = f(f(t - f(1.0)) * f(f(a * a) - f(b * b)))
+    cn = f(f(f(f(2.0) * f(fn + f(a - f(1.0)))) * f(fn + f(b - f(1.0)))) * t)
+    return an, bn1, bn2, cn
+
+
+def jacobi_basis(x_act: np.ndarray, degree: int, alpha: float, beta: float,
+                 mode: str) -> np.ndarray:
+    """Jacobi P_0..P_{degree-1}^(alpha, beta) of clamp(x, -1, 1) by the three-term recurrence
+    ``P_n = ((bn1 x + bn2) P_{n-1} - cn P_{n-2}) / an`` (``fused_kan.metal:331-366``).
+
+    fp32 evaluates the recurrence exactly in float64 with exact coefficients; fp16
+    (``:1578-1613``) mirrors the fp32 ``fma(fma(bn1, x, bn2), p1, -cn p0) / an`` recurrence
+    (each fma rounded once to fp32) and stores half.
+    """
+    B, D = x_act.shape
+    xc = np.clip(x_act.astype(np.float64), -1.0, 1.0)
+    out = np.empty((B, D, degree), np.float64)
+    a, b = float(alpha), float(beta)
+    if mode == "f16":
+        f = np.float32
+        x32 = xc.astype(np.float32)
+        ab = f(f(a) + f(b))
+        p0 = np.ones_like(x32)
+        out[..., 0] = 1.0
+        if degree > 1:
+            p1 = (f(0.5) * (f(f(a) - f(b)) + (ab + f(2.0)) * x32).astype(np.float32)).astype(np.float32)
+            out[..., 1] = p1
+            for n in range(2, degree):
+                an, bn1, bn2, cn = _jacobi_coeffs(n, a, b)
+                inner = (np.float64(bn1) * x32.astype(np.float64) + np.float64(bn2)).astype(np.float32)
+                m = (-(cn * p0)).astype(np.float32)
+                outer = (inner.astype(np.float64) * p1.astype(np.float64) + m.astype(np.float64)).astype(np.float32)
+                p = (outer / an).astype(np.float32)
+                out[..., n] = p
+                p0, p1 = p1, p
+        return out.reshape(B, D * degree).astype(np.float16).astype(np.float64)
+    ab = a + b
+    p0 = np.ones_like(xc)
+    out[..., 0] = 1.0
+    if degree > 1:
+        p1 = 0.5 * (a - b + (ab + 2.0) * xc)
+        out[..., 1] = p1
+        for n in range(2, degree):
+            an = 2.0 * n * (n + ab) * (2.0 * n + ab - 2.0)
+            bn1 = (2.0 * n + ab - 1.0) * (2.0 * n + ab) * (2.0 * n + ab - 2.0)
+            bn2 = (2.0 * n + ab - 1.0) * (a * a - b * b)
+            cn = 2.0 * (n + a - 1.0) * (n + b - 1.0) * (2.0 * n + ab)
+            p = ((bn1 * xc + bn2) * p1 - cn * p0) / an
+            out[..., n] = p
+            p0, p1 = p1, p
+    return _round_mode(out.reshape(B, D * degree), mode)
+
+
 # --------------------------------------------------------------------------------------------
 # Projection
 # --------------------------------------------------------------------------------------------
@@ -293,7 +406,7 @@ def project(phi64: np.ndarray, W, x_base64, W_base, bias, mode: str,
 def kan_layer(x, basis: str, mode: str, W, W_base=None, bias=None, *, K=None, grid=None,
               inv_den=None, grid_size=None, grid_min=None, inv_h=None, translation=None,
               inv_scale=None, wavelet_type=0, input_map="none", out_round=True,
-              round_weights=True):
+              round_weights=True, num_freqs=None, alpha=0.0, beta=0.0):
     """One KAN layer forward (reference call stack A of the bridge, any basis).
 
     ``x`` is rounded to the activation dtype first (the reference casts x to the weight dtype,
@@ -310,6 +423,12 @@ def kan_layer(x, basis: str, mode: str, W, W_base=None, bias=None, *, K=None, gr
         phi = bspline_basis(xm, grid_size, grid_min, inv_h, mode)
     elif basis == "wavelet":
         phi = wavelet_basis(xm, translation, inv_scale, wavelet_type, mode)
+    elif basis == "relu":
+        phi = relu_basis(xm, np.asarray(grid), inv_h, mode)
+    elif basis == "fourier":
+        phi = fourier_basis(xm, num_freqs if num_freqs is not None else (K - 1) // 2, mode)
+    elif basis == "jacobi":
+        phi = jacobi_basis(xm, K, alpha, beta, mode)
     else:
         raise ValueError(basis)
     xb = silu(xm, mode) if W_base is not None else None
@@ -594,6 +713,11 @@ def _basis_and_grad64(x, basis, K, grid=None, inv_den=None, grid_size=None, grid
             phi[tuple(idx) + (span + j,)] = vals[j]
             dphi[tuple(idx) + (span + j,)] = ders[j] * float(inv_h)
         return phi, dphi
+    if basis == "relu":
+        # tent derivative -sign(x - g) inv_h where the tent is positive (fused_kan.metal:1787-1826)
+        d = x[..., None] - np.asarray(grid, np.float64)
+        v = 1.0 - np.abs(d) * float(inv_h)
+        return np.maximum(0.0, v), np.where(v > 0.0, -np.sign(d) * float(inv_h), 0.0)
     raise ValueError(basis)
 
 

@@ -10,6 +10,7 @@ What is real reference code here and what is restated:
   run unchanged (the stand-in bridge returns -1 so the reference falls back to them).  These
   fixtures pin the oracle's quantisers bit-exactly.
 * layers: the reference's classes (``ChebyKAN``, ``FastKAN``, ``BSplineKAN``, ``WavKAN``,
+  ``ReLUKAN``, ``FourierKAN``, ``JacobiKAN``,
   ``GatedKAN``, ``MetalKAN``) run unchanged -- construction, weight init order, ``.half()``,
   casts, reshapes, ``to_int*`` -- with the Metal/MPS arithmetic supplied by
   ``oracle/fake_bridge.py`` (the Metal kernels cannot run off macOS).
@@ -48,6 +49,12 @@ def layer_goldens(mk):
         ("wav_mexican", lambda: mk.WavKAN(8, 16, num_wavelets=6, wavelet_type="mexican_hat"), (-1.0, 1.0), 64),
         ("wav_morlet", lambda: mk.WavKAN(8, 16, num_wavelets=6, wavelet_type="morlet"), (-1.0, 1.0), 64),
         ("wav_dog", lambda: mk.WavKAN(8, 16, num_wavelets=6, wavelet_type="dog"), (-1.0, 1.0), 64),
+        ("relu_g8", lambda: mk.ReLUKAN(8, 16, num_grids=8), (-1.2, 1.2), 64),
+        ("relu_g5_range2", lambda: mk.ReLUKAN(8, 16, num_grids=5, grid_range=(-2, 2)), (-2.0, 2.0), 64),
+        ("fourier_f4", lambda: mk.FourierKAN(8, 16, num_frequencies=4), (-1.0, 1.0), 64),
+        ("fourier_f3_nobase", lambda: mk.FourierKAN(8, 16, num_frequencies=3, use_base=False), (-2.0, 2.0), 64),
+        ("jacobi_d4", lambda: mk.JacobiKAN(8, 16, degree=4), (-1.2, 1.2), 64),
+        ("jacobi_d6_ab", lambda: mk.JacobiKAN(8, 16, degree=6, alpha=0.5, beta=1.5), (-1.0, 1.0), 64),
     ]
     for name, ctor, (lo, hi), B in cases:
         for mode in ("f32", "f16"):
@@ -61,13 +68,13 @@ def layer_goldens(mk):
                 xin = x
             y = layer(xin)
             rec = {"x": xin, "y": y}
-            for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_base", "bias", "grid",
-                         "translation", "_inv_scale"):
+            for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_relu", "w_fourier", "w_jacobi",
+                         "w_base", "bias", "grid", "translation", "_inv_scale"):
                 if hasattr(layer, attr):
                     rec[attr.lstrip("_")] = np.asarray(getattr(layer, attr))
             meta = dict(has_base=layer.has_base, has_bias=layer.has_bias)
             for attr in ("degree", "num_centers", "inv_denominator", "grid_size", "num_wavelets",
-                         "wavelet_type"):
+                         "wavelet_type", "num_grids", "inv_h", "num_frequencies", "alpha", "beta"):
                 if hasattr(layer, attr):
                     meta[attr] = getattr(layer, attr)
             for k, v in meta.items():
@@ -173,8 +180,8 @@ def block_goldens(mk):
         rec[f"net_{basis}/x"] = x
         rec[f"net_{basis}/y"] = net(x)
         for li, l in enumerate(net.layers):
-            for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_base", "bias", "grid",
-                         "translation", "_inv_scale"):
+            for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_relu", "w_fourier", "w_jacobi",
+                         "w_base", "bias", "grid", "translation", "_inv_scale"):
                 if hasattr(l, attr):
                     rec[f"net_{basis}/{li}.{attr.lstrip('_')}"] = np.asarray(getattr(l, attr))
     # pipelined Cheby chain (reference hard-codes degree 4 there, so use degree 4)

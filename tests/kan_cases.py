@@ -38,6 +38,12 @@ def oracle_for_layer(layer, x, mode, basis, out_round=True, exact_weights=False)
         kw = dict(translation=np.asarray(layer.translation).astype(np.float32),
                   inv_scale=np.asarray(layer._inv_scale).astype(np.float32),
                   wavelet_type=layer.wavelet_type)
+    elif basis == "relu":
+        kw = dict(grid=np.asarray(layer.grid), inv_h=layer.inv_h)
+    elif basis == "fourier":
+        kw = dict(num_freqs=layer.num_frequencies)
+    elif basis == "jacobi":
+        kw = dict(alpha=layer.alpha, beta=layer.beta)
     return O.kan_layer(x, basis, mode, W, wb, b, K=layer._terms(),
                        input_map=getattr(layer, "input_map", "none"), out_round=out_round,
                        round_weights=not exact_weights, **kw)
@@ -62,6 +68,16 @@ def make_layer(basis, d_in, d_out, K, *, bias=True, use_base=True, input_map="no
     if basis == "bspline":
         return mk.BSplineKAN(d_in, d_out, grid_size=K - 3, bias=bias, use_base=use_base,
                              input_map=input_map)
+    if basis == "relu":
+        return mk.ReLUKAN(d_in, d_out, num_grids=K, bias=bias, use_base=use_base,
+                          grid_range=(-2.0, 2.0))
+    if basis == "fourier":
+        return mk.FourierKAN(d_in, d_out, num_frequencies=(K - 1) // 2, bias=bias,
+                             use_base=use_base)
+    if basis == "jacobi":
+        # alpha, beta > 0: values above 1 (the recurrence's general coefficients)
+        return mk.JacobiKAN(d_in, d_out, degree=K, alpha=0.5, beta=0.25, bias=bias,
+                            use_base=use_base)
     return mk.WavKAN(d_in, d_out, num_wavelets=K, bias=bias, use_base=use_base,
                      wavelet_type=wavelet_type, input_map=input_map)
 

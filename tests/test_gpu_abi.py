@@ -60,6 +60,21 @@ def test_host_abi_all_forwards(mk):
             ref = O.kan_layer(x, "wavelet", mode, W, wb, b, K=5, translation=tr, inv_scale=isc,
                               wavelet_type=wt)
             assert O.max_rel_err(y, ref) <= TOL[mode]
+        # relu (grid in the layer dtype, inv_h fp32)
+        W = rng.normal(0, 0.1, (Do, Di * 7)).astype(dt)
+        grid = np.linspace(-1, 1, 7).astype(dt)
+        getattr(lib, "metal_kan_relu_forward" + sfx)(P(x), P(W), P(wb), P(grid), P(b), P(y), B, Di, Do, 7, 3.0, 1, 1)
+        ref = O.kan_layer(x, "relu", mode, W, wb, b, K=7, grid=grid, inv_h=3.0)
+        assert O.max_rel_err(y, ref) <= TOL[mode]
+        # fourier (3 frequencies: 7 bases)
+        getattr(lib, "metal_kan_fourier_forward" + sfx)(P(x), P(W), P(wb), P(b), P(y), B, Di, Do, 3, 1, 1)
+        ref = O.kan_layer(x, "fourier", mode, W, wb, b, K=7, num_freqs=3)
+        assert O.max_rel_err(y, ref) <= TOL[mode]
+        # jacobi
+        W = rng.normal(0, 0.1, (Do, Di * 5)).astype(dt)
+        getattr(lib, "metal_kan_jacobi_forward" + sfx)(P(x), P(W), P(wb), P(b), P(y), B, Di, Do, 5, 1.0, 0.5, 1, 1)
+        ref = O.kan_layer(x, "jacobi", mode, W, wb, b, K=5, alpha=1.0, beta=0.5)
+        assert O.max_rel_err(y, ref) <= TOL[mode]
 
 
 def test_host_abi_packed_cheby(mk):
@@ -97,12 +112,13 @@ def test_swiglu_and_benchmark_entry_points(mk):
     assert 0 < ms < 1000
 
 
-K_OF = {"cheby": 5, "rbf": 8, "bspline": 8, "wavelet": 6}
+K_OF = {"cheby": 5, "rbf": 8, "bspline": 8, "wavelet": 6, "relu": 8, "fourier": 9, "jacobi": 5}
 
 
-@pytest.mark.parametrize("basis", ["cheby", "rbf", "bspline", "wavelet"])
+@pytest.mark.parametrize("basis", ["cheby", "rbf", "bspline", "wavelet", "relu", "fourier",
+                                   "jacobi"])
 def test_benchmark_entry_points_all_bases(mk, basis):
-    """benchmark_metal_{cheby,fastkan,bspline,wavkan} (metal_kan_bridge.mm:1250-1371): a positive
+    """benchmark_metal_{cheby,fastkan,bspline,wavkan,relu,fourier,jacobi} (metal_kan_bridge.mm:1250-1371): a positive
     mean of milliseconds per host-pointer forward, and the Y each leaves behind is the layer's
     forward (fp32 path, 1e-5 against the oracle)."""
     lib = mk.get_metal_bridge()
@@ -123,6 +139,16 @@ def test_benchmark_entry_points_all_bases(mk, basis):
         g = np.ascontiguousarray(l.grid, np.float32)
         ms = lib.benchmark_metal_bspline(P(x), P(W), P(l.w_base), P(g), P(l.bias), P(y), 300, 48,
                                          40, l.grid_size, l.spline_order, 1, 1, 1, 3)
+    elif basis == "relu":
+        g = np.ascontiguousarray(l.grid, np.float32)
+        ms = lib.benchmark_metal_relu(P(x), P(W), P(l.w_base), P(g), P(l.bias), P(y), 300, 48, 40,
+                                      l.num_grids, l.inv_h, 1, 1, 1, 3)
+    elif basis == "fourier":
+        ms = lib.benchmark_metal_fourier(P(x), P(W), P(l.w_base), P(l.bias), P(y), 300, 48, 40,
+                                         l.num_frequencies, 1, 1, 1, 3)
+    elif basis == "jacobi":
+        ms = lib.benchmark_metal_jacobi(P(x), P(W), P(l.w_base), P(l.bias), P(y), 300, 48, 40,
+                                        l.degree, l.alpha, l.beta, 1, 1, 1, 3)
     else:
         ms = lib.benchmark_metal_wavkan(P(x), P(W), P(l.w_base), P(l.translation),
                                         P(l._inv_scale), P(l.bias), P(y), 300, 48, 40,
@@ -202,6 +228,6 @@ def test_torch_module(mk, dtype):
     mode = {"float32": "f32", "float16": "f16", "bfloat16": "bf16"}[dtype]
     ref = O.kan_layer(x.float().cpu().numpy(), "cheby", mode, layer.weight.detach().cpu().numpy(),
                       layer.base_weight.detach().cpu().numpy(), layer.bias_param.detach().cpu().numpy(), K=4)
-    assert O.max_rel_err(y.float().cpu().numpy(), ref.astype(np.float32)) <= TOL[mode]
+    assert O.max_rel_err(y.detach().float().cpu().numpy(), ref.astype(np.float32)) <= TOL[mode]
     net = mk.TorchMetalKAN([4, 8, 2], basis="cheby", degree=3).cuda()
     assert net(torch.randn(10, 4)).shape == (10, 2)  # CPU input -> CPU output

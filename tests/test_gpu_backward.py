@@ -25,7 +25,9 @@ def _oracle_grads(layer, x, dY):
         kw = dict(grid=np.asarray(layer.grid, np.float64), inv_den=layer.inv_denominator)
     elif layer.MAIN == "w_spline":
         kw = dict(grid_size=layer.grid_size, grid_min=float(layer.grid[0]), inv_h=float(layer.grid[1]))
-    basis = {"w_cheby": "cheby", "w_rbf": "rbf", "w_spline": "bspline"}[layer.MAIN]
+    elif layer.MAIN == "w_relu":
+        kw = dict(grid=np.asarray(layer.grid, np.float64), inv_h=layer.inv_h)
+    basis = {"w_cheby": "cheby", "w_rbf": "rbf", "w_spline": "bspline", "w_relu": "relu"}[layer.MAIN]
     return O.kan_layer_backward(x, dY, basis, getattr(layer, layer.MAIN),
                                 layer.w_base if layer.has_base else None, K=layer._terms(), **kw)
 
@@ -42,6 +44,8 @@ CASES = [
     ("rbf", 8, 257, 33, 20, True, True, 1.5),
     ("bspline", 8, 200, 24, 50, True, False, 1.4),  # inputs beyond the grid
     ("cheby", 4, 1, 130, 3, True, True, 1.0),
+    ("relu", 8, 150, 36, 44, True, True, 2.4),    # inputs beyond the outer tents
+    ("relu", 5, 64, 70, 16, False, True, 1.9),
 ]
 
 
@@ -173,7 +177,7 @@ def test_kan_backward_device_api():
                          None)
 
 
-@pytest.mark.parametrize("basis,K", [("cheby", 4), ("rbf", 6), ("bspline", 5)])
+@pytest.mark.parametrize("basis,K", [("cheby", 4), ("rbf", 6), ("bspline", 5), ("relu", 6)])
 def test_torch_autograd(basis, K):
     """TorchMetalKANLinear is differentiable on the GPU: gradients of x and of every parameter
     equal the oracle's."""
@@ -194,7 +198,9 @@ def test_torch_autograd(basis, K):
         kw = dict(grid=layer.grid.cpu().numpy(), inv_den=ml.inv_denominator)
     elif basis == "bspline":
         kw = dict(grid_size=ml.grid_size, grid_min=float(ml.grid[0]), inv_h=float(ml.grid[1]))
-    name = {"cheby": "cheby", "rbf": "rbf", "bspline": "bspline"}[basis]
+    elif basis == "relu":
+        kw = dict(grid=layer.grid.cpu().numpy(), inv_h=ml.inv_h)
+    name = basis
     wb = layer.base_weight.detach().cpu().numpy() if layer.base_weight is not None else None
     rdX, rdW, rdWb, rdb = O.kan_layer_backward(x.detach().cpu().numpy(), gy.cpu().numpy(), name,
                                                layer.weight.detach().cpu().numpy(), wb, K=terms,

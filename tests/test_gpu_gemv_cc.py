@@ -47,6 +47,10 @@ CASES = [
     ("int4", "bf16", "cheby", 5, 512, 256, 4, 64, True, True, "none"),
     ("int4", "f16", "bspline", 8, 1024, 96, 1, 32, True, True, "none"),
     ("int4", "bf16", "cheby", 9, 1024, 130, 3, 128, False, True, "tanh"),
+    ("ternary", "bf16", "relu", 8, 1024, 128, 2, 64, True, True, "none"),
+    ("ternary", "f16", "fourier", 9, 1024, 96, 4, 64, True, True, "none"),
+    ("int8", "bf16", "relu", 5, 1024, 64, 1, 64, True, False, "none"),
+    ("int4", "f16", "fourier", 5, 1024, 160, 3, 32, False, True, "none"),
 ]
 
 
@@ -140,3 +144,14 @@ def test_cc_rejects_unsupported():
     mk.to_ternary(f, group_size=64)  # fp32 layers keep the exact path
     with pytest.raises(KanError):
         f.forward(np.zeros((2, 1024), np.float32), path=CC)
+    j = make_layer("jacobi", 1024, 256, 4, seed=5)
+    mk.to_ternary(j, group_size=64)  # Jacobi values exceed 1: no 14-bit fixed-point basis
+    j.bfloat16()
+    with pytest.raises(KanError):
+        j.forward(x[:2], path=CC)
+    assert _plan(mk, j, 2)[0] != CC
+    g = make_layer("cheby", 1024, 256, 9, seed=6)
+    mk.to_ternary(g, group_size=48)  # group index by shift: power-of-two groups only
+    g.bfloat16()
+    with pytest.raises(KanError):
+        g.forward(x[:2], path=CC)

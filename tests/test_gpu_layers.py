@@ -38,6 +38,23 @@ def _layer_from_golden(mk, rec):
         l.w_spline = rec["w_spline"]
         l.grid = rec["grid"]
         basis = "bspline"
+    elif "w_relu" in rec:
+        l = mk.ReLUKAN(8, 16, num_grids=int(rec["meta_num_grids"]), bias=bool(hbi),
+                       use_base=bool(hb))
+        l.w_relu = rec["w_relu"]
+        l.grid = rec["grid"]
+        l.inv_h = float(rec["meta_inv_h"])
+        basis = "relu"
+    elif "w_fourier" in rec:
+        l = mk.FourierKAN(8, 16, num_frequencies=int(rec["meta_num_frequencies"]),
+                          bias=bool(hbi), use_base=bool(hb))
+        l.w_fourier = rec["w_fourier"]
+        basis = "fourier"
+    elif "w_jacobi" in rec:
+        l = mk.JacobiKAN(8, 16, degree=int(rec["meta_degree"]), alpha=float(rec["meta_alpha"]),
+                         beta=float(rec["meta_beta"]), bias=bool(hbi), use_base=bool(hb))
+        l.w_jacobi = rec["w_jacobi"]
+        basis = "jacobi"
     else:
         l = mk.WavKAN(8, 16, num_wavelets=int(rec["meta_num_wavelets"]), bias=bool(hbi),
                       use_base=bool(hb))
@@ -91,6 +108,12 @@ SHAPES = [  # (basis, d_in, d_out, K, B)
     # small grids of 256-wide tiles: the column-split cluster kernel (ragged rows and columns)
     ("wavelet", 64, 320, 6, 200),
     ("cheby", 256, 512, 9, 130),
+    ("relu", 64, 96, 8, 300),
+    ("relu", 200, 256, 5, 1024),
+    ("fourier", 64, 128, 9, 257),
+    ("fourier", 30, 50, 5, 64),
+    ("jacobi", 96, 128, 4, 300),
+    ("jacobi", 64, 256, 6, 1024),
 ]
 
 
@@ -104,7 +127,7 @@ def test_random_layers_vs_oracle(mk, shape, mode, path):
     layer = set_mode(make_layer(basis, d_in, d_out, K, seed=d_in + K), mode)
     randomize_bias(layer)
     rng = np.random.default_rng(B)
-    lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
+    lo, hi = (-2.5, 2.5) if basis in ("rbf", "relu") else (-1.2, 1.2)
     x = rng.uniform(lo, hi, (B, d_in)).astype(np.float32)
     y = layer.forward(x, path=PATHS[path])
     err = layer_err(y, layer, x, mode, basis)
@@ -195,7 +218,7 @@ def test_host_forward_chunked(mk, case):
     basis, d_in, d_out, K, B, mode = case
     layer = set_mode(make_layer(basis, d_in, d_out, K, seed=7), mode)
     randomize_bias(layer)
-    lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
+    lo, hi = (-2.5, 2.5) if basis in ("rbf", "relu") else (-1.2, 1.2)
     x = np.random.default_rng(B).uniform(lo, hi, (B, d_in)).astype(np.float32)
     y = layer(x)
     assert y.shape == (B, d_out)
@@ -216,7 +239,7 @@ def test_wide_tiles(mk, case):
     basis, d_in, d_out, K, B, mode = case
     layer = set_mode(make_layer(basis, d_in, d_out, K, seed=5), mode)
     randomize_bias(layer)
-    lo, hi = (-1.2, 1.2) if basis != "rbf" else (-2.5, 2.5)
+    lo, hi = (-2.5, 2.5) if basis in ("rbf", "relu") else (-1.2, 1.2)
     x = np.random.default_rng(B).uniform(lo, hi, (B, d_in)).astype(np.float32)
     y = layer.forward(x, path=PATHS["tc"])
     assert layer_err(y, layer, x, mode, basis) <= TOL[mode]
