@@ -57,6 +57,8 @@ TRAFFIC = {
                         "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b4096.md"},
     "c5:ternary:16": {"bytes": 53773568 + 152064,
                       "src": "profiles/kan_gemv_kernel_c5_ternary_bf16_b16.md"},
+    "c5:ternary:65536": {"bytes": 5865144576 + 527921408,
+                         "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b65536.md"},
 }
 
 
@@ -651,6 +653,12 @@ def main():
         roof["traffic_src"] = tr["src"] + (f" ({tr['note']})" if "note" in tr else "")
         if tr.get("scale"):
             roof["traffic_scale"] = tr["scale"]
+        if strong and w.bound == "tensor":
+            # the capture is of a full-batch launch; a rank's launch covers B / N rows, and the
+            # traffic of this tensor-bound kernel (input re-reads per N panel, output writes)
+            # grows with the rows it processes
+            roof["traffic"] = tr["bytes"] * B / w.B
+            roof["traffic_scale"] = f"{B}/{w.B} of the full-batch capture (this rank's rows)"
 
     # parity of the timed output (rank 0's rows; the gathered full output when output-sharded)
     parity = None

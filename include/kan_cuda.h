@@ -164,6 +164,36 @@ int metal_kan_jacobi_forward_fp16(const uint16_t* X, const uint16_t* W_jacobi,
                                   const uint16_t* W_base, const uint16_t* bias, uint16_t* Y, int B,
                                   int D_in, int D_out, int degree, float alpha, float beta,
                                   int has_base, int has_bias);
+/* metal_kan_bridge.mm:1700 -- MultKAN: an RBF layer to num_add + 2 num_mult internal outputs,
+ * then out[:, num_add + m] = internal[:, num_add + m] * internal[:, num_add + num_mult + m];
+ * D_out = num_add + num_mult, W_rbf / W_base / bias sized for the internal outputs */
+int metal_kan_mult_forward(const float* X, const float* W_rbf, const float* W_base,
+                           const float* grid, const float* bias, float* Y, int B, int D_in,
+                           int D_out, int num_add, int num_mult, int num_centers,
+                           float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2250 (grid is fp16 here, like the reference) */
+int metal_kan_mult_forward_fp16(const uint16_t* X, const uint16_t* W_rbf, const uint16_t* W_base,
+                                const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                int D_in, int D_out, int num_add, int num_mult, int num_centers,
+                                float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm:1535 -- LowRankKAN: Z = RBF layer to `rank` outputs (W_down, no base or
+ * bias), Y = bias + Z W_up^T + silu(X) W_base^T */
+int metal_kan_lowrank_forward(const float* X, const float* W_down, const float* W_up,
+                              const float* W_base, const float* grid, const float* bias, float* Y,
+                              int B, int D_in, int D_out, int rank, int num_centers,
+                              float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm:2153 */
+int metal_kan_lowrank_forward_fp16(const uint16_t* X, const uint16_t* W_down,
+                                   const uint16_t* W_up, const uint16_t* W_base,
+                                   const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                   int D_in, int D_out, int rank, int num_centers,
+                                   float inv_denominator, int has_base, int has_bias);
+/* metal_kan_bridge.mm:1004 -- RationalKAN (fp32 only, like the reference): per input feature
+ * P(xc) / (1 + |Q(xc)|) with Chebyshev expansions of xc = clamp(x, -1, 1) (W_p [D_out][D_in*p],
+ * W_q [D_out][D_in*q]) plus silu(xc) W_base; p, q in 0..16, 1 <= p + q <= 16 */
+int metal_kan_rational_forward(const float* X, const float* W_p, const float* W_q,
+                               const float* W_base, const float* bias, float* Y, int B, int D_in,
+                               int D_out, int p_degree, int q_degree, int has_base, int has_bias);
 
 /* Backward of one fp32 layer, host pointers, synchronous (the reference's training path).
  * dY [B][D_out], X [B][D_in] (the forward's input), W / Wb the layer's weights; outputs dW
@@ -231,6 +261,20 @@ double benchmark_metal_jacobi(const float* X, const float* W_jacobi, const float
                               const float* bias, float* Y, int B, int D_in, int D_out, int degree,
                               float alpha, float beta, int has_base, int has_bias, int warmup,
                               int iters);
+double benchmark_metal_mult(const float* X, const float* W_rbf, const float* W_base,
+                            const float* grid, const float* bias, float* Y, int B, int D_in,
+                            int D_out, int num_add, int num_mult, int num_centers,
+                            float inv_denominator, int has_base, int has_bias, int warmup,
+                            int iters);
+double benchmark_metal_lowrank(const float* X, const float* W_down, const float* W_up,
+                               const float* W_base, const float* grid, const float* bias, float* Y,
+                               int B, int D_in, int D_out, int rank, int num_centers,
+                               float inv_denominator, int has_base, int has_bias, int warmup,
+                               int iters);
+double benchmark_metal_rational(const float* X, const float* W_p, const float* W_q,
+                                const float* W_base, const float* bias, float* Y, int B, int D_in,
+                                int D_out, int p_degree, int q_degree, int has_base, int has_bias,
+                                int warmup, int iters);
 
 /* ------------------------------------------------------------------------------------------ */
 /* tier 2: device-resident engine (new)                                                       */
@@ -401,6 +445,19 @@ int kan_dequantize(const kan_weight* w, int rows, int cols, void* out, int out_d
 /* Elementwise: out = g * sigmoid(clamp(g,-20,20)) * u, dtype act_dtype, n elements. */
 int kan_swiglu(const void* gate, const void* up, void* out, long long n, int act_dtype,
                void* stream);
+/* MultKAN pair products on device buffers: in [B][num_add + 2 num_mult] -> out
+ * [B][num_add + num_mult] in `act_dtype` (metal_kan_bridge.mm:1788-1799). */
+int kan_mult_combine(const void* in, void* out, int B, int num_add, int num_mult, int act_dtype,
+                     void* stream);
+/* LowRankKAN second stage on device buffers: Y = bias + Z W_up^T + silu(X) W_base^T, Z [B][rank]
+ * the RBF stage's output (metal_kan_bridge.mm:1614-1636). */
+int kan_lowrank_up(const void* Z, const void* X, const void* W_up, const void* W_base,
+                   const void* bias, void* Y, int B, int D_in, int D_out, int rank, int has_base,
+                   int has_bias, int act_dtype, void* stream);
+/* RationalKAN on device buffers (fp32), as metal_kan_rational_forward. */
+int kan_rational_forward(const float* X, const float* W_p, const float* W_q, const float* W_base,
+                         const float* bias, float* Y, int B, int D_in, int D_out, int p_degree,
+                         int q_degree, int has_base, int has_bias, void* stream);
 /* Dtype conversion of n elements (any of KAN_F32/F16/BF16 to any). */
 int kan_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
                 void* stream);
@@ -425,6 +482,62 @@ int kan_device_error(int* code);
 
 /* Number of kernels this library launched since load (evidence counter for benchmarks). */
 long long kan_launch_count(void);
+
+/* ------------------------------------------------------------------------------------------ */
+/* training (fp32)                                                                             */
+/* ------------------------------------------------------------------------------------------ */
+/* Optimisers of kan_train_step / kan_optim_step; hyper = {lr, beta1, beta2, eps, weight_decay,
+ * lr_t} (SGD: beta1 = momentum; lr_t = lr * sqrt(1 - beta2^t) / (1 - beta1^t) for the Adams). */
+enum kan_optimizer { KAN_OPT_ADAMW = 0, KAN_OPT_ADAM = 1, KAN_OPT_SGD = 2, KAN_OPT_LION = 3 };
+/* One training step of a dense fp32 layer on device buffers (metal_kan_bridge.mm:3432-3640):
+ * forward, dY = (Y - target) * 2 / B (MSE), the weight / base / bias gradients, one optimiser
+ * update of the layer's tensors in place (their pointers in `layer` must be writable).  State:
+ * m (and v for the Adams) per tensor, NULL for absent base / bias. */
+int kan_train_step(const kan_layer* layer, const float* X, const float* target, int B,
+                   float* m_w, float* v_w, float* m_wb, float* v_wb, float* m_b, float* v_b,
+                   int optimizer, const float* hyper, int nesterov, void* stream);
+/* One optimiser update of n fp32 parameters on device buffers. */
+int kan_optim_step(int optimizer, float* param, const float* grad, float* m, float* v,
+                   long long n, const float* hyper, int nesterov, void* stream);
+/* metal_kan_bridge.mm (adamw_step, fused_kan.metal:1896) -- host pointers, updated in place */
+int metal_kan_adamw_step(float* param, const float* grad, float* m, float* v, float lr,
+                         float beta1, float beta2, float eps, float weight_decay, float lr_t,
+                         int n_elems);
+/* adam_coupled_step: weight decay added to the gradient */
+int metal_kan_adam_step(float* param, const float* grad, float* m, float* v, float lr,
+                        float beta1, float beta2, float eps, float weight_decay, float lr_t,
+                        int n_elems);
+/* sgd_step (fused_kan.metal:1923) */
+int metal_kan_sgd_step(float* param, const float* grad, float* velocity, float lr,
+                       float momentum, float weight_decay, int nesterov, int n_elems);
+/* lion_step (fused_kan.metal:1946) */
+int metal_kan_lion_step(float* param, const float* grad, float* m, float lr, float beta1,
+                        float beta2, float weight_decay, int n_elems);
+/* metal_kan_bridge.mm:3432 -- fused AdamW training step of a ChebyKAN layer, host pointers;
+ * weights and AdamW state updated in place */
+int metal_kan_cheby_train_step(const float* X, const float* target, float* W_cheby,
+                               float* W_base, float* bias, float* m_W, float* v_W, float* m_Wb,
+                               float* v_Wb, float* m_b, float* v_b, int B, int D_in, int D_out,
+                               int degree, int has_base, int has_bias, float lr, float beta1,
+                               float beta2, float eps, float weight_decay, float lr_t);
+/* FastKAN twin */
+int metal_kan_fastkan_train_step(const float* X, const float* target, float* W_rbf,
+                                 float* W_base, const float* grid, float* bias, float* m_W,
+                                 float* v_W, float* m_Wb, float* v_Wb, float* m_b, float* v_b,
+                                 int B, int D_in, int D_out, int num_centers,
+                                 float inv_denominator, int has_base, int has_bias, float lr,
+                                 float beta1, float beta2, float eps, float weight_decay,
+                                 float lr_t);
+/* metal_kan_bridge.mm:5148 -- the MSE loss gradient dY = (pred - target) * scale */
+int metal_kan_calc_mse_loss_backward(const float* pred, const float* target, float* dY,
+                                     int n_elems, float scale);
+/* BSplineKAN twin (uniform grid [grid_min, grid_max] of grid_size intervals) */
+int metal_kan_bspline_train_step(const float* X, const float* target, float* W_spline,
+                                 float* W_base, float* bias, float* m_W, float* v_W, float* m_Wb,
+                                 float* v_Wb, float* m_b, float* v_b, int B, int D_in, int D_out,
+                                 int grid_size, float grid_min, float grid_max, int has_base,
+                                 int has_bias, float lr, float beta1, float beta2, float eps,
+                                 float weight_decay, float lr_t);
 
 #ifdef __cplusplus
 }

@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -72,7 +73,8 @@ struct PendingCopy {
 // Engine scratch of one stream: packed tensor-core weights (when the caller passes none) and the
 // GatedKAN gate/up activations.  Kept per stream so that work queued on different streams never
 // shares a buffer.
-enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, SC_HX, SC_HY, SC_CC, NUM_SCRATCH };
+enum ScratchId { SC_TCW, SC_GATE, SC_UP, SC_PHI, SC_HX, SC_HY, SC_CC, SC_TY, SC_TDY, SC_TDW,
+                 SC_TDWB, SC_TDB, NUM_SCRATCH };
 struct Scratch {
   cudaStream_t stream = nullptr;
   void* ptr[NUM_SCRATCH] = {};
@@ -651,6 +653,51 @@ int kan_swiglu(const void* gate, const void* up, void* out, long long n, int act
   return KAN_OK;
 }
 
+int kan_mult_combine(const void* in, void* out, int B, int num_add, int num_mult,
+                     int act_dtype, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (B < 0 || num_add < 0 || num_mult < 0 || (B > 0 && (!in || !out)))
+    return fail(KAN_ERR_ARG, "mult_combine: bad args");
+  cudaError_t e = launch_mult_combine(in, out, B, num_add, num_mult, act_dtype,
+                                      pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "mult_combine: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_lowrank_up(const void* Z, const void* X, const void* Wup, const void* Wb,
+                   const void* bias, void* Y, int B, int D_in, int D_out, int rank, int has_base,
+                   int has_bias, int act_dtype, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (B < 0 || D_in <= 0 || D_out <= 0 || rank <= 0 ||
+      (B > 0 && (!Z || !Y || !Wup || (has_base && (!X || !Wb)) || (has_bias && !bias))))
+    return fail(KAN_ERR_ARG, "lowrank_up: bad args");
+  cudaError_t e = launch_lowrank_up(Z, X, Wup, Wb, bias, Y, B, D_in, D_out, rank, has_base,
+                                    has_bias, act_dtype, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "lowrank_up: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int kan_rational_forward(const float* X, const float* Wp, const float* Wq, const float* Wb,
+                         const float* bias, float* Y, int B, int D_in, int D_out, int p, int q,
+                         int has_base, int has_bias, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!rational_supported(p, q)) return fail(KAN_ERR_UNSUPPORTED, "rational: degrees");
+  if (B < 0 || D_in <= 0 || D_out <= 0 ||
+      (B > 0 && (!X || !Y || (p && !Wp) || (q && !Wq) || (has_base && !Wb) ||
+                 (has_bias && !bias))))
+    return fail(KAN_ERR_ARG, "rational: bad args");
+  cudaError_t e = launch_rational(X, Wp, Wq, Wb, bias, Y, B, D_in, D_out, p, q, has_base,
+                                  has_bias, pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "rational: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
 int kan_convert(const void* src, int src_dtype, void* dst, int dst_dtype, long long n,
                 void* stream) {
   DeviceState* d;
@@ -782,6 +829,9 @@ struct HostLayer {
   const void* hWb = nullptr;
   const void* hBias = nullptr;
   std::vector<float> grid, trans, isc;  // basis parameters, already fp32
+  // optional second stage on the device output: (state, device X, device Y of the layer) ->
+  // the buffer and size to copy back (MultKAN's pair products, LowRankKAN's up projection)
+  std::function<int(DeviceState*, void*, void*, void**, size_t*)> post;
 };
 
 static int run_host_layer(HostLayer& h) {
@@ -813,7 +863,10 @@ static int run_host_layer(HostLayer& h) {
   L.translation = (const float*)dT;
   L.inv_scale = (const float*)dS;
   if ((rc = run_forward(&L, dX, dY, h.B, KAN_PATH_AUTO, d->stream, d))) return rc;
-  return stage_out(d, h.Y, dY, (size_t)h.B * L.D_out * es);
+  void* dOut = dY;
+  size_t out_bytes = (size_t)h.B * L.D_out * es;
+  if (h.post && (rc = h.post(d, dX, dY, &dOut, &out_bytes))) return rc;
+  return stage_out(d, h.Y, dOut, out_bytes);
 }
 
 static kan_layer base_layer(int basis, int dt, int D_in, int D_out, int K, int hb, int hbi) {
@@ -999,6 +1052,119 @@ int metal_kan_jacobi_forward_fp16(const uint16_t* X, const uint16_t* W, const ui
   h.L.alpha = alpha;
   h.L.beta = beta;
   return run_host_layer(h);
+}
+
+// MultKAN (metal_kan_bridge.mm:1700-1802, fp16 :2250-2350): the RBF layer to num_add +
+// 2 num_mult internal outputs, then the pair products.  `grid` is in the layer dtype.
+static int mult_common(int dt, const void* X, const void* W, const void* Wb, const void* grid,
+                       const void* bias, void* Y, int B, int D_in, int D_out, int num_add,
+                       int num_mult, int K, float inv_den, int hb, int hbi) {
+  if (!grid || K <= 0) return fail(KAN_ERR_ARG, "mult: NULL grid");
+  if (num_add < 0 || num_mult < 0 || num_add + num_mult != D_out)
+    return fail(KAN_ERR_ARG, "mult: num_add + num_mult must equal D_out");
+  const int internal = num_add + 2 * num_mult;
+  HostLayer h{base_layer(KAN_RBF, dt, D_in, internal, K, hb, hbi), X, Y, B, W, Wb, bias};
+  h.L.inv_den = inv_den;
+  h.grid = dt == KAN_F16 ? half_to_float((const uint16_t*)grid, (size_t)K)
+                         : std::vector<float>((const float*)grid, (const float*)grid + K);
+  if (num_mult > 0) {
+    h.post = [=](DeviceState* d, void*, void* dIn, void** dOut, size_t* bytes) {
+      const size_t es = dtype_size(dt);
+      int rc = slot(d, S_T1, (size_t)B * D_out * es, dOut);
+      if (rc) return rc;
+      cudaError_t e = launch_mult_combine(dIn, *dOut, B, num_add, num_mult, dt, d->stream);
+      if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "mult combine: %s", cudaGetErrorString(e));
+      *bytes = (size_t)B * D_out * es;
+      return KAN_OK;
+    };
+  }
+  return run_host_layer(h);
+}
+
+int metal_kan_mult_forward(const float* X, const float* W, const float* Wb, const float* grid,
+                           const float* bias, float* Y, int B, int D_in, int D_out, int num_add,
+                           int num_mult, int K, float inv_den, int hb, int hbi) {
+  return mult_common(KAN_F32, X, W, Wb, grid, bias, Y, B, D_in, D_out, num_add, num_mult, K,
+                     inv_den, hb, hbi);
+}
+
+int metal_kan_mult_forward_fp16(const uint16_t* X, const uint16_t* W, const uint16_t* Wb,
+                                const uint16_t* grid, const uint16_t* bias, uint16_t* Y, int B,
+                                int D_in, int D_out, int num_add, int num_mult, int K,
+                                float inv_den, int hb, int hbi) {
+  return mult_common(KAN_F16, X, W, Wb, grid, bias, Y, B, D_in, D_out, num_add, num_mult, K,
+                     inv_den, hb, hbi);
+}
+
+// LowRankKAN (metal_kan_bridge.mm:1535-1698, fp16 :2153-2248): Z = RBF layer to `rank` outputs
+// (no base, no bias; Z in the layer dtype), then Y = bias + Z W_up^T + silu(x) W_base^T.
+static int lowrank_common(int dt, const void* X, const void* Wdown, const void* Wup,
+                          const void* Wb, const void* grid, const void* bias, void* Y, int B,
+                          int D_in, int D_out, int rank, int K, float inv_den, int hb, int hbi) {
+  if (!grid || K <= 0 || rank <= 0 || !Wup) return fail(KAN_ERR_ARG, "lowrank: bad arguments");
+  if (hb && !Wb) return fail(KAN_ERR_ARG, "lowrank: has_base with NULL W_base");
+  if (hbi && !bias) return fail(KAN_ERR_ARG, "lowrank: has_bias with NULL bias");
+  HostLayer h{base_layer(KAN_RBF, dt, D_in, rank, K, 0, 0), X, Y, B, Wdown, nullptr, nullptr};
+  h.L.inv_den = inv_den;
+  h.grid = dt == KAN_F16 ? half_to_float((const uint16_t*)grid, (size_t)K)
+                         : std::vector<float>((const float*)grid, (const float*)grid + K);
+  h.post = [=](DeviceState* d, void* dX, void* dZ, void** dOut, size_t* bytes) {
+    const size_t es = dtype_size(dt);
+    void *dWup, *dWb = nullptr, *dB = nullptr;
+    int rc;
+    if ((rc = stage_in(d, S_T0, Wup, (size_t)D_out * rank * es, &dWup))) return rc;
+    if (hb && (rc = stage_in(d, S_WB, Wb, (size_t)D_out * D_in * es, &dWb))) return rc;
+    if (hbi && (rc = stage_in(d, S_BIAS, bias, (size_t)D_out * es, &dB))) return rc;
+    if ((rc = slot(d, S_T1, (size_t)B * D_out * es, dOut))) return rc;
+    cudaError_t e = launch_lowrank_up(dZ, dX, dWup, dWb, dB, *dOut, B, D_in, D_out, rank, hb,
+                                      hbi, dt, d->stream);
+    if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "lowrank up: %s", cudaGetErrorString(e));
+    *bytes = (size_t)B * D_out * es;
+    return KAN_OK;
+  };
+  return run_host_layer(h);
+}
+
+int metal_kan_lowrank_forward(const float* X, const float* Wdown, const float* Wup,
+                              const float* Wb, const float* grid, const float* bias, float* Y,
+                              int B, int D_in, int D_out, int rank, int K, float inv_den, int hb,
+                              int hbi) {
+  return lowrank_common(KAN_F32, X, Wdown, Wup, Wb, grid, bias, Y, B, D_in, D_out, rank, K,
+                        inv_den, hb, hbi);
+}
+
+int metal_kan_lowrank_forward_fp16(const uint16_t* X, const uint16_t* Wdown,
+                                   const uint16_t* Wup, const uint16_t* Wb, const uint16_t* grid,
+                                   const uint16_t* bias, uint16_t* Y, int B, int D_in, int D_out,
+                                   int rank, int K, float inv_den, int hb, int hbi) {
+  return lowrank_common(KAN_F16, X, Wdown, Wup, Wb, grid, bias, Y, B, D_in, D_out, rank, K,
+                        inv_den, hb, hbi);
+}
+
+// RationalKAN (metal_kan_bridge.mm:1004-1067), fp32 only like the reference.
+int metal_kan_rational_forward(const float* X, const float* Wp, const float* Wq, const float* Wb,
+                               const float* bias, float* Y, int B, int D_in, int D_out, int p,
+                               int q, int hb, int hbi) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (B < 0 || D_in <= 0 || D_out <= 0) return fail(KAN_ERR_ARG, "rational: bad sizes");
+  if (!rational_supported(p, q)) return fail(KAN_ERR_UNSUPPORTED, "rational: degrees p, q in 0..16 with p + q in 1..16");
+  if (B == 0) return KAN_OK;
+  if (!X || !Y || (p && !Wp) || (q && !Wq) || (hb && !Wb) || (hbi && !bias))
+    return fail(KAN_ERR_ARG, "rational: NULL pointer");
+  void *dX, *dWp = nullptr, *dWq = nullptr, *dWb = nullptr, *dB = nullptr, *dY;
+  if ((rc = stage_in(d, S_X, X, (size_t)B * D_in * 4, &dX))) return rc;
+  if (p && (rc = stage_in(d, S_W, Wp, (size_t)D_out * D_in * p * 4, &dWp))) return rc;
+  if (q && (rc = stage_in(d, S_T0, Wq, (size_t)D_out * D_in * q * 4, &dWq))) return rc;
+  if (hb && (rc = stage_in(d, S_WB, Wb, (size_t)D_out * D_in * 4, &dWb))) return rc;
+  if (hbi && (rc = stage_in(d, S_BIAS, bias, (size_t)D_out * 4, &dB))) return rc;
+  if ((rc = slot(d, S_Y, (size_t)B * D_out * 4, &dY))) return rc;
+  cudaError_t e = launch_rational((const float*)dX, (const float*)dWp, (const float*)dWq,
+                                  (const float*)dWb, (const float*)dB, (float*)dY, B, D_in, D_out,
+                                  p, q, hb, hbi, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "rational launch: %s", cudaGetErrorString(e));
+  return stage_out(d, Y, dY, (size_t)B * D_out * 4);
 }
 
 int metal_kan_chain_pipeline_cheby(const float* X, float* Y, int B, int num_layers,
@@ -1326,6 +1492,34 @@ double benchmark_metal_jacobi(const float* X, const float* W, const float* Wb, c
   }, warmup, iters);
 }
 
+double benchmark_metal_mult(const float* X, const float* W, const float* Wb, const float* grid,
+                            const float* bias, float* Y, int B, int D_in, int D_out, int num_add,
+                            int num_mult, int K, float inv_den, int hb, int hbi, int warmup,
+                            int iters) {
+  return bench_loop([&] {
+    return metal_kan_mult_forward(X, W, Wb, grid, bias, Y, B, D_in, D_out, num_add, num_mult, K,
+                                  inv_den, hb, hbi);
+  }, warmup, iters);
+}
+
+double benchmark_metal_lowrank(const float* X, const float* Wdown, const float* Wup,
+                               const float* Wb, const float* grid, const float* bias, float* Y,
+                               int B, int D_in, int D_out, int rank, int K, float inv_den, int hb,
+                               int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_lowrank_forward(X, Wdown, Wup, Wb, grid, bias, Y, B, D_in, D_out, rank, K,
+                                     inv_den, hb, hbi);
+  }, warmup, iters);
+}
+
+double benchmark_metal_rational(const float* X, const float* Wp, const float* Wq,
+                                const float* Wb, const float* bias, float* Y, int B, int D_in,
+                                int D_out, int p, int q, int hb, int hbi, int warmup, int iters) {
+  return bench_loop([&] {
+    return metal_kan_rational_forward(X, Wp, Wq, Wb, bias, Y, B, D_in, D_out, p, q, hb, hbi);
+  }, warmup, iters);
+}
+
 }  // extern "C"
 
 // ==========================================================================================
@@ -1409,6 +1603,137 @@ static int run_host_backward(kan_layer L, const float* dY, const float* X, const
   if (oB) KAN_CUDA_TRY(cudaMemcpyAsync(dbias, oB, (size_t)L.D_out * 4, cudaMemcpyDeviceToHost,
                                        d->stream));
   KAN_CUDA_TRY(cudaMemcpyAsync(dX, oX, (size_t)B * L.D_in * 4, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return check_device_error(d);
+}
+
+// One fp32 training step on device buffers (metal_kan_bridge.mm:3432-3640 for the Chebyshev
+// layer; the FastKAN and B-spline steps are alike): forward, dY = (Y - T) * 2 / B, the weight,
+// base-weight and bias gradients (no input gradient), then one optimiser launch over the layer's
+// tensors -- which the layer's own weight pointers are, updated in place.
+static int run_train_step(DeviceState* d, cudaStream_t s, const kan_layer* L, const float* X,
+                          const float* T, int B, float* const* m, float* const* v, int op,
+                          const OptimHyper& h) {
+  if (!L) return fail(KAN_ERR_ARG, "train_step: NULL layer");
+  if (B <= 0 || !X || !T) return fail(KAN_ERR_ARG, "train_step: bad batch or NULL X / target");
+  if (L->act_dtype != KAN_F32) return fail(KAN_ERR_UNSUPPORTED, "train_step: fp32 layers only");
+  const int n_t = 1 + (L->has_base ? 1 : 0) + (L->has_bias ? 1 : 0);
+  for (int k = 0; k < n_t; ++k)
+    if (!m[k] || ((op == OPTIM_ADAMW || op == OPTIM_ADAM) && !v[k]))
+      return fail(KAN_ERR_ARG, "train_step: NULL optimiser state");
+  const size_t nw = (size_t)L->D_out * L->D_in * L->K, nb = (size_t)L->D_out * L->D_in;
+  void *Y, *dY, *dW, *dWb = nullptr, *db = nullptr;
+  int rc;
+  if ((rc = scratch_buf(d, s, SC_TY, (size_t)B * L->D_out * 4, false, &Y))) return rc;
+  if ((rc = scratch_buf(d, s, SC_TDY, (size_t)B * L->D_out * 4, false, &dY))) return rc;
+  if ((rc = scratch_buf(d, s, SC_TDW, nw * 4, false, &dW))) return rc;
+  if (L->has_base && (rc = scratch_buf(d, s, SC_TDWB, nb * 4, false, &dWb))) return rc;
+  if (L->has_bias && (rc = scratch_buf(d, s, SC_TDB, (size_t)L->D_out * 4, false, &db))) return rc;
+  BackwardArgs a;
+  if ((rc = make_backward_args(L, X, dY, nullptr, dW, dWb, db, B, &a))) return rc;
+  if ((rc = run_forward(L, X, Y, B, KAN_PATH_AUTO, s, d))) return rc;
+  cudaError_t e = launch_mse_grad((const float*)Y, T, (float*)dY, (long long)B * L->D_out,
+                                  2.0f / (float)B, s);
+  if (e == cudaSuccess) e = launch_backward(a, s);
+  float* params[3];
+  const float* grads[3];
+  long long n[3];
+  int c = 0;
+  params[c] = (float*)L->w.data, grads[c] = (const float*)dW, n[c++] = (long long)nw;
+  if (L->has_base) params[c] = (float*)L->wb.data, grads[c] = (const float*)dWb, n[c++] = (long long)nb;
+  if (L->has_bias) params[c] = (float*)L->bias, grads[c] = (const float*)db, n[c++] = L->D_out;
+  if (e == cudaSuccess) e = launch_optim(op, c, params, grads, m, v, n, h, s);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "train_step: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+static OptimHyper hyper_of(const float* hp, int nesterov) {
+  OptimHyper h = {hp[0], hp[1], hp[2], hp[3], hp[4], hp[5], nesterov};
+  return h;
+}
+
+// Host-pointer training step: stage the batch, the layer and its AdamW state, run, copy the
+// updated weights and state back (in place, as the reference's shared-memory buffers are).
+static int run_host_train_step(kan_layer L, const float* X, const float* T, float* W, float* Wb,
+                               float* bias, const float* grid, float* mW, float* vW, float* mWb,
+                               float* vWb, float* mb, float* vb, int B, const OptimHyper& h) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (B <= 0 || L.D_in <= 0 || L.D_out <= 0 || L.K <= 0 || !X || !T || !W || !mW || !vW)
+    return fail(KAN_ERR_ARG, "train_step: bad sizes or NULL pointer");
+  if ((L.has_base && (!Wb || !mWb || !vWb)) || (L.has_bias && (!bias || !mb || !vb)))
+    return fail(KAN_ERR_ARG, "train_step: NULL base / bias tensor or state");
+  const size_t nw = (size_t)L.D_out * L.D_in * L.K * 4, nb = (size_t)L.D_out * L.D_in * 4,
+               nbias = (size_t)L.D_out * 4;
+  void *dX, *dT, *dW, *dWb = nullptr, *dB = nullptr, *dG = nullptr;
+  void *dmW, *dvW, *dmWb = nullptr, *dvWb = nullptr, *dmb = nullptr, *dvb = nullptr;
+  if ((rc = stage_in(d, S_X, X, (size_t)B * L.D_in * 4, &dX))) return rc;
+  if ((rc = stage_in(d, S_DY, T, (size_t)B * L.D_out * 4, &dT))) return rc;
+  if ((rc = stage_in(d, S_W, W, nw, &dW))) return rc;
+  if ((rc = stage_in(d, S_DW, mW, nw, &dmW))) return rc;
+  if ((rc = stage_in(d, S_DWB, vW, nw, &dvW))) return rc;
+  if (L.has_base) {
+    if ((rc = stage_in(d, S_WB, Wb, nb, &dWb))) return rc;
+    if ((rc = stage_in(d, S_DBIAS, mWb, nb, &dmWb))) return rc;
+    if ((rc = stage_in(d, S_DX, vWb, nb, &dvWb))) return rc;
+  }
+  if (L.has_bias) {
+    if ((rc = stage_in(d, S_BIAS, bias, nbias, &dB))) return rc;
+    if ((rc = stage_in(d, S_SC, mb, nbias, &dmb))) return rc;
+    if ((rc = stage_in(d, S_BI, vb, nbias, &dvb))) return rc;
+  }
+  if (grid && (rc = stage_in(d, S_GRID, grid, (size_t)L.K * 4, &dG))) return rc;
+  L.w.format = KAN_W_DENSE;
+  L.w.data = dW;
+  L.wb.format = KAN_W_DENSE;
+  L.wb.data = dWb;
+  L.bias = dB;
+  L.grid = (const float*)dG;
+  float* m[3] = {(float*)dmW, nullptr, nullptr};
+  float* v[3] = {(float*)dvW, nullptr, nullptr};
+  int c = 1;
+  if (L.has_base) m[c] = (float*)dmWb, v[c++] = (float*)dvWb;
+  if (L.has_bias) m[c] = (float*)dmb, v[c++] = (float*)dvb;
+  if ((rc = run_train_step(d, d->stream, &L, (const float*)dX, (const float*)dT, B, m, v,
+                           OPTIM_ADAMW, h)))
+    return rc;
+  struct Back { void* host; const void* dev; size_t bytes; } back[9] = {
+      {W, dW, nw}, {mW, dmW, nw}, {vW, dvW, nw}, {Wb, dWb, L.has_base ? nb : 0},
+      {mWb, dmWb, L.has_base ? nb : 0}, {vWb, dvWb, L.has_base ? nb : 0},
+      {bias, dB, L.has_bias ? nbias : 0}, {mb, dmb, L.has_bias ? nbias : 0},
+      {vb, dvb, L.has_bias ? nbias : 0}};
+  for (const Back& b : back)
+    if (b.bytes) KAN_CUDA_TRY(cudaMemcpyAsync(b.host, b.dev, b.bytes, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return check_device_error(d);
+}
+
+// Host-pointer optimiser step on one tensor (the reference's metal_kan_*_step): param, m (and v)
+// updated in place.
+static int run_host_optim(int op, float* param, const float* grad, float* m, float* v, long long n,
+                          const OptimHyper& h) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (n < 0 || (n > 0 && (!param || !grad || !m || ((op == OPTIM_ADAMW || op == OPTIM_ADAM) && !v))))
+    return fail(KAN_ERR_ARG, "optimiser step: bad arguments");
+  if (n == 0) return KAN_OK;
+  const size_t bytes = (size_t)n * 4;
+  void *dp, *dg, *dm, *dv = nullptr;
+  if ((rc = stage_in(d, S_T0, param, bytes, &dp))) return rc;
+  if ((rc = stage_in(d, S_T1, grad, bytes, &dg))) return rc;
+  if ((rc = stage_in(d, S_SC, m, bytes, &dm))) return rc;
+  if (v && (rc = stage_in(d, S_BI, v, bytes, &dv))) return rc;
+  float* P[1] = {(float*)dp};
+  const float* G[1] = {(const float*)dg};
+  float* M[1] = {(float*)dm};
+  float* V[1] = {(float*)dv};
+  cudaError_t e = launch_optim(op, 1, P, G, M, V, &n, h, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "optimiser step: %s", cudaGetErrorString(e));
+  KAN_CUDA_TRY(cudaMemcpyAsync(param, dp, bytes, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaMemcpyAsync(m, dm, bytes, cudaMemcpyDeviceToHost, d->stream));
+  if (v) KAN_CUDA_TRY(cudaMemcpyAsync(v, dv, bytes, cudaMemcpyDeviceToHost, d->stream));
   KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
   return check_device_error(d);
 }
@@ -1510,6 +1835,131 @@ int metal_kan_swiglu_backward(const float* d_hidden, const float* gate, const fl
   if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "swiglu_backward: %s", cudaGetErrorString(e));
   KAN_CUDA_TRY(cudaMemcpyAsync(d_gate, dg, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
   KAN_CUDA_TRY(cudaMemcpyAsync(d_up, du, (size_t)n * 4, cudaMemcpyDeviceToHost, d->stream));
+  KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
+  return check_device_error(d);
+}
+
+// ---- training step and optimisers (fp32) ---------------------------------------------------
+
+int kan_train_step(const kan_layer* layer, const float* X, const float* target, int B,
+                   float* m_w, float* v_w, float* m_wb, float* v_wb, float* m_b, float* v_b,
+                   int optimizer, const float* hyper, int nesterov, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!hyper || optimizer < OPTIM_ADAMW || optimizer > OPTIM_LION)
+    return fail(KAN_ERR_ARG, "train_step: bad optimiser or NULL hyper-parameters");
+  if (layer && (layer->w.format != KAN_W_DENSE || (layer->has_base && layer->wb.format != KAN_W_DENSE)))
+    return fail(KAN_ERR_UNSUPPORTED, "train_step: dense weights only");
+  float* m[3] = {m_w, nullptr, nullptr};
+  float* v[3] = {v_w, nullptr, nullptr};
+  int c = 1;
+  if (layer && layer->has_base) m[c] = m_wb, v[c++] = v_wb;
+  if (layer && layer->has_bias) m[c] = m_b, v[c++] = v_b;
+  return run_train_step(d, pick_stream(stream, d), layer, X, target, B, m, v, optimizer,
+                        hyper_of(hyper, nesterov));
+}
+
+int kan_optim_step(int optimizer, float* param, const float* grad, float* m, float* v,
+                   long long n, const float* hyper, int nesterov, void* stream) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!hyper || optimizer < OPTIM_ADAMW || optimizer > OPTIM_LION || n < 0 ||
+      (n > 0 && (!param || !grad || !m ||
+                 ((optimizer == OPTIM_ADAMW || optimizer == OPTIM_ADAM) && !v))))
+    return fail(KAN_ERR_ARG, "optim_step: bad arguments");
+  if (n == 0) return KAN_OK;
+  float* P[1] = {param};
+  const float* G[1] = {grad};
+  float* M[1] = {m};
+  float* V[1] = {v};
+  cudaError_t e = launch_optim(optimizer, 1, P, G, M, V, &n, hyper_of(hyper, nesterov),
+                               pick_stream(stream, d));
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "optim_step: %s", cudaGetErrorString(e));
+  return KAN_OK;
+}
+
+int metal_kan_adamw_step(float* param, const float* grad, float* m, float* v, float lr,
+                         float beta1, float beta2, float eps, float weight_decay, float lr_t,
+                         int n) {
+  const OptimHyper h = {lr, beta1, beta2, eps, weight_decay, lr_t, 0};
+  return run_host_optim(OPTIM_ADAMW, param, grad, m, v, n, h);
+}
+
+int metal_kan_adam_step(float* param, const float* grad, float* m, float* v, float lr,
+                        float beta1, float beta2, float eps, float weight_decay, float lr_t,
+                        int n) {
+  const OptimHyper h = {lr, beta1, beta2, eps, weight_decay, lr_t, 0};
+  return run_host_optim(OPTIM_ADAM, param, grad, m, v, n, h);
+}
+
+int metal_kan_sgd_step(float* param, const float* grad, float* velocity, float lr,
+                       float momentum, float weight_decay, int nesterov, int n) {
+  const OptimHyper h = {lr, momentum, 0.f, 0.f, weight_decay, 0.f, nesterov ? 1 : 0};
+  return run_host_optim(OPTIM_SGD, param, grad, velocity, nullptr, n, h);
+}
+
+int metal_kan_lion_step(float* param, const float* grad, float* m, float lr, float beta1,
+                        float beta2, float weight_decay, int n) {
+  const OptimHyper h = {lr, beta1, beta2, 0.f, weight_decay, 0.f, 0};
+  return run_host_optim(OPTIM_LION, param, grad, m, nullptr, n, h);
+}
+
+int metal_kan_cheby_train_step(const float* X, const float* T, float* W, float* Wb, float* bias,
+                               float* mW, float* vW, float* mWb, float* vWb, float* mb, float* vb,
+                               int B, int D_in, int D_out, int degree, int hb, int hbi, float lr,
+                               float beta1, float beta2, float eps, float weight_decay,
+                               float lr_t) {
+  const OptimHyper h = {lr, beta1, beta2, eps, weight_decay, lr_t, 0};
+  return run_host_train_step(base_layer(KAN_CHEBY, KAN_F32, D_in, D_out, degree, hb, hbi), X, T,
+                             W, Wb, bias, nullptr, mW, vW, mWb, vWb, mb, vb, B, h);
+}
+
+int metal_kan_fastkan_train_step(const float* X, const float* T, float* W, float* Wb,
+                                 const float* grid, float* bias, float* mW, float* vW,
+                                 float* mWb, float* vWb, float* mb, float* vb, int B, int D_in,
+                                 int D_out, int num_centers, float inv_den, int hb, int hbi,
+                                 float lr, float beta1, float beta2, float eps,
+                                 float weight_decay, float lr_t) {
+  if (!grid) return fail(KAN_ERR_ARG, "fastkan train_step: NULL grid");
+  kan_layer L = base_layer(KAN_RBF, KAN_F32, D_in, D_out, num_centers, hb, hbi);
+  L.inv_den = inv_den;
+  const OptimHyper h = {lr, beta1, beta2, eps, weight_decay, lr_t, 0};
+  return run_host_train_step(L, X, T, W, Wb, bias, grid, mW, vW, mWb, vWb, mb, vb, B, h);
+}
+
+int metal_kan_bspline_train_step(const float* X, const float* T, float* W, float* Wb,
+                                 float* bias, float* mW, float* vW, float* mWb, float* vWb,
+                                 float* mb, float* vb, int B, int D_in, int D_out, int grid_size,
+                                 float grid_min, float grid_max, int hb, int hbi, float lr,
+                                 float beta1, float beta2, float eps, float weight_decay,
+                                 float lr_t) {
+  if (grid_size <= 0 || !(grid_max > grid_min))
+    return fail(KAN_ERR_ARG, "bspline train_step: bad grid");
+  kan_layer L = base_layer(KAN_BSPLINE, KAN_F32, D_in, D_out, grid_size + 3, hb, hbi);
+  L.grid_size = grid_size;
+  L.grid_min = grid_min;
+  L.inv_h = (float)grid_size / (grid_max - grid_min);  // metal_kan_bridge.mm bspline train step
+  const OptimHyper h = {lr, beta1, beta2, eps, weight_decay, lr_t, 0};
+  return run_host_train_step(L, X, T, W, Wb, bias, nullptr, mW, vW, mWb, vWb, mb, vb, B, h);
+}
+
+/* metal_kan_bridge.mm:5148 -- dY = (pred - target) * scale, host pointers */
+int metal_kan_calc_mse_loss_backward(const float* pred, const float* target, float* dY, int n,
+                                     float scale) {
+  DeviceState* d;
+  int rc = current_state(&d);
+  if (rc) return rc;
+  if (!pred || !target || !dY || n <= 0) return fail(KAN_ERR_ARG, "mse_loss_backward: bad arguments");
+  const size_t bytes = (size_t)n * 4;
+  void *dp, *dt, *dd;
+  if ((rc = stage_in(d, S_T0, pred, bytes, &dp))) return rc;
+  if ((rc = stage_in(d, S_T1, target, bytes, &dt))) return rc;
+  if ((rc = slot(d, S_SC, bytes, &dd))) return rc;
+  cudaError_t e = launch_mse_grad((const float*)dp, (const float*)dt, (float*)dd, n, scale, d->stream);
+  if (e != cudaSuccess) return fail(KAN_ERR_CUDA, "mse_loss_backward: %s", cudaGetErrorString(e));
+  KAN_CUDA_TRY(cudaMemcpyAsync(dY, dd, bytes, cudaMemcpyDeviceToHost, d->stream));
   KAN_CUDA_TRY(cudaStreamSynchronize(d->stream));
   return check_device_error(d);
 }

@@ -212,6 +212,7 @@ bool gemv_cc_supported(const LayerArgs& a, int act_dtype) {
   // the fixed-point basis matrix needs |phi| <= 1: every basis but Jacobi (whose polynomials
   // exceed 1 for alpha or beta > 0)
   if (a.basis == KAN_JACOBI) return false;
+  if (pre_smem_bytes(a.K) > 48 * 1024) return false;  // the pre-pass stages 64 features' terms
   const int fmt = a.w.format;
   if (fmt != KAN_W_TERNARY && fmt != KAN_W_INT8 && fmt != KAN_W_INT4) return false;
   const int gs = a.w.group_size;
@@ -250,17 +251,18 @@ int gemv_cc_splits(const LayerArgs& a) {
 template <int MODE>
 static void launch_phi(const LayerArgs& a, const cc::Params& p, cudaStream_t s) {
   const dim3 grid((unsigned)((a.D_in + cc::PRE_FEATURES - 1) / cc::PRE_FEATURES), (unsigned)a.B);
+  const size_t sm = (size_t)cc::pre_smem_bytes(a.K);
   switch (a.basis) {
-    case KAN_CHEBY: cc::cc_phi_kernel<MODE, KAN_CHEBY><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
-    case KAN_RBF: cc::cc_phi_kernel<MODE, KAN_RBF><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
+    case KAN_CHEBY: cc::cc_phi_kernel<MODE, KAN_CHEBY><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
+    case KAN_RBF: cc::cc_phi_kernel<MODE, KAN_RBF><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
     case KAN_BSPLINE:
-      cc::cc_phi_kernel<MODE, KAN_BSPLINE><<<grid, cc::PRE_THREADS, 0, s>>>(a, p);
+      cc::cc_phi_kernel<MODE, KAN_BSPLINE><<<grid, cc::PRE_THREADS, sm, s>>>(a, p);
       break;
     case KAN_WAVELET:
-      cc::cc_phi_kernel<MODE, KAN_WAVELET><<<grid, cc::PRE_THREADS, 0, s>>>(a, p);
+      cc::cc_phi_kernel<MODE, KAN_WAVELET><<<grid, cc::PRE_THREADS, sm, s>>>(a, p);
       break;
-    case KAN_RELU: cc::cc_phi_kernel<MODE, KAN_RELU><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
-    default: cc::cc_phi_kernel<MODE, KAN_FOURIER><<<grid, cc::PRE_THREADS, 0, s>>>(a, p); break;
+    case KAN_RELU: cc::cc_phi_kernel<MODE, KAN_RELU><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
+    default: cc::cc_phi_kernel<MODE, KAN_FOURIER><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
   }
 }
 

@@ -66,8 +66,8 @@ constexpr int THREADS = (NWARPS + 1) * 32;
 constexpr int STAGES = 4;
 constexpr int MAXB = 4;
 constexpr int PHI_E = 13;                     // fixed-point exponent of the basis terms
-constexpr int PRE_THREADS = 128;              // pre-pass: 4 warps x 64 features
-constexpr int PRE_FEATURES = 256;
+constexpr int PRE_THREADS = 64;               // pre-pass: one thread per input feature,
+constexpr int PRE_FEATURES = 64;              // 64 features (one base exponent chunk) per CTA
 
 struct Params {
   int fmt;                   // KAN_W_TERNARY / KAN_W_INT8 / KAN_W_INT4
@@ -194,66 +194,83 @@ __global__ void __launch_bounds__(PRE_THREADS) cc_phi_kernel(LayerArgs a, Params
     }
   }
 
-  // this warp's 64 features: basis terms (E = 13) and silu (E of the chunk)
-  const int f0 = blockIdx.x * PRE_FEATURES + warp * 64;
-  float sv[2];
-  float smax = 0.f;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int f = f0 + h * 32 + lane;
-    sv[h] = 0.f;
-    if (f < a.D_in) {
-      const float xm = map_input<MODE>(Act<MODE>::to_f(xrow[f]), a.input_map, mean, rstd);
-      Gen gen;
-      gen.init(xm, f, a);
-      for (int k = 0; k < K; ++k)
-        put_fixed(hi, lo, f * K + k, __float2int_rn(gen.next() * (float)(1 << PHI_E)), fast);
-      if (a.has_base) sv[h] = silu_value<MODE>(xm);
-      smax = fmaxf(smax, fabsf(sv[h]));
+  // this CTA's 64 features, one per thread: the basis terms (E = 13) and silu (E of the chunk)
+  // are put in fixed point into shared memory in the main kernel's byte order, then copied out
+  // with 16-byte stores and summed per unit there -- no read-back of scattered global bytes
+  extern __shared__ __align__(16) int8_t pre_smem[];
+  const int wcodes = PRE_FEATURES * K;  // this CTA's basis codes: a whole number of 64-code groups
+  int8_t* s_hi = pre_smem;
+  int8_t* s_lo = pre_smem + wcodes + PRE_FEATURES;
+  __shared__ float s_max[PRE_THREADS / 32];
+  const int f0 = blockIdx.x * PRE_FEATURES, f = f0 + tid;
+  const bool valid = f < a.D_in;
+  float xm = 0.f;
+  if (valid) xm = map_input<MODE>(Act<MODE>::to_f(xrow[f]), a.input_map, mean, rstd);
+  {
+    Gen gen;
+    if (valid) gen.init(xm, f, a);
+    for (int k = 0; k < K; ++k) {
+      const int q = valid ? __float2int_rn(gen.next() * (float)(1 << PHI_E)) : 0;
+      put_fixed(s_hi, s_lo, tid * K + k, q, fast);
     }
   }
-  if (a.has_base && f0 < a.D_in) {
-    for (int o = 16; o; o >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
-    const int e = fixed_exponent(smax);
-    const float sc = exp2f((float)e);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int f = f0 + h * 32 + lane;
-      if (f < a.D_in)
-        put_fixed(hi + p.units_w * 16, lo + p.units_w * 16, f, __float2int_rn(sv[h] * sc), fast);
-    }
-    if (lane < 4 && f0 / 16 + lane < p.units_b)
-      p.p2b[(size_t)n * p.units_b + f0 / 16 + lane] = exp2f((float)-e);
+  const float sv = (valid && a.has_base) ? silu_value<MODE>(xm) : 0.f;
+  float smax = fabsf(sv);
+  for (int o = 16; o; o >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, o));
+  if (lane == 0) s_max[warp] = smax;
+  __syncthreads();
+  smax = 0.f;
+  for (int w = 0; w < PRE_THREADS / 32; ++w) smax = fmaxf(smax, s_max[w]);
+  const int e = fixed_exponent(smax);
+  put_fixed(s_hi + wcodes, s_lo + wcodes, tid, __float2int_rn(sv * exp2f((float)e)), fast);
+  __syncthreads();
+
+  // basis units [f0 K / 16, + 4 K) (clamped to the row's units) and the 4 base units
+  const int u_lo = f0 * K / 16, nunits = wcodes / 16;
+  for (int i = tid; i < nunits; i += PRE_THREADS) {
+    const int u = u_lo + i;
+    if (u >= p.units_w) break;
+    reinterpret_cast<uint4*>(hi)[u] = reinterpret_cast<const uint4*>(s_hi)[i];
+    reinterpret_cast<uint4*>(lo)[u] = reinterpret_cast<const uint4*>(s_lo)[i];
   }
-  if (!need_sums || f0 >= a.D_in) return;
-  // exact basis sum of each unit this warp wrote (its own global writes, ordered by the warp
-  // barrier); codes past the real ones are skipped, whatever the padding holds.  INT8/INT4 keep
-  // the real value (times the minimum of the group), in-place ternary the fixed-point integer
-  // (subtracted from the integer sum: value c - 1)
-  __syncwarp();
-  const int ulo = f0 * K / 16, uhi = min((f0 + 64) * K, kdim + 15) / 16;
-  for (int u = ulo + lane; u < uhi && u < p.units_w; u += 32) {
-    int acc = 0;
-    for (int j = 0; j < 16; ++j) {
-      const int c = u * 16 + j;
-      if (c >= kdim) break;
-      const int pos = u * 16 + unit_pos(j, fast);
-      acc += 128 * (int)hi[pos] + (int)lo[pos];
-    }
-    sum[u] = fast ? (float)acc : (float)acc * (1.0f / (float)(1 << PHI_E));
+  const int ub = f0 / 16 + tid;  // base units of this CTA (tid < 4)
+  if (a.has_base && tid < PRE_FEATURES / 16 && ub < p.units_b) {
+    reinterpret_cast<uint4*>(hi + p.units_w * 16)[ub] = reinterpret_cast<const uint4*>(s_hi + wcodes)[tid];
+    reinterpret_cast<uint4*>(lo + p.units_w * 16)[ub] = reinterpret_cast<const uint4*>(s_lo + wcodes)[tid];
+    p.p2b[(size_t)n * p.units_b + ub] = exp2f((float)-e);
   }
-  if (a.has_base && lane < 4) {
-    const int u = f0 / 16 + lane;
-    if (u < p.units_b && u * 16 < a.D_in) {
-      int acc = 0;
-      for (int j = 0; j < 16 && u * 16 + j < a.D_in; ++j) {
-        const int pos = p.units_w * 16 + u * 16 + unit_pos(j, fast);
-        acc += 128 * (int)hi[pos] + (int)lo[pos];
-      }
-      sum[p.units_w + u] = fast ? (float)acc : (float)acc * p.p2b[(size_t)n * p.units_b + u];
-    }
+  if (!need_sums) return;
+  // basis sum of each flush group (p.fu units, the codes the main kernel converts at once),
+  // stored at the group's first unit.  Shared memory holds zeros for features past D_in, so
+  // every unit sums all 16 positions.  INT8/INT4 keep the real value (times the minimum of the
+  // group), in-place ternary the fixed-point integer (subtracted from the integer sum: value
+  // c - 1).  A group is fu consecutive threads (fu divides 4; a CTA's range is whole groups).
+  const int fu = p.fu;
+  auto unit_sum = [&](const int8_t* h8, const int8_t* l8, int i) {
+    const uint4 h = reinterpret_cast<const uint4*>(h8)[i];
+    const uint4 l = reinterpret_cast<const uint4*>(l8)[i];
+    const uint32_t one = 0x01010101u;
+    const int sh = dp4a_ss(h.x, one, dp4a_ss(h.y, one, dp4a_ss(h.z, one, dp4a_ss(h.w, one, 0))));
+    const int sl = dp4a_ss(l.x, one, dp4a_ss(l.y, one, dp4a_ss(l.z, one, dp4a_ss(l.w, one, 0))));
+    return 128 * sh + sl;
+  };
+  for (int i0 = 0; i0 < nunits; i0 += PRE_THREADS) {
+    const int i = i0 + tid, u = u_lo + i;
+    int acc = i < nunits ? unit_sum(s_hi, s_lo, i) : 0;
+    for (int o = 1; o < fu; o <<= 1) acc += __shfl_down_sync(0xffffffffu, acc, o, fu);
+    if (i < nunits && u < p.units_w && u % fu == 0)
+      sum[u] = fast ? (float)acc : (float)acc * (1.0f / (float)(1 << PHI_E));
+  }
+  if (a.has_base) {
+    int acc = tid < PRE_FEATURES / 16 ? unit_sum(s_hi + wcodes, s_lo + wcodes, tid) : 0;
+    for (int o = 1; o < fu; o <<= 1) acc += __shfl_down_sync(0xffffffffu, acc, o, fu);
+    if (tid < PRE_FEATURES / 16 && ub < p.units_b && ub % fu == 0)
+      sum[p.units_w + ub] = fast ? (float)acc : (float)acc * exp2f((float)-e);
   }
 }
+
+// Dynamic shared memory of the pre-pass: hi and lo bytes of 64 features' K terms and silu.
+__host__ __device__ inline int pre_smem_bytes(int K) { return 2 * (PRE_FEATURES * K + PRE_FEATURES); }
 
 // ---------------------------------------------------------------------------------------------
 // main kernel
@@ -323,6 +340,7 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
   constexpr bool SUMS = AFFINE || FAST;                // unit sums of the basis are used
   constexpr bool SIGNED = FMT == KAN_W_TERNARY && !FAST;  // decoded bytes are signed
   constexpr int UPC = FMT == KAN_W_TERNARY ? 4 : (FMT == KAN_W_INT4 ? 2 : 1);  // units/chunk
+  constexpr int ups = ROW_BYTES / 16 * UPC;  // units per stage
   static_assert(UPC % FU == 0, "a flush covers whole units of one chunk");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -337,7 +355,6 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
   const int rb = blockIdx.x, z = blockIdx.y;
   const int st0 = (int)((long long)p.nst * z / p.S), st1 = (int)((long long)p.nst * (z + 1) / p.S);
   const int nmine = st1 - st0;
-  const int ups = p.ups;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -502,9 +519,9 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
 #pragma unroll
         for (int n = 0; n < NB; ++n) {
           int H, L;
-          if (FAST) {  // chain f holds 4^f * sum(c v)
-            H = ((ch[n][0] * 4 + ch[n][1]) * 4 + ch[n][2]) * 4 + ch[n][3];
-            L = ((ch[n][4] * 4 + ch[n][5]) * 4 + ch[n][6]) * 4 + ch[n][7];
+          if (FAST) {  // chain f holds 4^f * sum(c v): H = 64 * sum over the four chains
+            H = (ch[n][0] * 4 + ch[n][1]) * 16 + (ch[n][2] * 4 + ch[n][3]);
+            L = (ch[n][4] * 4 + ch[n][5]) * 16 + (ch[n][6] * 4 + ch[n][7]);
           } else {
             H = (ch[n][0] + ch[n][1]) + (ch[n][2] + ch[n][3]);
             L = (ch[n][4] + ch[n][5]) + (ch[n][6] + ch[n][7]);
@@ -512,12 +529,8 @@ __global__ void __launch_bounds__(THREADS) kan_gemv_cc_kernel(
           int tot = H * 128 + L;
           if (FAST) tot >>= 6;  // exact: a multiple of 64
           float v = (float)tot;
-          float sp = 0.f;
-          if (SUMS) {
-            const float* an = atile + (2 * n) * ups + ul0;
-#pragma unroll
-            for (int jj = 0; jj < FU; ++jj) sp += an[jj];
-          }
+          // the basis sum of the FU units (pre-summed by the pre-pass at the first unit)
+          const float sp = SUMS ? atile[(2 * n) * ups + ul0] : 0.f;
           if (FAST) v -= sp;  // value c - 1
           const float sc = seg ? s * atile[(2 * n + 1) * ups + ul0] : s * (1.0f / (1 << PHI_E));
           acc[n] = fmaf(v, sc, acc[n]);

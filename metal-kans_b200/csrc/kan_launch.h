@@ -80,6 +80,28 @@ bool backward_supported(const BackwardArgs& a);
 cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s);
 cudaError_t launch_swiglu_backward(const float* dh, const float* g, const float* u, float* dg,
                                    float* du, long long n, cudaStream_t s);
+// kan_extra.cu: MultKAN pair products, LowRankKAN up projection (+ base branch), RationalKAN
+cudaError_t launch_mult_combine(const void* in, void* out, int B, int num_add, int num_mult,
+                                int act_dtype, cudaStream_t s);
+cudaError_t launch_lowrank_up(const void* Z, const void* X, const void* Wup, const void* Wb,
+                              const void* bias, void* Y, int B, int D_in, int D_out, int rank,
+                              int has_base, int has_bias, int act_dtype, cudaStream_t s);
+bool rational_supported(int p, int q);
+cudaError_t launch_rational(const float* X, const float* Wp, const float* Wq, const float* Wb,
+                            const float* bias, float* Y, int B, int D_in, int D_out, int p, int q,
+                            int has_base, int has_bias, cudaStream_t s);
+// kan_train.cu: MSE loss gradient and the optimiser updates of the fp32 training step
+enum { OPTIM_ADAMW = 0, OPTIM_ADAM = 1, OPTIM_SGD = 2, OPTIM_LION = 3 };
+struct OptimHyper {
+  float lr, beta1, beta2, eps, weight_decay, lr_t;  // SGD: beta1 = momentum
+  int nesterov;
+};
+cudaError_t launch_mse_grad(const float* pred, const float* target, float* dY, long long n,
+                            float scale, cudaStream_t s);
+// `count` (1..3) tensors in one launch; v may be null for SGD and Lion
+cudaError_t launch_optim(int op, int count, float* const* param, const float* const* grad,
+                         float* const* m, float* const* v, const long long* n,
+                         const OptimHyper& h, cudaStream_t s);
 // kan_misc.cu
 cudaError_t launch_dequantize(const kan_weight& w, int rows, int cols, void* out, int out_dtype,
                               cudaStream_t s);

@@ -204,23 +204,29 @@ static cudaError_t launch_simt_mode(const LayerArgs& a, cudaStream_t s) {
 // A CTA computes an 8-row x BN-column tile (BN = 64, or 32 when the grid of 64-wide tiles would
 // not cover the SMs).  K runs in chunks of 64 columns -- the basis segment (W, basis values) then
 // the base segment (W_base, silu values) -- and each chunk of the panel, [BN][64] fp32, is copied
-// by 16-byte cp.async into stage t % 4 three chunks ahead of its use, so the L2 round trips of
-// several chunks overlap each other and the FMAs.  While a chunk's copies are in flight the
-// threads evaluate that chunk's 8 x 64 basis values into its A stage.  The four warps split each
-// chunk's columns (16 each); a lane owns one or two output columns for all 8 rows, reads its
+// by 16-byte cp.async into stage t % S (S = 8 for BN = 32, 4 for BN = 64) S - 1 chunks ahead of
+// its use, so the L2 round trips of several chunks overlap each other and the FMAs.  Layers of at
+// most 16 chunks build their whole 8-row basis tile once, after the first S - 1 chunks' copies
+// are issued (the input and weight latencies overlap); longer ones evaluate each chunk's 8 x 64
+// basis values into a ring of A stages while its copies are in flight.  The eight warps split each
+// chunk's columns (8 each: short dependent chains per warp, which bound this latency-limited
+// kernel); a lane owns one or two output columns for all 8 rows, reads its
 // weights as float4 (row pitch 68 floats: conflict-free) and the basis values as float4
 // broadcasts, and the warps' partial tiles are summed in warp order at the end.
 // ---------------------------------------------------------------------------------------------
 constexpr int DN_BM = 8;
 constexpr int DN_KC = 64;
 constexpr int DN_PITCH = DN_KC + 4;
-constexpr int DN_STAGES = 4;
-constexpr int DN_THREADS = 128;
+constexpr int DN_THREADS = 256;
+constexpr int DN_COLS_PER_WARP = DN_KC / (DN_THREADS / 32);  // chunk columns per warp (8)
 constexpr int DN_ACHUNKS = 16;  // basis-tile chunks kept: all of them when the layer has <= 16
+// Weight-ring depth: 8 chunks for 32-wide tiles (the small-grid case, where the whole K loop of a
+// short layer is then one memory latency), 4 for 64-wide tiles (shared memory).
+template <int BN> struct DnStages { static constexpr int value = BN == 32 ? 8 : 4; };
 
 template <int BN>
 struct DnSmem {
-  float W[DN_STAGES][BN][DN_PITCH];
+  float W[DnStages<BN>::value][BN][DN_PITCH];
   // the whole basis tile (T <= 16 chunks: built once, before the K loop) or a ring of 4 chunks
   float A[DN_ACHUNKS][DN_BM][DN_PITCH];
   float red[DN_THREADS / 32][DN_BM][BN];
@@ -236,6 +242,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int sr
 template <int BASIS, int BN>
 __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a) {
   using Gen = typename GenFor<BASIS, MODE_F32>::type;
+  constexpr int DN_STAGES = DnStages<BN>::value;
   extern __shared__ __align__(16) uint8_t dn_raw[];
   DnSmem<BN>& sm = *reinterpret_cast<DnSmem<BN>*>(dn_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -247,30 +254,13 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
   const float* W = (const float*)a.w.data;
   const float* Wb = (const float*)a.wb.data;
 
-  if (a.input_map == KAN_MAP_LAYERNORM) row_stats<MODE_F32>(a, row0, DN_BM, sm.mean, sm.rstd);
+  if (a.input_map == KAN_MAP_LAYERNORM) {
+    row_stats<MODE_F32>(a, row0, DN_BM, sm.mean, sm.rstd);
+    __syncthreads();
+  }
   // whole basis tile at once when it fits: every input load of the CTA is in flight together
   // (one memory latency) instead of one dependent round trip per chunk
   const bool whole_a = T <= DN_ACHUNKS;
-  if (whole_a) {
-    for (int e = tid; e < T * DN_BM * DN_PITCH; e += DN_THREADS) (&sm.A[0][0][0])[e] = 0.f;
-  }
-  __syncthreads();
-  if (whole_a) {
-    for (int it = tid; it < DN_BM * a.D_in; it += DN_THREADS) {
-      const int r = it / a.D_in, i = it % a.D_in;
-      const int row = row0 + r;
-      if (row >= a.B) continue;
-      const float xm = map_input<MODE_F32>(X[(size_t)row * a.D_in + i], a.input_map, sm.mean[r],
-                                           sm.rstd[r]);
-      Gen g;
-      g.init(xm, i, a);
-      for (int k = 0; k < a.K; ++k) {
-        const int c = i * a.K + k;
-        sm.A[c / DN_KC][r][c % DN_KC] = g.next();
-      }
-      if (a.has_base) sm.A[Tw + i / DN_KC][r][i % DN_KC] = silu_value<MODE_F32>(xm);
-    }
-  }
 
   // issue the copies of chunk t's weight panel and (ring mode) build its basis tile
   auto prepare = [&](int t) {
@@ -327,10 +317,41 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
 #pragma unroll
     for (int j = 0; j < NJ; ++j) acc[r][j] = 0.f;
 
+  // the first chunks' weight copies go out before the basis tile is built, so that the two
+  // memory latencies (weights from L2/HBM, inputs for the basis) overlap
 #pragma unroll 1
   for (int t = 0; t < DN_STAGES - 1; ++t) {
     if (t < T) prepare(t);
     asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  if (whole_a) {
+    // every row of the tile is written (zeros past B), and the columns past the last basis and
+    // base column of their chunks are zeroed; the K loop's first barrier publishes the tile
+    for (int it = tid; it < DN_BM * a.D_in; it += DN_THREADS) {
+      const int r = it / a.D_in, i = it % a.D_in;
+      const int row = row0 + r;
+      const bool ok = row < a.B;
+      Gen g;
+      float xm = 0.f;
+      if (ok) {
+        xm = map_input<MODE_F32>(X[(size_t)row * a.D_in + i], a.input_map, sm.mean[r],
+                                 sm.rstd[r]);
+        g.init(xm, i, a);
+      }
+      for (int k = 0; k < a.K; ++k) {
+        const int c = i * a.K + k;
+        sm.A[c / DN_KC][r][c % DN_KC] = ok ? g.next() : 0.f;
+      }
+      if (a.has_base) sm.A[Tw + i / DN_KC][r][i % DN_KC] = ok ? silu_value<MODE_F32>(xm) : 0.f;
+    }
+    const int tail_w = Tw * DN_KC - Kw;  // unused columns of the last basis chunk
+    for (int it = tid; it < DN_BM * tail_w; it += DN_THREADS)
+      sm.A[Tw - 1][it / tail_w][DN_KC - tail_w + it % tail_w] = 0.f;
+    if (a.has_base) {
+      const int tail_b = (T - Tw) * DN_KC - a.D_in;
+      for (int it = tid; it < DN_BM * tail_b; it += DN_THREADS)
+        sm.A[T - 1][it / tail_b][DN_KC - tail_b + it % tail_b] = 0.f;
+    }
   }
 #pragma unroll 1
   for (int i = 0; i < T; ++i) {
@@ -342,8 +363,8 @@ __global__ void __launch_bounds__(DN_THREADS) kan_simt_dense_kernel(LayerArgs a)
     const int st = i % DN_STAGES;
     const int sa = whole_a ? i : st;  // basis-tile chunk
 #pragma unroll
-    for (int s4 = 0; s4 < 4; ++s4) {
-      const int c = warp * 16 + s4 * 4;
+    for (int s4 = 0; s4 < DN_COLS_PER_WARP / 4; ++s4) {
+      const int c = warp * DN_COLS_PER_WARP + s4 * 4;
       float4 wv[NJ];
 #pragma unroll
       for (int j = 0; j < NJ; ++j) wv[j] = *reinterpret_cast<const float4*>(&sm.W[st][lane + 32 * j][c]);
@@ -386,7 +407,7 @@ template <int BASIS, int BN>
 static cudaError_t launch_dense_basis(const LayerArgs& a, cudaStream_t s) {
   const dim3 grid((a.D_out + BN - 1) / BN, (a.B + DN_BM - 1) / DN_BM);
   const int smem = (int)sizeof(DnSmem<BN>);
-  static std::atomic<unsigned long long> configured{0};
+  static std::atomic<unsigned long long> configured{0};  // per device: smem limit raised
   cudaError_t e = ensure_smem_attr(kan_simt_dense_kernel<BASIS, BN>, smem, configured);
   if (e != cudaSuccess) return e;
   kan_simt_dense_kernel<BASIS, BN><<<grid, DN_THREADS, smem, s>>>(a);

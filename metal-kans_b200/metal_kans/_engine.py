@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
+import weakref
 from typing import Dict, Optional, Tuple
 
 import numpy as np
@@ -202,6 +203,20 @@ def flush_pending() -> None:
 # ---------------------------------------------------------------------------------------------
 # layers: read-only weights mirrored on the device
 # ---------------------------------------------------------------------------------------------
+_PARAM_OWNERS: dict = {}
+
+
+def param_updated(arr) -> None:
+    """Tell the layer owning weight array ``arr`` (as handed out by its parameters()) that the
+    array was changed in place: its device copy is refreshed before the next forward."""
+    ent = _PARAM_OWNERS.get(id(arr))
+    if ent is None:
+        return
+    owner = ent[0]()
+    if owner is not None and getattr(owner, ent[1], None) is arr:
+        owner._bump(ent[1])
+
+
 class DeviceLayerMixin:
     """Weight attributes named in ``_WEIGHTS`` are stored read-only and mirrored on the device."""
 
@@ -224,6 +239,20 @@ class DeviceLayerMixin:
 
     def _version(self, name: str) -> int:
         return self.__dict__.get("_versions", {}).get(name, 0)
+
+    def _bump(self, name: str) -> None:
+        """The host array of weight ``name`` was changed in place (an optimiser step): a new
+        version, so that the device copies and packed weights of the old one are not used."""
+        vers = self.__dict__.setdefault("_versions", {})
+        vers[name] = vers.get(name, 0) + 1
+        self.__dict__["_pver"] = self.__dict__.get("_pver", 0) + 1
+
+    def _register_param(self, name: str):
+        """The weight array of ``name``, recorded so that an optimiser can report in-place
+        updates of it (parameters() of the layers)."""
+        arr = getattr(self, name)
+        _PARAM_OWNERS[id(arr)] = (weakref.ref(self), name)
+        return arr
 
     def _dev(self, name: str, dtype=None) -> DeviceBuffer:
         """Device copy of weight ``name`` (optionally cast to ``dtype``), uploaded when stale."""

@@ -237,15 +237,76 @@ class KANLayerBase(E.DeviceLayerMixin):
     def parameters(self):
         """(param, grad) pairs of the trainable arrays (fast_kan.py:80-87)."""
         d = self.__dict__
-        params = [(getattr(self, self.MAIN), d.get("grad_" + self.MAIN))]
+        params = [(self._register_param(self.MAIN), d.get("grad_" + self.MAIN))]
         if self.has_base and d.get("grad_w_base") is not None:
-            params.append((self.w_base, d["grad_w_base"]))
+            params.append((self._register_param("w_base"), d["grad_w_base"]))
         if self.has_bias and d.get("grad_bias") is not None:
-            params.append((self.bias, d["grad_bias"]))
+            params.append((self._register_param("bias"), d["grad_bias"]))
         return params
 
-    def train_step(self, *args, **kwargs):
-        raise NotImplementedError("the fused training step is not built in this engine")
+    def _train_call(self, lib, x, target, W, Wb, bias, st, hyper):
+        """The bridge's fused training step for this basis (subclasses)."""
+        raise NotImplementedError(f"{type(self).__name__} has no fused training step in the "
+                                  "reference")
+
+    def train_step(self, x: np.ndarray, target: np.ndarray, lr: float = 1e-3, beta1: float = 0.9,
+                   beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.01,
+                   opt_state: Optional[dict] = None, optimizer=None, **kwargs) -> float:
+        """Fused training step on the GPU (cheby_kan.py:258-343): forward, MSE gradient
+        (2/B (y - target)), weight / base / bias gradients and an AdamW update, in one call.
+        The AdamW moments live in ``opt_state`` (or the layer's ``_fused_opt_state``) as the
+        reference keeps them; returns 0.0 like the reference."""
+        import math
+
+        if optimizer is not None:
+            lr = getattr(optimizer, "lr", lr)
+            beta1 = getattr(optimizer, "beta1", beta1)
+            beta2 = getattr(optimizer, "beta2", beta2)
+            eps = getattr(optimizer, "eps", eps)
+            weight_decay = getattr(optimizer, "weight_decay", weight_decay)
+        if self.dtype != np.float32:
+            raise RuntimeError("train_step runs on fp32 layers (the reference trains in fp32)")
+        if getattr(self, "input_map", "none") not in (None, "none", "clamp"):
+            raise NotImplementedError("train_step takes the raw input (no tanh / LayerNorm map)")
+        x = np.ascontiguousarray(np.asarray(x, np.float32).reshape(-1, self.in_features))
+        target = np.ascontiguousarray(np.asarray(target, np.float32).reshape(x.shape[0], -1))
+        if target.shape[1] != self.out_features:
+            raise ValueError(f"target has {target.shape[1]} columns, expected {self.out_features}")
+        main = getattr(self, self.MAIN)
+        if opt_state is None:
+            st = self.__dict__.get("_fused_opt_state")
+            if st is None:
+                z = lambda a, on: np.zeros_like(a, np.float32) if on else np.zeros((1,), np.float32)  # noqa: E731
+                st = {"m_w": np.zeros_like(main, np.float32), "v_w": np.zeros_like(main, np.float32),
+                      "m_wb": z(self.w_base, self.has_base), "v_wb": z(self.w_base, self.has_base),
+                      "m_b": z(self.bias, self.has_bias), "v_b": z(self.bias, self.has_bias),
+                      "step": 0}
+                self.__dict__["_fused_opt_state"] = st
+        else:
+            st = opt_state
+        st["step"] += 1
+        t = st["step"]
+        lr_t = lr * math.sqrt(1.0 - beta2 ** t) / (1.0 - beta1 ** t)
+        # writable copies, updated in place by the step and assigned back (a new weight version:
+        # the device copies are refreshed on the next forward)
+        W = np.array(main, np.float32)
+        Wb = np.array(self.w_base, np.float32) if self.has_base else None
+        bias = np.array(self.bias, np.float32) if self.has_bias else None
+        self._train_call(E.lib(), x, target, W, Wb, bias, st,
+                         (lr, beta1, beta2, eps, weight_decay, lr_t))
+        setattr(self, self.MAIN, W)
+        if self.has_base:
+            self.w_base = Wb
+        if self.has_bias:
+            self.bias = bias
+        return 0.0
+
+    @staticmethod
+    def _train_ptrs(W, Wb, bias, st, has_base, has_bias):
+        P = lambda a, on=True: a.ctypes.data if (a is not None and on) else None  # noqa: E731
+        return (P(W), P(Wb, has_base), P(bias, has_bias), P(st["m_w"]), P(st["v_w"]),
+                P(st["m_wb"], has_base), P(st["v_wb"], has_base), P(st["m_b"], has_bias),
+                P(st["v_b"], has_bias))
 
     def _benchmark_fallback(self, x, warmup, iters):
         import time

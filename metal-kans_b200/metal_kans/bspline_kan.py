@@ -53,6 +53,14 @@ class BSplineKAN(KANLayerBase):
     def _terms(self) -> int:
         return int(self.grid_size) + 3
 
+    def _train_call(self, lib, x, target, W, Wb, bias, st, hyper):
+        w, wb, b, mw, vw, mwb, vwb, mb, vb = self._train_ptrs(W, Wb, bias, st, self.has_base,
+                                                              self.has_bias)
+        lib.metal_kan_bspline_train_step(x.ctypes.data, target.ctypes.data, w, wb, b, mw, vw, mwb,
+                                         vwb, mb, vb, x.shape[0], self.in_features,
+                                         self.out_features, self.grid_size, self.grid_min,
+                                         self.grid_max, self.has_base, self.has_bias, *hyper)
+
     def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
         P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
         g = np.asarray(self.grid, np.float32)

@@ -52,6 +52,14 @@ class ChebyKAN(KANLayerBase):
     def _terms(self) -> int:
         return int(self.degree)
 
+    def _train_call(self, lib, x, target, W, Wb, bias, st, hyper):
+        w, wb, b, mw, vw, mwb, vwb, mb, vb = self._train_ptrs(W, Wb, bias, st, self.has_base,
+                                                              self.has_bias)
+        lib.metal_kan_cheby_train_step(x.ctypes.data, target.ctypes.data, w, wb, b, mw, vw, mwb,
+                                       vwb, mb, vb, x.shape[0], self.in_features,
+                                       self.out_features, self.degree, self.has_base,
+                                       self.has_bias, *hyper)
+
     def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
         fn = lib.metal_kan_cheby_backward_fused if fused else lib.metal_kan_cheby_backward
         P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731

@@ -116,6 +116,14 @@ SIGNATURES = [
     ("benchmark_metal_relu", ctypes.c_double, [vp] * 6 + [i32] * 4 + [f32] + [i32] * 4),
     ("benchmark_metal_fourier", ctypes.c_double, [vp] * 5 + [i32] * 8),
     ("benchmark_metal_jacobi", ctypes.c_double, [vp] * 5 + [i32] * 4 + [f32, f32] + [i32] * 4),
+    ("metal_kan_mult_forward", i32, [vp] * 6 + [i32] * 6 + [f32] + [i32] * 2),
+    ("metal_kan_mult_forward_fp16", i32, [vp] * 6 + [i32] * 6 + [f32] + [i32] * 2),
+    ("metal_kan_lowrank_forward", i32, [vp] * 7 + [i32] * 5 + [f32] + [i32] * 2),
+    ("metal_kan_lowrank_forward_fp16", i32, [vp] * 7 + [i32] * 5 + [f32] + [i32] * 2),
+    ("metal_kan_rational_forward", i32, [vp] * 6 + [i32] * 7),
+    ("benchmark_metal_mult", ctypes.c_double, [vp] * 6 + [i32] * 6 + [f32] + [i32] * 4),
+    ("benchmark_metal_lowrank", ctypes.c_double, [vp] * 7 + [i32] * 5 + [f32] + [i32] * 4),
+    ("benchmark_metal_rational", ctypes.c_double, [vp] * 6 + [i32] * 9),
     ("kan_set_wait_limit", i32, [i64]),
     ("kan_forward_host", i32, [ctypes.POINTER(KanLayer), vp, vp, i32]),
     ("kan_gated_forward", i32, [ctypes.POINTER(KanLayer)] * 3 + [vp, vp, vp, i32, vp]),
@@ -128,6 +136,19 @@ SIGNATURES = [
     ("kan_tc_pack", i32, [ctypes.POINTER(KanLayer), vp, vp]),
     ("kan_dequantize", i32, [ctypes.POINTER(KanWeight), i32, i32, vp, i32, vp]),
     ("kan_swiglu", i32, [vp, vp, vp, i64, i32, vp]),
+    ("kan_mult_combine", i32, [vp, vp, i32, i32, i32, i32, vp]),
+    ("kan_train_step", i32, [vp] * 3 + [i32] + [vp] * 6 + [i32, vp, i32, vp]),
+    ("kan_optim_step", i32, [i32] + [vp] * 4 + [i64, vp, i32, vp]),
+    ("metal_kan_adamw_step", i32, [vp] * 4 + [f32] * 6 + [i32]),
+    ("metal_kan_adam_step", i32, [vp] * 4 + [f32] * 6 + [i32]),
+    ("metal_kan_sgd_step", i32, [vp] * 3 + [f32] * 3 + [i32, i32]),
+    ("metal_kan_lion_step", i32, [vp] * 3 + [f32] * 4 + [i32]),
+    ("metal_kan_calc_mse_loss_backward", i32, [vp] * 3 + [i32, f32]),
+    ("metal_kan_cheby_train_step", i32, [vp] * 11 + [i32] * 6 + [f32] * 6),
+    ("metal_kan_fastkan_train_step", i32, [vp] * 12 + [i32] * 4 + [f32] + [i32] * 2 + [f32] * 6),
+    ("metal_kan_bspline_train_step", i32, [vp] * 11 + [i32] * 4 + [f32] * 2 + [i32] * 2 + [f32] * 6),
+    ("kan_lowrank_up", i32, [vp] * 6 + [i32] * 7 + [vp]),
+    ("kan_rational_forward", i32, [vp] * 6 + [i32] * 7 + [vp]),
     ("kan_convert", i32, [vp, i32, vp, i32, i64, vp]),
     ("kan_device_count", i32, [ctypes.POINTER(i32)]),
     ("kan_set_device", i32, [i32]),

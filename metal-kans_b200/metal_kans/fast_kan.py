@@ -55,6 +55,16 @@ class FastKAN(KANLayerBase):
                      else np.zeros((1,), dtype=np.float32))
         self._bridge = D.get_metal_bridge()
 
+    def _train_call(self, lib, x, target, W, Wb, bias, st, hyper):
+        w, wb, b, mw, vw, mwb, vwb, mb, vb = self._train_ptrs(W, Wb, bias, st, self.has_base,
+                                                              self.has_bias)
+        g = np.ascontiguousarray(self.grid, np.float32)
+        lib.metal_kan_fastkan_train_step(x.ctypes.data, target.ctypes.data, w, wb, g.ctypes.data,
+                                         b, mw, vw, mwb, vwb, mb, vb, x.shape[0],
+                                         self.in_features, self.out_features, self.num_centers,
+                                         self.inv_denominator, self.has_base, self.has_bias,
+                                         *hyper)
+
     def _backward_call(self, lib, dY, x, dW, dWb, dbias, dX, fused):
         P = lambda a: a.ctypes.data if a is not None else None  # noqa: E731
         grid = np.ascontiguousarray(self.grid, np.float32)

@@ -6,8 +6,8 @@ Activations stay on the device between layers (ping-pong buffers); only the inpu
 output cross PCIe.  ``pipeline=True`` on an fp32 Cheby net runs the reference's single-call chain
 entry point ``metal_kan_chain_pipeline_cheby``, which here honours each layer's degree (the
 reference hard-codes 4 terms, ``metal_kan_bridge.mm:1210``).
-Bases served by this engine: cheby, fastkan/rbf, bspline/spline/kan, wav/wavkan/wavelet, relu,
-fourier, jacobi.
+Bases served by this engine: every basis_type of the reference -- cheby, fastkan/rbf,
+bspline/spline/kan, wav/wavkan/wavelet, relu, fourier, jacobi, rational, mult, lowrank.
 """
 from __future__ import annotations
 
@@ -21,6 +21,9 @@ from .bspline_kan import BSplineKAN
 from .cheby_kan import ChebyKAN
 from .fourier_kan import FourierKAN
 from .jacobi_kan import JacobiKAN
+from .low_rank_kan import LowRankKAN
+from .mult_kan import MultKAN
+from .rational_kan import RationalKAN
 from .relu_kan import ReLUKAN
 from .fast_kan import FastKAN
 from .wav_kan import WavKAN
@@ -59,6 +62,14 @@ class MetalKAN:
                                    use_base=use_base)
             elif b in ("jacobi", "jacobikan"):
                 layer = JacobiKAN(in_f, out_f, degree=degree, bias=bias, use_base=use_base)
+            elif b in ("rational", "rationalkan"):
+                layer = RationalKAN(in_f, out_f, p_degree=degree, q_degree=max(2, degree // 2),
+                                    bias=bias, use_base=use_base)
+            elif b in ("mult", "multkan"):
+                layer = MultKAN(in_f, out_f, num_grids=degree, bias=bias, use_base=use_base)
+            elif b in ("lowrank", "lowrankkan"):
+                layer = LowRankKAN(in_f, out_f, rank=degree, num_grids=degree, bias=bias,
+                                   use_base=use_base)
             else:
                 raise ValueError(f"Unknown or unsupported basis_type for this engine: {basis_type}")
             self.layers.append(layer)
@@ -158,6 +169,27 @@ class MetalKAN:
         for layer in reversed(self.layers):
             grad = layer.backward(grad)
         return grad
+
+    def train_step(self, x: np.ndarray, target: np.ndarray, optimizer=None, lr: float = 1e-3,
+                   beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8,
+                   weight_decay: float = 0.01, opt_state=None) -> float:
+        """One training step (metal_kan.py:227-283): a one-layer net takes the layer's fused
+        step; deeper nets run forward, the MSE gradient 2/B (y - target) on the GPU, backward,
+        and ``optimizer.step()`` + ``zero_grad()`` when an optimiser is given."""
+        if len(self.layers) == 1 and hasattr(self.layers[0], "train_step"):
+            return self.layers[0].train_step(x, target, lr=lr, beta1=beta1, beta2=beta2, eps=eps,
+                                             weight_decay=weight_decay, opt_state=opt_state)
+        pred = np.ascontiguousarray(self.forward(x), np.float32)
+        t = np.ascontiguousarray(np.asarray(target, np.float32).reshape(pred.shape))
+        B = pred.shape[0] if pred.ndim == 2 else int(np.prod(pred.shape[:-1]))
+        diff = np.empty_like(pred)
+        E.lib().metal_kan_calc_mse_loss_backward(pred.ctypes.data, t.ctypes.data,
+                                                 diff.ctypes.data, pred.size, 2.0 / float(B))
+        self.backward(diff)
+        if optimizer is not None:
+            optimizer.step()
+            self.zero_grad()
+        return 0.0
 
     def zero_grad(self) -> None:
         """Zeros gradients across all layers."""

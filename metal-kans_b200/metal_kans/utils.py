@@ -43,3 +43,36 @@ def get_model_size(model: Any) -> Dict[str, Any]:
     mb = total_bytes / (1024 * 1024)
     return {"bytes": total_bytes, "mb": mb, "parameters": total_params,
             "summary": f"{mb:.3f} MB ({total_bytes:,} bytes, {total_params:,} elements)"}
+
+
+def build_train_step(model: Any, optimizer: Any, loss_fn: Any = None):
+    """A training-step function for ``model`` (utils.py:70-124): the model's own fused
+    ``train_step`` when it has one, else forward, the MSE gradient on the GPU, backward,
+    ``optimizer.step()`` and ``zero_grad()``.  ``loss_fn`` is accepted and unused, like the
+    reference (MSE is built in)."""
+    lr = getattr(optimizer, "lr", 1e-3)
+    b1 = getattr(optimizer, "beta1", 0.9)
+    b2 = getattr(optimizer, "beta2", 0.999)
+    eps = getattr(optimizer, "eps", 1e-8)
+    wd = getattr(optimizer, "weight_decay", 0.01)
+
+    if hasattr(model, "train_step"):
+        def fused_step(x: np.ndarray, y: np.ndarray) -> float:
+            return model.train_step(x, y, optimizer=optimizer, lr=lr, beta1=b1, beta2=b2, eps=eps,
+                                    weight_decay=wd)
+        return fused_step
+
+    def standard_step(x: np.ndarray, y: np.ndarray) -> float:
+        from . import _engine as E
+
+        pred = np.ascontiguousarray(model(x), np.float32)
+        t = np.ascontiguousarray(np.asarray(y, np.float32).reshape(pred.shape))
+        diff = np.empty_like(pred)
+        E.lib().metal_kan_calc_mse_loss_backward(pred.ctypes.data, t.ctypes.data, diff.ctypes.data,
+                                                 pred.size, 2.0 / float(len(x)))
+        model.backward(diff)
+        optimizer.step()
+        model.zero_grad()
+        return 0.0
+
+    return standard_step

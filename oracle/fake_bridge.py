@@ -134,6 +134,51 @@ class FakeBridge:
     def metal_kan_jacobi_forward_fp16(self, *a):
         return self._jacobi("f16", *a)
 
+    def _mult(self, mode, X, W, Wb, grid, bias, Y, B, D_in, D_out, na, nm, K, inv_den, hb, hbi):
+        dt = np.float16 if mode == "f16" else np.float32
+        internal = na + 2 * nm
+        x = _arr(X, (B, D_in), dt)
+        w = _arr(W, (internal, D_in * K), dt)
+        wb = _arr(Wb, (internal, D_in), dt) if hb else None
+        b = _arr(bias, (internal,), dt) if hbi else None
+        g = _arr(grid, (K,), dt).copy()
+        _arr(Y, (B, D_out), dt)[...] = O.mult_layer(x, mode, w, wb, b, grid=g, inv_den=inv_den,
+                                                    num_add=na, num_mult=nm)
+        return 0
+
+    def metal_kan_mult_forward(self, *a):
+        return self._mult("f32", *a)
+
+    def metal_kan_mult_forward_fp16(self, *a):
+        return self._mult("f16", *a)
+
+    def _lowrank(self, mode, X, Wd, Wu, Wb, grid, bias, Y, B, D_in, D_out, rank, K, inv_den, hb,
+                 hbi):
+        dt = np.float16 if mode == "f16" else np.float32
+        x = _arr(X, (B, D_in), dt)
+        wd = _arr(Wd, (rank, D_in * K), dt)
+        wu = _arr(Wu, (D_out, rank), dt)
+        wb = _arr(Wb, (D_out, D_in), dt) if hb else None
+        b = _arr(bias, (D_out,), dt) if hbi else None
+        g = _arr(grid, (K,), dt).copy()
+        _arr(Y, (B, D_out), dt)[...] = O.lowrank_layer(x, mode, wd, wu, wb, b, grid=g,
+                                                       inv_den=inv_den)
+        return 0
+
+    def metal_kan_lowrank_forward(self, *a):
+        return self._lowrank("f32", *a)
+
+    def metal_kan_lowrank_forward_fp16(self, *a):
+        return self._lowrank("f16", *a)
+
+    def metal_kan_rational_forward(self, X, Wp, Wq, Wb, bias, Y, B, D_in, D_out, p, q, hb, hbi):
+        f = np.float32
+        _arr(Y, (B, D_out), f)[...] = O.rational_layer(
+            _arr(X, (B, D_in), f), _arr(Wp, (D_out, D_in * p), f), _arr(Wq, (D_out, D_in * q), f),
+            _arr(Wb, (D_out, D_in), f) if hb else None, _arr(bias, (D_out,), f) if hbi else None,
+            p_degree=p, q_degree=q)
+        return 0
+
     def metal_kan_chain_pipeline_cheby(self, X, Y, B, L, dims, degs, Ws, Wbs, biases):
         """``metal_kan_bridge.mm:1168-1248`` -- note the reference hard-codes degree 4 there
         (``:1210``); the stand-in honours ``degs[]`` like the B200 engine does."""

@@ -445,6 +445,59 @@ def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------------------------
+# Composite layers: MultKAN, LowRankKAN, RationalKAN
+# --------------------------------------------------------------------------------------------
+
+def mult_layer(x, mode: str, W_rbf, W_base, bias, *, grid, inv_den, num_add: int,
+               num_mult: int):
+    """MultKAN (``metal_kan_bridge.mm:1700-1802``): the RBF layer to num_add + 2 num_mult
+    internal outputs (rounded to the layer dtype, the MPS output), then the pair products
+    ``u v`` of ``combine_mult_nodes`` (``fused_kan.metal:368-389`` / ``:1615-1640``), rounded."""
+    internal = kan_layer(x, "rbf", mode, W_rbf, W_base, bias, K=np.asarray(grid).shape[0],
+                         grid=grid, inv_den=inv_den)
+    if num_mult == 0:
+        return internal
+    u = internal[:, num_add:num_add + num_mult].astype(np.float64)
+    v = internal[:, num_add + num_mult:num_add + 2 * num_mult].astype(np.float64)
+    prod = u * v
+    prod = (prod.astype(np.float32).astype(act_dtype(mode)) if mode != "f32"
+            else prod.astype(np.float32))
+    return np.concatenate([internal[:, :num_add], prod], axis=1)
+
+
+def lowrank_layer(x, mode: str, W_down, W_up, W_base, bias, *, grid, inv_den, out_round=True):
+    """LowRankKAN (``metal_kan_bridge.mm:1535-1698``): Z = RBF layer to `rank` outputs, no base
+    or bias, rounded to the layer dtype (the MPS output); then
+    ``bias + Z W_up^T + silu(x) W_base^T`` in float64, rounded once."""
+    z = kan_layer(x, "rbf", mode, W_down, None, None, K=np.asarray(grid).shape[0], grid=grid,
+                  inv_den=inv_den)
+    xa = to_mode(x, mode) if mode != "f32" else np.asarray(x, np.float32)
+    xb = silu(xa, mode) if W_base is not None else None
+    return project(np.asarray(z, np.float64), W_up, xb, W_base, bias, mode, out_round=out_round)
+
+
+def rational_layer(x, W_p, W_q, W_base, bias, *, p_degree: int, q_degree: int):
+    """RationalKAN (``kan_rational_tiled``, ``fused_kan.metal:996-1125``), fp32 layer in float64:
+    ``y = bias + sum_i silu(xc) W_base[:, i] + P_i / (1 + |Q_i|)``, xc = clamp(x, -1, 1),
+    ``P_i = sum_{d<p} T_d(xc) W_p[:, i p + d]``, ``Q_i = sum_{d<q} T_d(xc) W_q[:, i q + d]``."""
+    x64 = np.clip(np.asarray(x, np.float32).astype(np.float64), -1.0, 1.0)
+    B, D = x64.shape
+    md = max(p_degree, q_degree)
+    T = cheby_basis(x64, md, "f32").reshape(B, D, md) if md else np.zeros((B, D, 0))
+    D_out = np.asarray(W_p if p_degree else W_q).shape[0]
+    Wp = np.asarray(W_p, np.float32).astype(np.float64).reshape(D_out, D, p_degree)
+    Wq = np.asarray(W_q, np.float32).astype(np.float64).reshape(D_out, D, q_degree)
+    P = np.einsum("bik,jik->bji", T[..., :p_degree], Wp)
+    Q = np.einsum("bik,jik->bji", T[..., :q_degree], Wq)
+    y = (P / (1.0 + np.abs(Q))).sum(-1)
+    if W_base is not None:
+        y = y + (x64 / (1.0 + np.exp(-x64))) @ np.asarray(W_base, np.float32).astype(np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float32).astype(np.float64)[None, :]
+    return y.astype(np.float32)
+
+
+# --------------------------------------------------------------------------------------------
 # Quantisers (reference bridge C++ semantics by default; "numpy" mirrors quantization.py)
 # --------------------------------------------------------------------------------------------
 
@@ -753,6 +806,47 @@ def swiglu_backward(d_hidden, gate, up):
     dh = np.asarray(d_hidden, np.float64)
     s = 1.0 / (1.0 + np.exp(-np.clip(g, -20.0, 20.0)))
     return dh * u * (s * (1.0 + g * (1.0 - s))), dh * g * s
+
+
+# --------------------------------------------------------------------------------------------
+# Training: optimiser updates and the fused step (fp32 path of the reference), float64
+# --------------------------------------------------------------------------------------------
+
+def optim_update(op: str, p, g, m, v=None, *, lr, beta1=0.9, beta2=0.999, eps=1e-8,
+                 weight_decay=0.0, lr_t=None, nesterov=False):
+    """One update of the reference's optimiser kernels, returning (p, m, v) in float64:
+    ``adamw`` (adamw_step, fused_kan.metal:1896-1921: decoupled decay), ``adam``
+    (adam_coupled_step: decay added to the gradient), ``sgd`` (sgd_step :1923-1944: m is the
+    velocity, beta1 the momentum), ``lion`` (lion_step :1946-1968)."""
+    p = np.asarray(p, np.float64).copy()
+    g = np.asarray(g, np.float64).copy()
+    m = np.asarray(m, np.float64)
+    if op in ("adamw", "adam"):
+        if op == "adamw" and weight_decay > 0:
+            p = p - lr * weight_decay * p
+        if op == "adam" and weight_decay > 0:
+            g = g + weight_decay * p
+        mv = beta1 * m + (1.0 - beta1) * g
+        vv = beta2 * np.asarray(v, np.float64) + (1.0 - beta2) * (g * g)
+        return p - lr_t * (mv / (np.sqrt(vv) + eps)), mv, vv
+    if op == "sgd":
+        if weight_decay > 0:
+            g = g + weight_decay * p
+        vel = beta1 * m + g
+        upd = g + beta1 * vel if nesterov else vel
+        return p - lr * upd, vel, None
+    if op == "lion":
+        if weight_decay > 0:
+            p = p - lr * weight_decay * p
+        u = beta1 * m + (1.0 - beta1) * g
+        return p - lr * np.sign(u), beta2 * m + (1.0 - beta2) * g, None
+    raise ValueError(op)
+
+
+def mse_grad(pred, target):
+    """dY = (pred - target) * 2 / B (mse_loss_backward, fused_kan.metal:1884-1894)."""
+    pred = np.asarray(pred, np.float64)
+    return (pred - np.asarray(target, np.float64)) * (2.0 / pred.shape[0])
 
 
 # --------------------------------------------------------------------------------------------

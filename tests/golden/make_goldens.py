@@ -10,7 +10,7 @@ What is real reference code here and what is restated:
   run unchanged (the stand-in bridge returns -1 so the reference falls back to them).  These
   fixtures pin the oracle's quantisers bit-exactly.
 * layers: the reference's classes (``ChebyKAN``, ``FastKAN``, ``BSplineKAN``, ``WavKAN``,
-  ``ReLUKAN``, ``FourierKAN``, ``JacobiKAN``,
+  ``ReLUKAN``, ``FourierKAN``, ``JacobiKAN``, ``MultKAN``, ``LowRankKAN``, ``RationalKAN``,
   ``GatedKAN``, ``MetalKAN``) run unchanged -- construction, weight init order, ``.half()``,
   casts, reshapes, ``to_int*`` -- with the Metal/MPS arithmetic supplied by
   ``oracle/fake_bridge.py`` (the Metal kernels cannot run off macOS).
@@ -55,9 +55,15 @@ def layer_goldens(mk):
         ("fourier_f3_nobase", lambda: mk.FourierKAN(8, 16, num_frequencies=3, use_base=False), (-2.0, 2.0), 64),
         ("jacobi_d4", lambda: mk.JacobiKAN(8, 16, degree=4), (-1.2, 1.2), 64),
         ("jacobi_d6_ab", lambda: mk.JacobiKAN(8, 16, degree=6, alpha=0.5, beta=1.5), (-1.0, 1.0), 64),
+        ("mult_g8", lambda: mk.MultKAN(8, 16, num_grids=8), (-1.0, 1.0), 64),
+        ("mult_m3_nobias", lambda: mk.MultKAN(8, 16, num_mult=3, num_grids=5, bias=False), (-1.5, 1.5), 64),
+        ("lowrank_r4", lambda: mk.LowRankKAN(8, 16, rank=4, num_grids=8), (-1.0, 1.0), 64),
+        ("lowrank_r6_nobase", lambda: mk.LowRankKAN(8, 16, rank=6, num_grids=6, use_base=False), (-1.5, 1.5), 64),
+        ("rational_p4q2", lambda: mk.RationalKAN(8, 16, p_degree=4, q_degree=2), (-1.3, 1.3), 64),
+        ("rational_p6q3_nobias", lambda: mk.RationalKAN(8, 16, p_degree=6, q_degree=3, bias=False), (-1.0, 1.0), 64),
     ]
     for name, ctor, (lo, hi), B in cases:
-        for mode in ("f32", "f16"):
+        for mode in (("f32",) if name.startswith("rational") else ("f32", "f16")):
             np.random.seed(42)
             layer = ctor()
             x = np.random.uniform(lo, hi, (B, 8)).astype(np.float32)
@@ -69,12 +75,14 @@ def layer_goldens(mk):
             y = layer(xin)
             rec = {"x": xin, "y": y}
             for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_relu", "w_fourier", "w_jacobi",
-                         "w_base", "bias", "grid", "translation", "_inv_scale"):
+                         "w_down", "w_up", "w_p", "w_q", "w_base", "bias", "grid", "translation",
+                         "_inv_scale"):
                 if hasattr(layer, attr):
                     rec[attr.lstrip("_")] = np.asarray(getattr(layer, attr))
             meta = dict(has_base=layer.has_base, has_bias=layer.has_bias)
             for attr in ("degree", "num_centers", "inv_denominator", "grid_size", "num_wavelets",
-                         "wavelet_type", "num_grids", "inv_h", "num_frequencies", "alpha", "beta"):
+                         "wavelet_type", "num_grids", "inv_h", "num_frequencies", "alpha", "beta",
+                         "num_add", "num_mult", "rank", "p_degree", "q_degree"):
                 if hasattr(layer, attr):
                     meta[attr] = getattr(layer, attr)
             for k, v in meta.items():
@@ -181,7 +189,8 @@ def block_goldens(mk):
         rec[f"net_{basis}/y"] = net(x)
         for li, l in enumerate(net.layers):
             for attr in ("w_cheby", "w_rbf", "w_spline", "w_wav", "w_relu", "w_fourier", "w_jacobi",
-                         "w_base", "bias", "grid", "translation", "_inv_scale"):
+                         "w_down", "w_up", "w_p", "w_q", "w_base", "bias", "grid", "translation",
+                         "_inv_scale"):
                 if hasattr(l, attr):
                     rec[f"net_{basis}/{li}.{attr.lstrip('_')}"] = np.asarray(getattr(l, attr))
     # pipelined Cheby chain (reference hard-codes degree 4 there, so use degree 4)

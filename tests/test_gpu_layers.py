@@ -21,6 +21,25 @@ def mk():
 
 def _layer_from_golden(mk, rec):
     hb, hbi = int(rec["meta_has_base"]), int(rec["meta_has_bias"])
+    if "meta_num_mult" in rec:
+        l = mk.MultKAN(8, 16, num_mult=int(rec["meta_num_mult"]), num_grids=int(rec["meta_num_grids"]),
+                       bias=bool(hbi), use_base=bool(hb))
+        l.w_rbf, l.grid = rec["w_rbf"], rec["grid"]
+        l.inv_denominator = float(rec["meta_inv_denominator"])
+        l.w_base, l.bias = rec["w_base"], rec["bias"]
+        return l, "mult"
+    if "w_up" in rec:
+        l = mk.LowRankKAN(8, 16, rank=int(rec["meta_rank"]), num_grids=int(rec["meta_num_grids"]),
+                          bias=bool(hbi), use_base=bool(hb))
+        l.w_down, l.grid, l.w_up = rec["w_down"], rec["grid"], rec["w_up"]
+        l.inv_denominator = float(rec["meta_inv_denominator"])
+        l.w_base, l.bias = rec["w_base"], rec["bias"]
+        return l, "lowrank"
+    if "w_p" in rec:
+        l = mk.RationalKAN(8, 16, p_degree=int(rec["meta_p_degree"]),
+                           q_degree=int(rec["meta_q_degree"]), bias=bool(hbi), use_base=bool(hb))
+        l.w_p, l.w_q, l.w_base, l.bias = rec["w_p"], rec["w_q"], rec["w_base"], rec["bias"]
+        return l, "rational"
     if "w_cheby" in rec:
         l = mk.ChebyKAN(8, 16, degree=int(rec["meta_degree"]), bias=bool(hbi), use_base=bool(hb))
         l.w_cheby = rec["w_cheby"]
@@ -80,8 +99,13 @@ def test_reference_layer_goldens(mk, case, path):
     mode = case.rsplit("_", 1)[1]
     if path == "tc" and mode == "f32":
         pytest.skip("the tensor-core path serves f16/bf16 layers")
-    layer, _ = _layer_from_golden(mk, rec)
-    y = layer.forward(rec["x"], path=PATHS[path])
+    layer, kind = _layer_from_golden(mk, rec)
+    if kind in ("mult", "lowrank", "rational"):
+        if path != "auto":
+            pytest.skip("composite layers choose their kernels themselves")
+        y = layer.forward(rec["x"])
+    else:
+        y = layer.forward(rec["x"], path=PATHS[path])
     assert y.dtype == rec["y"].dtype and y.shape == rec["y"].shape
     err = O.max_rel_err(y, rec["y"])
     assert err <= TOL[mode], f"{case}/{path}: max-rel-err {err:.3e}"

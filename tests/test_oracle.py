@@ -23,6 +23,19 @@ def oracle_layer_from_golden(rec, mode):
     hb = int(rec["meta_has_base"])
     hbi = int(rec["meta_has_bias"])
     kw = {}
+    wb = rec["w_base"] if hb else None
+    b = rec["bias"] if hbi else None
+    if "meta_num_mult" in rec:
+        return O.mult_layer(rec["x"], mode, rec["w_rbf"], wb, b, grid=rec["grid"],
+                            inv_den=float(rec["meta_inv_denominator"]),
+                            num_add=int(rec["meta_num_add"]), num_mult=int(rec["meta_num_mult"]))
+    if "w_up" in rec:
+        return O.lowrank_layer(rec["x"], mode, rec["w_down"], rec["w_up"], wb, b, grid=rec["grid"],
+                               inv_den=float(rec["meta_inv_denominator"]))
+    if "w_p" in rec:
+        return O.rational_layer(rec["x"], rec["w_p"], rec["w_q"], wb, b,
+                                p_degree=int(rec["meta_p_degree"]),
+                                q_degree=int(rec["meta_q_degree"]))
     if "w_cheby" in rec:
         basis, W, K = "cheby", rec["w_cheby"], int(rec["meta_degree"])
     elif "w_rbf" in rec:
@@ -67,7 +80,8 @@ def test_fp16_vs_fp32_reference_tolerance():
         # Fourier and Jacobi are outside that test too (it covers Chebyshev, RBF and ReLU): half
         # angles (half(pi) x, rounded) and Jacobi values above 1 (alpha, beta > 0) put their
         # fp16 outputs up to ~1.6e-2 from fp32 on these cases.
-        if not case.endswith("_f32") or "morlet" in case or case.startswith(("fourier", "jacobi")):
+        if (not case.endswith("_f32") or "morlet" in case
+                or case.startswith(("fourier", "jacobi", "rational"))):
             continue
         r32 = group(LAYERS, case)
         r16 = group(LAYERS, case[:-4] + "_f16")
