@@ -62,14 +62,6 @@ def test_optimizer_kernels_vs_oracle(mk, op):
     np.testing.assert_allclose(p, rp, rtol=0, atol=2 * np.spacing(np.abs(p0)).max())
 
 
-def _state(layer):
-    z = lambda a, on: np.zeros_like(a, np.float32) if on else np.zeros((1,), np.float32)  # noqa: E731
-    main = getattr(layer, layer.MAIN)
-    return {"m_w": np.zeros_like(main), "v_w": np.zeros_like(main),
-            "m_wb": z(layer.w_base, layer.has_base), "v_wb": z(layer.w_base, layer.has_base),
-            "m_b": z(layer.bias, layer.has_bias), "v_b": z(layer.bias, layer.has_bias), "step": 0}
-
-
 @pytest.mark.parametrize("basis,K", [("cheby", 5), ("rbf", 8), ("bspline", 8)])
 def test_fused_train_step_matches_composed_step(mk, basis, K):
     """train_step == forward + MSE gradient + backward + AdamW from the layer API, bit for bit,
