@@ -215,11 +215,20 @@ class KANLayerBase(E.DeviceLayerMixin):
         dY = np.ascontiguousarray(np.asarray(dY, np.float32).reshape(B, self.out_features))
         d = self.__dict__
         main = getattr(self, self.MAIN)
-        d["grad_" + self.MAIN] = np.zeros(main.shape, np.float32)
-        d["grad_w_base"] = (np.zeros(self.w_base.shape, np.float32) if self.has_base
-                            else np.zeros((1,), np.float32))
-        d["grad_bias"] = (np.zeros(self.bias.shape, np.float32) if self.has_bias
-                          else np.zeros((1,), np.float32))
+
+        def grad_array(name, shape):
+            # reused (zeroed) when it exists, as the reference does (cheby_kan.py:165-178): an
+            # optimiser holding the (param, grad) pairs of parameters() sees every new gradient
+            g = d.get(name)
+            if g is None or g.shape != shape or g.dtype != np.float32:
+                g = d[name] = np.zeros(shape, np.float32)
+            else:
+                g.fill(0)
+            return g
+
+        grad_array("grad_" + self.MAIN, main.shape)
+        grad_array("grad_w_base", self.w_base.shape if self.has_base else (1,))
+        grad_array("grad_bias", self.bias.shape if self.has_bias else (1,))
         dX = np.empty((B, self.in_features), np.float32)
         self._backward_call(E.lib(), dY, x, d["grad_" + self.MAIN],
                             d["grad_w_base"] if self.has_base else None,

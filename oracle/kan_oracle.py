@@ -821,6 +821,11 @@ def optim_update(op: str, p, g, m, v=None, *, lr, beta1=0.9, beta2=0.999, eps=1e
     p = np.asarray(p, np.float64).copy()
     g = np.asarray(g, np.float64).copy()
     m = np.asarray(m, np.float64)
+    # the kernels take fp32 hyper-parameters: 1 - beta is then exact in fp32 (Sterbenz) and
+    # differs from 1 - beta of the float64 literal by up to ~1e-5 relative (beta2 = 0.999)
+    f = lambda a: None if a is None else float(np.float32(a))  # noqa: E731
+    lr, beta1, beta2, eps, weight_decay, lr_t = (f(lr), f(beta1), f(beta2), f(eps),
+                                                 f(weight_decay), f(lr_t))
     if op in ("adamw", "adam"):
         if op == "adamw" and weight_decay > 0:
             p = p - lr * weight_decay * p
