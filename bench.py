@@ -49,7 +49,7 @@ TOL = {"f32": 1e-5, "f16": 2e-3, "bf16": 2e-3}
 # a smaller batch of the same layer and scaled by the rows processed (the summary says why that
 # holds); the line reports the scale.
 TRAFFIC = {
-    "c1": {"bytes": 453632, "src": "profiles/kan_simt_kernel_c1_cheby_fp32_b1024.md"},
+    "c1": {"bytes": 451328, "src": "profiles/kan_simt_dense_kernel_c1_cheby_fp32_b1024.md"},
     "c2": {"bytes": 3386368, "src": "profiles/kan_tc_kernel_c2_fastkan_fp16_b4096.md"},
     "c3": {"bytes": 20276992, "src": "profiles/kan_tc_kernel_c3_bspline_fp16_b8192.md",
            "note": "first (largest) of the net's three launches"},
@@ -57,6 +57,9 @@ TRAFFIC = {
                         "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b4096.md"},
     "c5:ternary:16": {"bytes": 53773568 + 152064,
                       "src": "profiles/kan_gemv_kernel_c5_ternary_bf16_b16.md"},
+    "c5:ternary:1": {"bytes": 52557312 + 40448,
+                     "src": "profiles/kan_gemv_cc_kernel_c5_ternary_bf16_b1.md",
+                     "note": "the main kernel; the pre-pass reads 40 KB"},
     "c5:ternary:65536": {"bytes": 5865144576 + 527921408,
                          "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b65536.md"},
 }

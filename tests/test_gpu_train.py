@@ -144,7 +144,7 @@ def test_metalkan_training_reduces_loss(mk, opt_name):
     target = np.stack([np.sin(2 * x[:, 0]), x[:, 1] * x[:, 2], np.cos(x[:, 3])], 1).astype(np.float32)
     net(x)
     net.backward(np.zeros((256, 3), np.float32))
-    kw = {"AdamW": dict(lr=1e-2), "Adam": dict(lr=1e-2), "SGD": dict(lr=0.1, momentum=0.9),
+    kw = {"AdamW": dict(lr=1e-2), "Adam": dict(lr=1e-2), "SGD": dict(lr=0.02, momentum=0.9),
           "Lion": dict(lr=3e-3)}[opt_name]
     opt = getattr(mk.optim, opt_name)(net.parameters(), **kw)
     step = mk.build_train_step(net, opt)
