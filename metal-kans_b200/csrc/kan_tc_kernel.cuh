@@ -97,14 +97,17 @@ static_assert(BM * 256 * 2 <= STAGES * A_STAGE_BYTES, "x tile must fit in the A 
 
 // Shared-memory layout of one kernel variant.  WIDE (BN = 512): two N = 256 accumulators (all 512
 // TMEM columns) take every basis block, so each block the producers build feeds twice the MMA
-// work; its 64 KB weight stages leave room for 3 A and 2 input stages, no split-K slots and no
-// staged LayerNorm tile.
+// work.  Its weights stream through a ring of four 32 KB slots, one 256-row half of a block's
+// 64 KB panel each, released half by half as the MMAs of that half complete: the load of a half
+// is issued 1.5 blocks of MMA time before it is needed (a ring of two whole-block stages gave one
+// block, and the weight loads then stalled the tensor pipe for ~20 % of the step).  This leaves
+// room for 3 A and 2 input stages, no split-K slots and no staged LayerNorm tile.
 template <bool WIDE>
 struct Layout {
   static constexpr int kStages = WIDE ? 3 : STAGES;
-  static constexpr int kBStages = WIDE ? 2 : BSTAGES;
+  static constexpr int kBStages = WIDE ? 4 : BSTAGES;  // WIDE: half-block slots
   static constexpr int kXStages = WIDE ? 2 : XSTAGES;
-  static constexpr int kBStageBytes = WIDE ? 2 * B_STAGE_BYTES : B_STAGE_BYTES;
+  static constexpr int kBStageBytes = B_STAGE_BYTES;
   static constexpr uint32_t kTmemCols = WIDE ? 512u : TMEM_COLS;
   static constexpr int kOffB = OFF_A + kStages * A_STAGE_BYTES;
   static constexpr int kOffX = kOffB + kBStages * kBStageBytes;
@@ -923,11 +926,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == TMA_WARP) {
     // ------------------------------------------------------------------ weight TMA
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)BN * BK * 2;
+      // a wide tile's block is two slots (weight rows 0..255, 256..511: one box each)
+      constexpr int H = WIDE ? 2 : 1;
+      const uint32_t bytes = (uint32_t)(WIDE ? 256 : BN) * BK * 2;
       int issued = 0;
-      for (int j = 0; j < nj; ++j) {
-        const int s = j % BSTAGES;
-        const uint32_t it = (uint32_t)(j / BSTAGES);
+      for (int t = 0; t < nj * H; ++t) {
+        const int j = t / H, h = t % H;
+        const int s = t % BSTAGES;
+        const uint32_t it = (uint32_t)(t / BSTAGES);
         if (!mbar_wait(bar_empty_b + 8 * s, (it & 1u) ^ 1u, plim)) {
           raise_device_error(a.err, DEVERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
@@ -936,11 +942,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (*abort_flag) break;
         mbar_arrive_expect_tx(bar_full_b + 8 * s, bytes);
         tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES, &tmap_w, bar_full_b + 8 * s,
-                    (kb0 + j) * BK, n0);
-        // the second 256 weight rows of a wide tile (a box is at most 256 rows)
-        if (WIDE)
-          tma_load_2d(s_base + OFF_B + s * B_STAGE_BYTES + 256 * BK * 2, &tmap_w,
-                      bar_full_b + 8 * s, (kb0 + j) * BK, n0 + 256);
+                    (kb0 + j) * BK, n0 + 256 * h);
         ++issued;
       }
       // drain: wait (bounded) for the copies still landing in shared memory
@@ -952,34 +954,39 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = instr_desc(MODE == MODE_BF16 ? 1 : 0, WIDE ? 256 : BN, BM);
-      for (int j = 0; j < nj; ++j) {
-        const int s = j % STAGES, sb = j % BSTAGES;
+      constexpr int H = WIDE ? 2 : 1;  // weight slots (accumulator halves) per block
+      bool stop = false;
+      for (int j = 0; j < nj && !stop; ++j) {
+        const int s = j % STAGES;
         const uint32_t par = (uint32_t)(j / STAGES) & 1u;
-        bool ok = mbar_wait(bar_full_a + 8 * s, par, plim);
-        if (!ok) raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
-        if (ok && !mbar_wait(bar_full_b + 8 * sb, (uint32_t)(j / BSTAGES) & 1u, plim)) {
-          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
-          ok = false;
-        }
-        if (!ok || *abort_flag) {
+        if (!mbar_wait(bar_full_a + 8 * s, par, plim)) {
+          raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
           *abort_flag = 1;
           break;
         }
-        tc_fence_after();
         const uint32_t a_addr = s_base + OFF_A + s * A_STAGE_BYTES;
-        const uint32_t b_addr = s_base + OFF_B + sb * B_STAGE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          mma_f16(tmem_d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32),
-                  idesc, (j > 0 || kk > 0) ? 1u : 0u);
-          // wide tile: the same basis block against weight rows 256..511, columns 256..511
-          if (WIDE)
-            mma_f16(tmem_d + 256u, smem_desc_sw128(a_addr + kk * 32),
-                    smem_desc_sw128(b_addr + 256 * BK * 2 + kk * 32), idesc,
-                    (j > 0 || kk > 0) ? 1u : 0u);
+        for (int h = 0; h < H; ++h) {
+          const int t = j * H + h, sb = t % BSTAGES;
+          if (!mbar_wait(bar_full_b + 8 * sb, (uint32_t)(t / BSTAGES) & 1u, plim)) {
+            raise_device_error(a.err, DEVERR_TIMEOUT_FULL_B);
+            *abort_flag = 1;
+          }
+          if (*abort_flag) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t b_addr = s_base + OFF_B + sb * B_STAGE_BYTES;
+          // wide tile: half h takes weight rows / accumulator columns 256 h .. 256 h + 255
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16(tmem_d + 256u * (uint32_t)h, smem_desc_sw128(a_addr + kk * 32),
+                    smem_desc_sw128(b_addr + kk * 32), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(bar_empty_b + 8 * sb);  // this half's weight slot is free once it is read
         }
+        if (stop) break;
         mma_commit(bar_empty + 8 * s);
-        mma_commit(bar_empty_b + 8 * sb);
       }
       // signal the epilogue (also on abort, so that it does not wait out its own limit)
       mma_commit(bar_accum);
