@@ -377,8 +377,10 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
  * KAN_PATH_AUTO), and for the tensor-core path info[1] = tile width BN, info[2] = split-K factor
  * (cluster size), info[3] = M tiles, info[4] = N tiles, info[5] = 64-column K blocks; for the
  * tensor-core small-batch path info[3] = 128-row blocks; for the CUDA-core small-batch path
- * info[2] = K splits, info[3] = 32-row blocks.  Tests and benchmarks use it to name the plan they
- * check.  info must hold 6 ints. */
+ * info[1] = output rows per CTA (128: the lanes-along-K kernel for ternary weights in groups of
+ * 32..256; 32: the lane-per-row kernel), info[2] = most CTAs summed into one row block (K
+ * splits), info[3] = row blocks.  Tests and benchmarks use it to name the plan they check.
+ * info must hold 6 ints. */
 int kan_forward_plan(const kan_layer* layer, int B, int path, int* info);
 /* No counterpart in the reference.  Limit of the tensor-core kernel's pipeline waits (a stage
  * filled or freed by another warp role), in SM clock cycles, for the launches that follow on any

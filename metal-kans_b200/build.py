@@ -39,9 +39,9 @@ SOURCES = [("kan_abi.cpp", "kan_abi", []), ("kan_misc.cu", "kan_misc", []),
     ("kan_tc_inst.cu", f"kan_tc_inst_{m}_{b}", [f"-DKAN_TC_MODE={m}", f"-DKAN_TC_BASIS={b}"])
     for m in (1, 2) for b in range(7)] + [
     ("kan_gemv_cc_inst.cu", f"kan_gemv_cc_inst_{m}_{n}", [f"-DKAN_CC_MODE={m}", f"-DKAN_CC_NB={n}"])
+    for m in (1, 2) for n in range(1, 5)] + [
+    ("kan_gemv_kl_inst.cu", f"kan_gemv_kl_inst_{m}_{n}", [f"-DKAN_KL_MODE={m}", f"-DKAN_KL_NB={n}"])
     for m in (1, 2) for n in range(1, 5)]
-HEADERS = ["kan_device.cuh", "kan_launch.h", "kan_args.h", "kan_tc_kernel.cuh",
-           "kan_tc_dispatch.h", "kan_gemv_cc.cuh"]
 
 
 def nvcc() -> str:
@@ -49,6 +49,25 @@ def nvcc() -> str:
         if c and os.path.exists(c):
             return c
     raise RuntimeError("nvcc not found")
+
+
+def _includes(path, seen=None):
+    """The quoted includes of `path`, followed recursively (csrc/ and include/ files only)."""
+    import re
+
+    seen = set() if seen is None else seen
+    try:
+        text = open(path).read()
+    except OSError:
+        return seen
+    for name in re.findall(r'^\s*#\s*include\s+"([^"]+)"', text, re.M):
+        dep = os.path.normpath(os.path.join(os.path.dirname(path), name))
+        if not os.path.exists(dep):
+            dep = os.path.join(INCLUDE, os.path.basename(name))
+        if os.path.exists(dep) and dep not in seen:
+            seen.add(dep)
+            _includes(dep, seen)
+    return seen
 
 
 def _newer(src_paths, target):
@@ -62,7 +81,7 @@ def _compile(spec, verbose: bool) -> str:
     src, name, defines = spec
     path = os.path.join(CSRC, src)
     obj = os.path.join(BUILD, name + ".o")
-    deps = [path] + [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "kan_cuda.h")]
+    deps = [path] + sorted(_includes(path))
     if not _newer(deps, obj):
         return obj
     cmd = [nvcc(), *ARCH, *NVCC_COMMON, *defines, "-c", path, "-o", obj]

@@ -373,7 +373,8 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
                   "CUDA-core small-batch path needs an f16/bf16 layer with ternary/INT8/INT4 "
                   "weights (group a multiple of 16), B <= 4, and code rows of >= 128 bytes");
     void* scratch;
-    // zeroed when first allocated: the split counters start at zero (the pre-pass resets them)
+    // zeroed when first allocated: the split counters start at zero (the lane-per-row kernel's
+    // pre-pass resets them; the lanes-along-K kernel tags them with the call's epoch)
     if ((rc = scratch_buf(d, s, SC_CC, gemv_cc_scratch_bytes(a), true, &scratch))) return rc;
     e = launch_gemv_cc(a, L->act_dtype, scratch, s);
   } else if (path == KAN_PATH_SIMT) {
@@ -443,8 +444,9 @@ int kan_forward_plan(const kan_layer* layer, int B, int path, int* info) {
     if (!gemv_cc_supported(a, layer->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED,
                   "forward_plan: the layer does not fit the CUDA-core small-batch path");
+    info[1] = gemv_cc_rows(a);
     info[2] = gemv_cc_splits(a);
-    info[3] = (layer->D_out + 31) / 32;
+    info[3] = (layer->D_out + info[1] - 1) / info[1];
   } else if (path != KAN_PATH_SIMT) {
     return fail(KAN_ERR_ARG, "forward_plan: unknown path %d", path);
   }

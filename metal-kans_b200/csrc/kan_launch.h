@@ -63,11 +63,14 @@ cudaError_t launch_tc_pack_pair(const LayerArgs& gate, const LayerArgs& up, int 
 // (kan_tc.cu).
 void* tensor_map_encoder();
 // kan_gemv_cc.cu: small-batch path on the CUDA cores (B <= 4; ternary / INT8 / INT4 weights decoded
-// on chip, integer dot products against a fixed-point basis matrix).  launch_gemv_cc also runs the
-// basis pre-pass; `scratch` holds gemv_cc_scratch_bytes() of device memory, zeroed when allocated.
+// on chip, integer dot products against a fixed-point basis).  Ternary weights in groups of
+// 32..256 run the lanes-along-K kernel (kan_gemv_kl.cuh, basis evaluated in the kernel); the
+// others the lane-per-row kernel, whose basis pre-pass launch_gemv_cc also runs.  `scratch` holds
+// gemv_cc_scratch_bytes() of device memory, zeroed when allocated.
 bool gemv_cc_supported(const LayerArgs& a, int act_dtype);
 size_t gemv_cc_scratch_bytes(const LayerArgs& a);
 int gemv_cc_splits(const LayerArgs& a);
+int gemv_cc_rows(const LayerArgs& a);  // output rows per CTA of the kernel launch_gemv_cc runs
 cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s);
 // kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
 // from the packed codes into TMEM; no dense copy)
