@@ -262,7 +262,7 @@ static int kl_fixed_smem(const LayerArgs& a, int NB, int stages) {
   const size_t phi = (size_t)2 * NB * PHI_BUF;
   const size_t fac = (size_t)2 * NB * 16 * 4;
   const size_t misc = align16((size_t)MISC_BYTES);
-  return (int)(x + phi + fac + misc + (size_t)(stages + 2) * 8 + 1024);
+  return (int)(x + phi + fac + misc + (size_t)(stages + 3) * 8 + 1024);
 }
 
 // The launch plan; `scratch` (may be null) fills the scratch pointers.  Returns the scratch
@@ -286,7 +286,7 @@ static size_t kl_plan(const LayerArgs& a, Params& p, void* scratch) {
   p.off_fac = p.off_phi + 2 * NB * PHI_BUF;
   p.off_misc = p.off_fac + 2 * NB * 16 * 4;
   p.off_bar = p.off_misc + (int)align16((size_t)MISC_BYTES);
-  p.smem = p.off_bar + (p.stages + 2) * 8 + 1024;
+  p.smem = p.off_bar + (p.stages + 3) * 8 + 1024;
   p.rowblocks = (a.D_out + ROWS - 1) / ROWS;
   p.tasks = (long long)p.rowblocks * p.W;
   p.G = (int)std::min<long long>(p.tasks, cc::sm_count());
@@ -336,14 +336,19 @@ static bool kl_supported(const LayerArgs& a, int act_dtype) {
   return tensor_map_encoder() != nullptr;
 }
 
+unsigned kl::next_epoch() {
+  static std::atomic<unsigned> epoch{0};
+  unsigned e = ++epoch;
+  if (e == 0) e = ++epoch;  // 0 marks a reset counter
+  return e;
+}
+
 static cudaError_t launch_gemv_kl(const LayerArgs& a, int act_dtype, void* scratch,
                                   cudaStream_t s) {
   using namespace kl;
-  static std::atomic<unsigned> epoch{0};
   Params p;
   kl_plan(a, p, scratch);
-  p.epoch = ++epoch;
-  if (p.epoch == 0) p.epoch = ++epoch;  // 0 marks a reset counter
+  p.epoch = next_epoch();
   const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;
   const cc::RowShape rw = cc::row_shape(a.w, a.D_in * a.K);
   CUtensorMap cw, sw, cb, sb;
@@ -440,6 +445,14 @@ static void launch_phi(const LayerArgs& a, const cc::Params& p, cudaStream_t s) 
     case KAN_RELU: cc::cc_phi_kernel<MODE, KAN_RELU><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
     default: cc::cc_phi_kernel<MODE, KAN_FOURIER><<<grid, cc::PRE_THREADS, sm, s>>>(a, p); break;
   }
+}
+
+cudaError_t launch_cc_prepass(const LayerArgs& a, int act_dtype, const cc::Params& p,
+                              cudaStream_t s) {
+  if (act_dtype == KAN_F16) launch_phi<MODE_F16>(a, p, s);
+  else launch_phi<MODE_BF16>(a, p, s);
+  note_launch();
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s) {

@@ -98,6 +98,12 @@ __host__ __device__ __forceinline__ int owner(long long x, long long T, int G) {
   return (int)(((x + 1) * (long long)G - 1) / T);
 }
 
+// Epoch of a launch of a kernel with per-row-block counters (this one and the 8-bit tensor-core
+// small-batch kernel): one process-wide sequence, never 0, so that a counter left behind by any
+// earlier launch (an aborted one, or another layer sharing the scratch) never carries the
+// current epoch (kan_gemv_cc.cu).
+unsigned next_epoch();
+
 // Position of code c (0..1023) of a window in the basis buffer: unit u = c / 16 of lane u / 2,
 // slot [u & 1][lane], byte cc::unit_pos inside the unit.
 __device__ __forceinline__ int phi_pos(int c, bool fast) {
@@ -299,6 +305,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t s_base = smem_u32(smem);
   const uint32_t bar_full = s_base + p.off_bar;
   const uint32_t bar_phi = bar_full + 8 * p.stages;  // [2]: a window's basis is in place
+  const uint32_t bar_never = bar_phi + 16;            // completed by nothing (abort-path tests)
   T* xs = reinterpret_cast<T*>(smem + p.off_x);                  // [NB][D_in]
   int8_t* phi = reinterpret_cast<int8_t*>(smem + p.off_phi);     // [2][NB][hi, lo][1024]
   float* fac = reinterpret_cast<float*>(smem + p.off_fac);       // [2][NB][16]
@@ -339,6 +346,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     mbar_init(bar_phi, WARPS);
     mbar_init(bar_phi + 8, WARPS);
+    mbar_init(bar_never, 1);
     *abort_flag = 0;
     *decision = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -412,8 +420,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     const bool seg = w >= p.Ww;
     const int pb = i & 1;
     bool live = __shfl_sync(0xffffffffu, *abort_flag, 0) == 0;
-    // this window's basis (produced one window ahead by all warps)
-    if (live && !mbar_wait_warp(bar_phi + 8 * pb, (uint32_t)(i >> 1) & 1u, plim)) {
+    // this window's basis (produced one window ahead by all warps).  The kernel's waits are short
+    // (stages land while the warps build the basis, and the warps reach each basis barrier
+    // together), so a limit below 16 cycles -- the abort-path tests -- makes the first of them wait
+    // on a barrier that nothing completes: the abort path then runs whatever the timing.
+    const bool never = i == 0 && a.wait_cycles > 0 && a.wait_cycles < 16;
+    if (live && !mbar_wait_warp(never ? bar_never : bar_phi + 8 * pb, (uint32_t)(i >> 1) & 1u,
+                                plim)) {
       raise_device_error(a.err, DEVERR_TIMEOUT_FULL_A);
       *abort_flag = 1;
       live = false;

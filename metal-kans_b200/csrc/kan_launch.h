@@ -75,9 +75,19 @@ cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cud
 // kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
 // from the packed codes into TMEM; no dense copy)
 // launch_gemv also runs the basis pre-pass into `phi` (gemv_phi_bytes() of device scratch).
+// Ternary layers in groups of 64/128 codes at 5 <= B <= 16 run the 8-bit kernel instead
+// (kan_gemv_i8.cu: codes as signed bytes, the fixed-point basis of the CUDA-core path, per-group
+// int32 accumulators scaled in an epilogue); launch_gemv picks it, `phi` then holds
+// gemv_i8_scratch_bytes().
 bool gemv_supported(const LayerArgs& a, int act_dtype);
 size_t gemv_phi_bytes(const LayerArgs& a);
+int gemv_operand_bits(const LayerArgs& a);  // 8: the 8-bit kernel, 16: the 16-bit one
+int gemv_splits(const LayerArgs& a);
 cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream_t s);
+bool gemv_i8_supported(const LayerArgs& a, int act_dtype);
+size_t gemv_i8_scratch_bytes(const LayerArgs& a);
+int gemv_i8_splits(const LayerArgs& a);
+cudaError_t launch_gemv_i8(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s);
 // kan_backward.cu: fp32 layer backward (Chebyshev, RBF, B-spline bases; raw input)
 bool backward_supported(const BackwardArgs& a);
 cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s);

@@ -165,15 +165,32 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity`; false when `limit` SM cycles passed first.  The suspend
-// hint never exceeds about half the limit, so that a short limit (tests of the abort path) is
-// honoured instead of sleeping through it.
+// Non-blocking probe of the phase.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity`; false when `limit` SM cycles passed first.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
                                           long long limit = WAIT_LIMIT_CYCLES) {
+  if (limit < 40000LL) {
+    // a short limit (the abort-path tests): poll without suspending, so that the limit and not
+    // the hardware's own suspend window of try_wait decides when the wait gives up
+    const long long t0 = clock64();
+    while (!mbar_test_wait(bar, parity))
+      if (clock64() - t0 > limit) return false;
+    return true;
+  }
   if (mbar_try_wait(bar, parity)) return true;
-  const uint32_t hint = limit >= 40000LL ? 20000u : (uint32_t)(limit / 2 + 1);
   const long long t0 = clock64();
-  while (!mbar_try_wait_hint(bar, parity, hint))
+  while (!mbar_try_wait_hint(bar, parity, 20000u))
     if (clock64() - t0 > limit) return false;
   return true;
 }
