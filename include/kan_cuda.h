@@ -376,13 +376,9 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
  * run, without running it: info[0] = the path taken (KAN_PATH_SIMT / TC / GEMV; `path` may be
  * KAN_PATH_AUTO), and for the tensor-core path info[1] = tile width BN, info[2] = split-K factor
  * (cluster size), info[3] = M tiles, info[4] = N tiles, info[5] = 64-column K blocks; for the
- * tensor-core small-batch path info[1] = operand bits (8: the 8-bit kernel for ternary weights in
- * groups of 64/128 at 5 <= B <= 16; 16: the 16-bit one), info[2] = K splits (8-bit: most CTAs
- * summed into one row block), info[3] = 128-row blocks; for the CUDA-core small-batch path
- * info[1] = output rows per CTA (128: the lanes-along-K kernel for ternary weights in groups of
- * 32..256; 32: the lane-per-row kernel), info[2] = most CTAs summed into one row block (K
- * splits), info[3] = row blocks.  Tests and benchmarks use it to name the plan they check.
- * info must hold 6 ints. */
+ * tensor-core small-batch path info[3] = 128-row blocks; for the CUDA-core small-batch path
+ * info[2] = K splits, info[3] = 32-row blocks.  Tests and benchmarks use it to name the plan they
+ * check.  info must hold 6 ints. */
 int kan_forward_plan(const kan_layer* layer, int B, int path, int* info);
 /* No counterpart in the reference.  Limit of the tensor-core kernel's pipeline waits (a stage
  * filled or freed by another warp role), in SM clock cycles, for the launches that follow on any

@@ -34,14 +34,11 @@ CXX_FLAGS = ["-Xcompiler", "-ffp-contract=off"]
 SOURCES = [("kan_abi.cpp", "kan_abi", []), ("kan_misc.cu", "kan_misc", []),
            ("kan_simt.cu", "kan_simt", []), ("kan_tc.cu", "kan_tc", []),
            ("kan_noalloc.cu", "kan_noalloc", []), ("kan_gemv.cu", "kan_gemv", []),
-           ("kan_gemv_cc.cu", "kan_gemv_cc", []), ("kan_gemv_i8.cu", "kan_gemv_i8", []),
-           ("kan_backward.cu", "kan_backward", []),
+           ("kan_gemv_cc.cu", "kan_gemv_cc", []), ("kan_backward.cu", "kan_backward", []),
            ("kan_extra.cu", "kan_extra", []), ("kan_train.cu", "kan_train", [])] + [
     ("kan_tc_inst.cu", f"kan_tc_inst_{m}_{b}", [f"-DKAN_TC_MODE={m}", f"-DKAN_TC_BASIS={b}"])
     for m in (1, 2) for b in range(7)] + [
     ("kan_gemv_cc_inst.cu", f"kan_gemv_cc_inst_{m}_{n}", [f"-DKAN_CC_MODE={m}", f"-DKAN_CC_NB={n}"])
-    for m in (1, 2) for n in range(1, 5)] + [
-    ("kan_gemv_kl_inst.cu", f"kan_gemv_kl_inst_{m}_{n}", [f"-DKAN_KL_MODE={m}", f"-DKAN_KL_NB={n}"])
     for m in (1, 2) for n in range(1, 5)]
 
 

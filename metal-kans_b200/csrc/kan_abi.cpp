@@ -363,11 +363,9 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
     if (!gemv_ok)
       return fail(KAN_ERR_UNSUPPORTED,
                   "small-batch path needs an f16/bf16 Chebyshev layer with ternary/INT2 weights "
-                  "(group 32/64/128), B <= 64, D_in >= 512, D_out >= 256, or a ternary layer of "
-                  "any basis but Jacobi with groups of 64/128 at 5 <= B <= 16");
+                  "(group 32/64/128), B <= 64, D_in >= 512, D_out >= 256");
     void* phi;
-    // zeroed when first allocated (the 8-bit kernel's row-block counters start at zero)
-    if ((rc = scratch_buf(d, s, SC_PHI, gemv_phi_bytes(a), true, &phi))) return rc;
+    if ((rc = scratch_buf(d, s, SC_PHI, gemv_phi_bytes(a), false, &phi))) return rc;
     e = launch_gemv(a, L->act_dtype, phi, s);
   } else if (path == KAN_PATH_GEMV_CC) {
     if (!gemv_cc_supported(a, L->act_dtype))
@@ -375,8 +373,7 @@ static int run_forward(const kan_layer* L, const void* X, void* Y, int B, int pa
                   "CUDA-core small-batch path needs an f16/bf16 layer with ternary/INT8/INT4 "
                   "weights (group a multiple of 16), B <= 4, and code rows of >= 128 bytes");
     void* scratch;
-    // zeroed when first allocated: the split counters start at zero (the lane-per-row kernel's
-    // pre-pass resets them; the lanes-along-K kernel tags them with the call's epoch)
+    // zeroed when first allocated: the split counters start at zero (the pre-pass resets them)
     if ((rc = scratch_buf(d, s, SC_CC, gemv_cc_scratch_bytes(a), true, &scratch))) return rc;
     e = launch_gemv_cc(a, L->act_dtype, scratch, s);
   } else if (path == KAN_PATH_SIMT) {
@@ -441,16 +438,13 @@ int kan_forward_plan(const kan_layer* layer, int B, int path, int* info) {
   } else if (path == KAN_PATH_GEMV) {
     if (!gemv_supported(a, layer->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED, "forward_plan: the layer does not fit the small-batch path");
-    info[1] = gemv_operand_bits(a);
-    info[2] = gemv_splits(a);
     info[3] = (layer->D_out + 127) / 128;
   } else if (path == KAN_PATH_GEMV_CC) {
     if (!gemv_cc_supported(a, layer->act_dtype))
       return fail(KAN_ERR_UNSUPPORTED,
                   "forward_plan: the layer does not fit the CUDA-core small-batch path");
-    info[1] = gemv_cc_rows(a);
     info[2] = gemv_cc_splits(a);
-    info[3] = (layer->D_out + info[1] - 1) / info[1];
+    info[3] = (layer->D_out + 31) / 32;
   } else if (path != KAN_PATH_SIMT) {
     return fail(KAN_ERR_ARG, "forward_plan: unknown path %d", path);
   }

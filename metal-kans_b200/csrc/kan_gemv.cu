@@ -678,7 +678,6 @@ static GemvParams plan(const LayerArgs& a) {
 
 bool gemv_supported(const LayerArgs& a, int act_dtype) {
   using namespace sb;
-  if (gemv_i8_supported(a, act_dtype)) return true;
   if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
   if (a.basis != KAN_CHEBY) return false;
   if (a.B < 1 || a.B > MAXN) return false;
@@ -701,7 +700,6 @@ bool gemv_supported(const LayerArgs& a, int act_dtype) {
 }
 
 size_t gemv_phi_bytes(const LayerArgs& a) {
-  if (gemv_i8_supported(a, a.act_dtype)) return gemv_i8_scratch_bytes(a);
   const sb::GemvParams p = sb::plan(a);
   return (size_t)p.npad * p.kpad * 2;
 }
@@ -728,16 +726,8 @@ static int max_clusters(Kern kern, int ki, const cudaLaunchConfig_t& q) {
   return clusters;
 }
 
-int gemv_operand_bits(const LayerArgs& a) { return gemv_i8_supported(a, a.act_dtype) ? 8 : 16; }
-
-int gemv_splits(const LayerArgs& a) {
-  if (gemv_i8_supported(a, a.act_dtype)) return gemv_i8_splits(a);
-  return sb::plan(a).S;
-}
-
 cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream_t s) {
   using namespace sb;
-  if (gemv_i8_supported(a, act_dtype)) return launch_gemv_i8(a, act_dtype, phi, s);
   const GemvParams p = plan(a);
   const bool bf = act_dtype == KAN_BF16;
   CUtensorMap tphi;

@@ -9,7 +9,6 @@
 #include <tuple>
 
 #include "kan_gemv_cc.cuh"
-#include "kan_gemv_kl.cuh"
 
 namespace kan {
 namespace cc {
@@ -206,177 +205,8 @@ static size_t plan(const LayerArgs& a, int act_dtype, Params& p, void* scratch) 
 
 }  // namespace cc
 
-// ---------------------------------------------------------------------------------------------
-// lanes-along-K kernel (kan_gemv_kl.cuh): ternary weights, groups of 32..256 codes
-// ---------------------------------------------------------------------------------------------
-namespace kl {
-
-static KlFn kl_kernel(int mode, int B, bool fast) {
-  if (mode == MODE_F16) {
-    switch (B) {
-      case 1: return select_kl<MODE_F16, 1>(fast);
-      case 2: return select_kl<MODE_F16, 2>(fast);
-      case 3: return select_kl<MODE_F16, 3>(fast);
-      default: return select_kl<MODE_F16, 4>(fast);
-    }
-  }
-  switch (B) {
-    case 1: return select_kl<MODE_BF16, 1>(fast);
-    case 2: return select_kl<MODE_BF16, 2>(fast);
-    case 3: return select_kl<MODE_BF16, 3>(fast);
-    default: return select_kl<MODE_BF16, 4>(fast);
-  }
-}
-
-static std::atomic<unsigned long long>& kl_configured(KlFn k) {
-  static std::mutex mu;
-  static std::map<KlFn, std::atomic<unsigned long long>*> m;
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = m.find(k);
-  if (it == m.end()) it = m.emplace(k, new std::atomic<unsigned long long>(0)).first;
-  return *it->second;
-}
-
-// [rows][cols] matrix of 1- or 4-byte elements, box = box_cols x ROWS, no swizzle, zero fill.
-static bool kl_make_map(CUtensorMap* m, const void* base, int rows, long long cols, int box_cols,
-                        bool codes) {
-  cc::EncodeTiledFn enc = (cc::EncodeTiledFn)tensor_map_encoder();
-  const int esz = codes ? 1 : 4;
-  if (!enc || ((uintptr_t)base & 15) || ((cols * esz) % 16)) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(cols * esz)};
-  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)ROWS};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, codes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                   const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
-
-// Shared memory of every part but the stage ring (bytes), for NB batch rows.
-static int kl_fixed_smem(const LayerArgs& a, int NB, int stages) {
-  const size_t x = align16((size_t)NB * a.D_in * 2);
-  const size_t phi = (size_t)2 * NB * PHI_BUF;
-  const size_t fac = (size_t)2 * NB * 16 * 4;
-  const size_t misc = align16((size_t)MISC_BYTES);
-  return (int)(x + phi + fac + misc + (size_t)(stages + 3) * 8 + 1024);
-}
-
-// The launch plan; `scratch` (may be null) fills the scratch pointers.  Returns the scratch
-// bytes needed (0 when the layer does not fit).
-static size_t kl_plan(const LayerArgs& a, Params& p, void* scratch) {
-  p = Params{};
-  const int NB = std::min(MAXB, std::max(1, a.B));
-  const cc::RowShape rw = cc::row_shape(a.w, a.D_in * a.K);
-  const cc::RowShape rbs = a.has_base ? cc::row_shape(a.wb, a.D_in) : cc::RowShape{0, 0};
-  p.Ww = (int)((rw.bytes + WIN_BYTES - 1) / WIN_BYTES);
-  p.W = p.Ww + (int)((rbs.bytes + WIN_BYTES - 1) / WIN_BYTES);
-  p.lgs = 0;
-  while ((1 << p.lgs) < a.w.group_size) ++p.lgs;
-  p.sfl = WIN_CODES >> p.lgs;
-  p.stage_bytes = (CODE_TILE + ROWS * p.sfl * 4 + 1023) / 1024 * 1024;
-  p.stages = MAX_STAGES;
-  while (p.stages > 2 && p.stages * p.stage_bytes + kl_fixed_smem(a, NB, p.stages) > cc::SMEM_MAX)
-    --p.stages;
-  p.off_x = p.stages * p.stage_bytes;
-  p.off_phi = p.off_x + (int)align16((size_t)NB * a.D_in * 2);
-  p.off_fac = p.off_phi + 2 * NB * PHI_BUF;
-  p.off_misc = p.off_fac + 2 * NB * 16 * 4;
-  p.off_bar = p.off_misc + (int)align16((size_t)MISC_BYTES);
-  p.smem = p.off_bar + (p.stages + 3) * 8 + 1024;
-  p.rowblocks = (a.D_out + ROWS - 1) / ROWS;
-  p.tasks = (long long)p.rowblocks * p.W;
-  p.G = (int)std::min<long long>(p.tasks, cc::sm_count());
-  p.maxc = 1;
-  for (int rb = 0; rb < p.rowblocks; ++rb) {
-    const int c = owner((long long)rb * p.W + p.W - 1, p.tasks, p.G) -
-                  owner((long long)rb * p.W, p.tasks, p.G) + 1;
-    p.maxc = std::max(p.maxc, c);
-  }
-  size_t off = 0;
-  const size_t o_cnt = off;
-  off = cc::align256(off + (size_t)p.rowblocks * 8);
-  const size_t o_part = off;
-  off = cc::align256(off + (size_t)p.rowblocks * p.maxc * NB * ROWS * 4);
-  if (scratch) {
-    uint8_t* base = (uint8_t*)scratch;
-    p.counters = (unsigned long long*)(base + o_cnt);
-    p.part = (float*)(base + o_part);
-  }
-  return off;
-}
-
-}  // namespace kl
-
-// The lanes-along-K kernel takes the layer: ternary weights (basis and base branch alike) in
-// groups of 32..256 codes, code rows of 16-byte multiples, whole 4-float groups of scales per
-// row, and the batch rows' inputs within 64 KB of shared memory.
-static bool kl_supported(const LayerArgs& a, int act_dtype) {
-  using namespace kl;
-  if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
-  if (a.B < 1 || a.B > MAXB || a.D_in < 1 || a.D_out < 1 || a.K < 1) return false;
-  if (a.basis == KAN_JACOBI) return false;
-  if (a.w.format != KAN_W_TERNARY) return false;
-  const int gs = a.w.group_size;
-  if (gs < 32 || gs > 256 || (gs & (gs - 1))) return false;
-  if (a.has_base && (a.wb.format != KAN_W_TERNARY || a.wb.group_size != gs)) return false;
-  auto fits = [&](const cc::RowShape& s) { return s.bytes % 16 == 0 && s.groups % 4 == 0; };
-  if (!fits(cc::row_shape(a.w, a.D_in * a.K))) return false;
-  if (a.has_base && !fits(cc::row_shape(a.wb, a.D_in))) return false;
-  if ((size_t)a.B * a.D_in * 2 > 64 * 1024) return false;
-  auto al = [](const void* ptr) { return ((uintptr_t)ptr & 15) == 0; };
-  if (!al(a.w.data) || !al(a.w.scales)) return false;
-  if (a.has_base && (!al(a.wb.data) || !al(a.wb.scales))) return false;
-  Params p;
-  kl_plan(a, p, nullptr);
-  if (p.smem > cc::SMEM_MAX) return false;
-  return tensor_map_encoder() != nullptr;
-}
-
-unsigned kl::next_epoch() {
-  static std::atomic<unsigned> epoch{0};
-  unsigned e = ++epoch;
-  if (e == 0) e = ++epoch;  // 0 marks a reset counter
-  return e;
-}
-
-static cudaError_t launch_gemv_kl(const LayerArgs& a, int act_dtype, void* scratch,
-                                  cudaStream_t s) {
-  using namespace kl;
-  Params p;
-  kl_plan(a, p, scratch);
-  p.epoch = next_epoch();
-  const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;
-  const cc::RowShape rw = cc::row_shape(a.w, a.D_in * a.K);
-  CUtensorMap cw, sw, cb, sb;
-  if (!kl_make_map(&cw, a.w.data, a.D_out, rw.bytes, WIN_BYTES, true) ||
-      !kl_make_map(&sw, a.w.scales, a.D_out, rw.groups, p.sfl, false))
-    return cudaErrorInvalidValue;
-  cb = cw;
-  sb = sw;
-  if (a.has_base) {
-    const cc::RowShape rbs = cc::row_shape(a.wb, a.D_in);
-    if (!kl_make_map(&cb, a.wb.data, a.D_out, rbs.bytes, WIN_BYTES, true) ||
-        !kl_make_map(&sb, a.wb.scales, a.D_out, rbs.groups, p.sfl, false))
-      return cudaErrorInvalidValue;
-  }
-  const bool fast = (a.w.flags & KAN_WFLAG_TERNARY_NO3) &&
-                    (!a.has_base || (a.wb.flags & KAN_WFLAG_TERNARY_NO3));
-  const KlFn kern = kl_kernel(mode, a.B, fast);
-  cudaError_t e = ensure_smem_attr(kern, cc::SMEM_MAX, kl_configured(kern));
-  if (e != cudaSuccess) return e;
-  if (p.smem > cc::SMEM_MAX) return cudaErrorInvalidValue;
-  note_launch();
-  kern<<<p.G, THREADS, p.smem, s>>>(cw, sw, cb, sb, a, p);
-  return cudaGetLastError();
-}
-
 bool gemv_cc_supported(const LayerArgs& a, int act_dtype) {
   using namespace cc;
-  if (kl_supported(a, act_dtype)) return true;
   if (act_dtype != KAN_F16 && act_dtype != KAN_BF16) return false;
   if (a.B < 1 || a.B > MAXB || a.D_in < 1 || a.D_out < 1 || a.K < 1) return false;
   // the fixed-point basis matrix needs |phi| <= 1: every basis but Jacobi (whose polynomials
@@ -408,26 +238,15 @@ bool gemv_cc_supported(const LayerArgs& a, int act_dtype) {
 }
 
 size_t gemv_cc_scratch_bytes(const LayerArgs& a) {
-  if (kl_supported(a, a.act_dtype)) {
-    kl::Params q;
-    return kl::kl_plan(a, q, nullptr);
-  }
   cc::Params p;
   return cc::plan(a, a.act_dtype, p, nullptr);
 }
 
 int gemv_cc_splits(const LayerArgs& a) {
-  if (kl_supported(a, a.act_dtype)) {
-    kl::Params q;
-    kl::kl_plan(a, q, nullptr);
-    return q.maxc;
-  }
   cc::Params p;
   cc::plan(a, a.act_dtype, p, nullptr);
   return p.S;
 }
-
-int gemv_cc_rows(const LayerArgs& a) { return kl_supported(a, a.act_dtype) ? kl::ROWS : cc::ROWS; }
 
 template <int MODE>
 static void launch_phi(const LayerArgs& a, const cc::Params& p, cudaStream_t s) {
@@ -447,17 +266,8 @@ static void launch_phi(const LayerArgs& a, const cc::Params& p, cudaStream_t s) 
   }
 }
 
-cudaError_t launch_cc_prepass(const LayerArgs& a, int act_dtype, const cc::Params& p,
-                              cudaStream_t s) {
-  if (act_dtype == KAN_F16) launch_phi<MODE_F16>(a, p, s);
-  else launch_phi<MODE_BF16>(a, p, s);
-  note_launch();
-  return cudaGetLastError();
-}
-
 cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s) {
   using namespace cc;
-  if (kl_supported(a, act_dtype)) return launch_gemv_kl(a, act_dtype, scratch, s);
   Params p;
   plan(a, act_dtype, p, scratch);
   const int mode = act_dtype == KAN_F16 ? MODE_F16 : MODE_BF16;

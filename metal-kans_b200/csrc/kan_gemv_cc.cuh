@@ -597,12 +597,6 @@ template <int MODE, int NB>
 MainFn select_main(int fmt, bool fast, int fu);
 
 }  // namespace cc
-
-// The fixed-point basis pre-pass alone (grid: 64-feature blocks x batch rows), for the small-batch
-// kernels that take its matrix (kan_gemv_cc.cu).  Only the pre-pass fields of `p` are read: fmt,
-// fast, units_w / units_b, phi_pitch, rowblocks (counters it resets), the scratch pointers.
-cudaError_t launch_cc_prepass(const LayerArgs& a, int act_dtype, const cc::Params& p,
-                              cudaStream_t s);
 }  // namespace kan
 
 namespace kan {

@@ -63,31 +63,18 @@ cudaError_t launch_tc_pack_pair(const LayerArgs& gate, const LayerArgs& up, int 
 // (kan_tc.cu).
 void* tensor_map_encoder();
 // kan_gemv_cc.cu: small-batch path on the CUDA cores (B <= 4; ternary / INT8 / INT4 weights decoded
-// on chip, integer dot products against a fixed-point basis).  Ternary weights in groups of
-// 32..256 run the lanes-along-K kernel (kan_gemv_kl.cuh, basis evaluated in the kernel); the
-// others the lane-per-row kernel, whose basis pre-pass launch_gemv_cc also runs.  `scratch` holds
-// gemv_cc_scratch_bytes() of device memory, zeroed when allocated.
+// on chip, integer dot products against a fixed-point basis matrix).  launch_gemv_cc also runs the
+// basis pre-pass; `scratch` holds gemv_cc_scratch_bytes() of device memory, zeroed when allocated.
 bool gemv_cc_supported(const LayerArgs& a, int act_dtype);
 size_t gemv_cc_scratch_bytes(const LayerArgs& a);
 int gemv_cc_splits(const LayerArgs& a);
-int gemv_cc_rows(const LayerArgs& a);  // output rows per CTA of the kernel launch_gemv_cc runs
 cudaError_t launch_gemv_cc(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s);
 // kan_gemv.cu: small-batch path for 2-bit packed weights (weights as the MMA M operand, decoded
 // from the packed codes into TMEM; no dense copy)
 // launch_gemv also runs the basis pre-pass into `phi` (gemv_phi_bytes() of device scratch).
-// Ternary layers in groups of 64/128 codes at 5 <= B <= 16 run the 8-bit kernel instead
-// (kan_gemv_i8.cu: codes as signed bytes, the fixed-point basis of the CUDA-core path, per-group
-// int32 accumulators scaled in an epilogue); launch_gemv picks it, `phi` then holds
-// gemv_i8_scratch_bytes().
 bool gemv_supported(const LayerArgs& a, int act_dtype);
 size_t gemv_phi_bytes(const LayerArgs& a);
-int gemv_operand_bits(const LayerArgs& a);  // 8: the 8-bit kernel, 16: the 16-bit one
-int gemv_splits(const LayerArgs& a);
 cudaError_t launch_gemv(const LayerArgs& a, int act_dtype, void* phi, cudaStream_t s);
-bool gemv_i8_supported(const LayerArgs& a, int act_dtype);
-size_t gemv_i8_scratch_bytes(const LayerArgs& a);
-int gemv_i8_splits(const LayerArgs& a);
-cudaError_t launch_gemv_i8(const LayerArgs& a, int act_dtype, void* scratch, cudaStream_t s);
 // kan_backward.cu: fp32 layer backward (Chebyshev, RBF, B-spline bases; raw input)
 bool backward_supported(const BackwardArgs& a);
 cudaError_t launch_backward(const BackwardArgs& a, cudaStream_t s);

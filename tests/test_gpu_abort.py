@@ -1,4 +1,4 @@
-"""GPU: the bounded-wait abort path of the tensor-core kernel and of the small-batch kernel.
+"""GPU: the tensor-core kernel's bounded-wait abort path.
 
 Every pipeline wait of the kernel (a stage filled or freed by another warp role) has a limit; on
 expiry the kernel sets the device error word, skips its remaining work, still waits (with the
@@ -13,11 +13,10 @@ import numpy as np
 import pytest
 
 from kan_cases import TOL, layer_err, make_layer, set_mode
-from oracle import kan_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TC, CC = 2, 4
+TC = 2
 
 # (basis, mode, D_in, D_out, K, B, input map, expected (BN, splits))
 CASES = [
@@ -58,37 +57,3 @@ def test_short_wait_limit_aborts_and_recovers(case):
     assert code.value == 0
     err = layer_err(y, layer, x, mode, basis)
     assert err <= TOL[mode], f"after the aborted call: max-rel-err {err:.3e}"
-
-
-def test_small_batch_kernel_aborts_and_recovers():
-    """The lanes-along-K small-batch kernel (ternary weights, B <= 4).  Its waits are short (the
-    stages land while the warps build a window's basis, and the eight warps reach each basis
-    barrier together), so a limit below 16 cycles makes its first basis wait use a barrier that
-    nothing completes: the wait expires, the call reports the timeout, and the next call with the
-    default limit matches the oracle."""
-    import ctypes
-
-    import metal_kans as mk
-    from metal_kans.device import KanError
-
-    layer = make_layer("cheby", 2048, 1024, 9, seed=4)
-    mk.to_ternary(layer, group_size=64)
-    layer.bfloat16()
-    x = np.random.default_rng(6).normal(0, 1, (2, 2048)).astype(O.act_dtype("bf16"))
-    lib = mk.get_metal_bridge()
-    keep = []
-    info = (ctypes.c_int * 6)()
-    lib.kan_forward_plan(ctypes.byref(layer._descriptor(keep)), 2, CC, info)
-    assert (info[0], info[1]) == (CC, 128), list(info)
-    lib.kan_set_wait_limit(1)
-    try:
-        with pytest.raises(KanError, match="bounded wait"):
-            layer.forward(x, path=CC)
-    finally:
-        lib.kan_set_wait_limit(0)
-    code = ctypes.c_int(0)
-    lib.kan_device_error(ctypes.byref(code))
-    assert code.value == 0
-    y = layer.forward(x, path=CC)
-    err = layer_err(y, layer, x, "bf16", "cheby")
-    assert err <= TOL["bf16"], f"after the aborted call: max-rel-err {err:.3e}"

@@ -1,11 +1,6 @@
 """GPU: the CUDA-core small-batch path (B <= 4) for ternary / INT8 / INT4 weights.
 
-Two kernels serve it: ternary weights in groups of 32..256 codes run the lanes-along-K kernel
-(basis evaluated in the kernel, 128 rows per CTA, the row blocks' partials summed by their last
-contributor); INT8/INT4 and ternary weights in groups of 16 the lane-per-row kernel after its
-basis pre-pass (32 rows per CTA).  The plan's rows per CTA name the kernel each case runs.
-
-Neither kernel expands the packed codes: it decodes them on chip into bytes and takes integer
+The kernel never expands the packed codes: it decodes them on chip into bytes and takes integer
 dot products against a fixed-point copy of the basis values (two signed bytes per value, exact
 for every operand-dtype value of magnitude >= 2^-6), scaling each 16-code sum by its group's
 scale.  Ternary weights come out exactly as the reference's dequantiser rounded to the operand
@@ -56,15 +51,7 @@ CASES = [
     ("ternary", "f16", "fourier", 9, 1024, 96, 4, 64, True, True, "none"),
     ("int8", "bf16", "relu", 5, 1024, 64, 1, 64, True, False, "none"),
     ("int4", "f16", "fourier", 5, 1024, 160, 3, 32, False, True, "none"),
-    ("ternary", "bf16", "cheby", 9, 1024, 256, 2, 16, True, True, "none"),       # lane per row
-    ("ternary", "f16", "rbf", 8, 1024, 300, 3, 256, True, True, "none"),         # groups of 256
-    # 157 row blocks of 2 windows on at most 148 CTAs: some CTAs finish whole row blocks alone
-    ("ternary", "bf16", "cheby", 3, 256, 20000, 2, 64, True, True, "none"),
 ]
-
-
-def _rows_per_cta(fmt, gs):
-    return 128 if fmt == "ternary" and 32 <= gs <= 256 else 32
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: "-".join(map(str, c)))
@@ -78,9 +65,7 @@ def test_cc_matches_oracle_and_tc(case):
         randomize_bias(layer)
     _quantize(mk, layer, fmt, gs)
     set_mode(layer, mode)
-    plan = _plan(mk, layer, B)
-    assert plan[0] == CC  # the automatic choice for B <= 4
-    assert plan[1] == _rows_per_cta(fmt, gs), plan
+    assert _plan(mk, layer, B)[0] == CC  # the automatic choice for B <= 4
     x = np.random.default_rng(d_out).normal(0, 1, (B, d_in)).astype(O.act_dtype(mode))
     y = layer.forward(x, path=CC)
     # INT8/INT4: this path multiplies by the exact fp32 dequantised weight (q * scale + minimum),
@@ -132,7 +117,7 @@ def test_cc_c5_layer(c5_layer, B):
 
     fmt, l = c5_layer
     plan = _plan(mk, l, B)
-    assert plan[0] == CC and plan[2] > 1 and plan[1] == _rows_per_cta(fmt, 64), plan
+    assert plan[0] == CC and plan[2] > 1, plan
     x = np.random.default_rng(B).uniform(-1, 1, (B, 4096)).astype(O.act_dtype("bf16"))
     y = l.forward(x)
     err = layer_err(y, l, x, "bf16", "cheby", exact_weights=fmt != "ternary")
@@ -144,7 +129,7 @@ def test_cc_c5_layer(c5_layer, B):
 @pytest.mark.parametrize("B", [1, 3])
 def test_cc_ternary_code3(gs, B):
     """Ternary codes equal to 3 (which the reference's dequantiser maps to 0): the byte-permute
-    decoders of both kernels, against the oracle on the layer's own dequantised weights."""
+    decoder, against the oracle on the layer's own dequantised weights."""
     import metal_kans as mk
 
     layer = make_layer("cheby", 1024, 384, 9, seed=gs + B)
@@ -160,8 +145,7 @@ def test_cc_ternary_code3(gs, B):
         words |= np.where(hit, np.uint32(3) << (2 * field), np.uint32(0)).astype(np.uint32)
         assert not pk._no_code3()
     set_mode(layer, "bf16")
-    plan = _plan(mk, layer, B)
-    assert plan[0] == CC and plan[1] == _rows_per_cta("ternary", gs), plan
+    assert _plan(mk, layer, B)[0] == CC
     x = np.random.default_rng(B).normal(0, 1, (B, 1024)).astype(O.act_dtype("bf16"))
     y = layer.forward(x)
     # the layer's weight attributes hold the dequantised copies made before the edit: the oracle
