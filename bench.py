@@ -493,8 +493,6 @@ def plan_of(mk, layers, B):
             e.update(row_blocks=info[3])
         elif info[0] == 4:
             e.update(row_blocks=info[3], splits=info[2])
-        elif info[0] == 1 and info[2]:
-            e.update(kernel="split-K fp32, 64x64 tiles", cluster=info[2])
         out.append(e)
     return out
 

@@ -377,10 +377,8 @@ int kan_forward_path(const kan_layer* layer, const void* X, void* Y, int B, int 
  * KAN_PATH_AUTO), and for the tensor-core path info[1] = tile width BN, info[2] = split-K factor
  * (cluster size), info[3] = M tiles, info[4] = N tiles, info[5] = 64-column K blocks; for the
  * tensor-core small-batch path info[3] = 128-row blocks; for the CUDA-core small-batch path
- * info[2] = K splits, info[3] = 32-row blocks; for the CUDA-core path info[2] = the cluster size
- * of the split-K fp32 kernel (dense fp32 layers of >= 256 rows and short K: 64 x 64 output tiles,
- * input features split over the cluster), 0 for the tile kernels.  Tests and benchmarks use it to
- * name the plan they check.  info must hold 6 ints. */
+ * info[2] = K splits, info[3] = 32-row blocks.  Tests and benchmarks use it to name the plan they
+ * check.  info must hold 6 ints. */
 int kan_forward_plan(const kan_layer* layer, int B, int path, int* info);
 /* No counterpart in the reference.  Limit of the tensor-core kernel's pipeline waits (a stage
  * filled or freed by another warp role), in SM clock cycles, for the launches that follow on any

@@ -445,9 +445,7 @@ int kan_forward_plan(const kan_layer* layer, int B, int path, int* info) {
                   "forward_plan: the layer does not fit the CUDA-core small-batch path");
     info[2] = gemv_cc_splits(a);
     info[3] = (layer->D_out + 31) / 32;
-  } else if (path == KAN_PATH_SIMT) {
-    info[2] = simt_splits(a, layer->act_dtype);
-  } else {
+  } else if (path != KAN_PATH_SIMT) {
     return fail(KAN_ERR_ARG, "forward_plan: unknown path %d", path);
   }
   return KAN_OK;

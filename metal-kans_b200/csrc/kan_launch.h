@@ -45,8 +45,6 @@ int* device_error_ptr();
 
 // kan_simt.cu
 cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s);
-// Cluster size of the split-K fp32 kernel launch_simt runs for the layer (0: the tile kernels).
-int simt_splits(const LayerArgs& a, int act_dtype);
 // kan_tc.cu: the tensor-core path.  tc_plan() picks the tile width and the split-K factor (the
 // split CTAs of a tile form a cluster and reduce through distributed shared memory);
 // launch_tc() needs a.tc_weights (the packed layout).

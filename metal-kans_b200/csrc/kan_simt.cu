@@ -427,198 +427,6 @@ static cudaError_t launch_dense_bn(const LayerArgs& a, cudaStream_t s) {
   }
 }
 
-// ---------------------------------------------------------------------------------------------
-// Dense fp32 layers with short K and many rows (config 1: 1024 rows, 64 -> 64, 9 terms): the
-// output in 64 x 64 tiles, each computed by a thread-block cluster of S CTAs (S = 1, 2, 4 or 8)
-// that split the input features between them.
-//
-// A CTA builds the basis values of its Fs = ceil(D_in / S) features for the tile's 64 rows and
-// copies the matching weight slice, both k-major in shared memory (A[k][row], W[k][col], k over
-// the slice's Fs * K basis columns then its Fs base columns), so that a thread's 4 x 4 outputs
-// take one float4 of each per k (16 FMAs per two loads).  The S partial tiles are then added
-// through distributed shared memory: CTA z of the cluster finishes rows [z * 64 / S, ...) by
-// reading every CTA's partial of them in cluster-rank order (deterministic), adds the bias and
-// stores.  No global scratch: this path allocates nothing.  Two cluster barriers (partials
-// published; all remote reads done before any CTA exits) are reached unconditionally by every
-// thread of every CTA.
-// ---------------------------------------------------------------------------------------------
-constexpr int SG_TILE = 64;
-constexpr int SG_THREADS = 256;
-constexpr int SG_KMAX = 256;  // slice columns a CTA holds (A and W: 2 x 64 KB at the limit)
-constexpr int SG_MAXS = 8;
-
-__device__ __forceinline__ void sg_cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-__device__ __forceinline__ float sg_ld_rank(const float* local, uint32_t rank) {
-  uint32_t addr = (uint32_t)__cvta_generic_to_shared(local), remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(addr), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
-}
-
-template <int BASIS>
-__global__ void __launch_bounds__(SG_THREADS) kan_simt_splitk_kernel(LayerArgs a, int S, int Fs) {
-  using Gen = typename GenFor<BASIS, MODE_F32>::type;
-  extern __shared__ __align__(16) float sg_smem[];
-  const int KT = a.K + (a.has_base ? 1 : 0);
-  const int KS = Fs * KT;                     // slice columns
-  const int arows = KS > SG_TILE ? KS : SG_TILE;
-  float* A = sg_smem;                         // [arows][64]: basis, later the partial tile
-  float* Wt = sg_smem + arows * SG_TILE;      // [KS][64]
-  __shared__ float s_mean[SG_TILE], s_rstd[SG_TILE];
-  const int tid = threadIdx.x;
-  const int col0 = blockIdx.x * SG_TILE, row0 = blockIdx.y * SG_TILE;
-  uint32_t z;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(z));
-  const int f0 = (int)z * Fs;                 // this CTA's first input feature
-  const int nf = max(0, min(Fs, a.D_in - f0));
-  const float* X = (const float*)a.X;
-  const float* W = (const float*)a.w.data;
-  const float* Wb = (const float*)a.wb.data;
-  const int Kw = a.D_in * a.K;
-
-  // weight slice, transposed into Wt[k][col]: basis columns (f0 + fl) * K + k, then base columns
-  for (int it = tid; it < SG_TILE * KS; it += SG_THREADS) {
-    const int n = it % SG_TILE, kk = it / SG_TILE;
-    const int col = col0 + n;
-    float v = 0.f;
-    if (col < a.D_out) {
-      if (kk < Fs * a.K) {
-        const int fl = kk / a.K;
-        if (fl < nf) v = W[(size_t)col * Kw + (size_t)(f0 + fl) * a.K + (kk - fl * a.K)];
-      } else {
-        const int fl = kk - Fs * a.K;
-        if (fl < nf) v = Wb[(size_t)col * a.D_in + f0 + fl];
-      }
-    }
-    Wt[kk * SG_TILE + n] = v;
-  }
-  if (a.input_map == KAN_MAP_LAYERNORM) row_stats<MODE_F32>(a, row0, SG_TILE, s_mean, s_rstd);
-  __syncthreads();
-  // basis values of the slice, A[k][row]; rows past B and features past D_in give zeros
-  for (int it = tid; it < SG_TILE * Fs; it += SG_THREADS) {
-    const int r = it % SG_TILE, fl = it / SG_TILE;
-    const int row = row0 + r;
-    const bool ok = row < a.B && fl < nf;
-    Gen g;
-    float xm = 0.f;
-    if (ok) {
-      const float mean = a.input_map == KAN_MAP_LAYERNORM ? s_mean[r] : 0.f;
-      const float rstd = a.input_map == KAN_MAP_LAYERNORM ? s_rstd[r] : 1.f;
-      xm = map_input<MODE_F32>(X[(size_t)row * a.D_in + f0 + fl], a.input_map, mean, rstd);
-      g.init(xm, f0 + fl, a);
-    }
-    for (int k = 0; k < a.K; ++k) A[(fl * a.K + k) * SG_TILE + r] = ok ? g.next() : 0.f;
-    if (a.has_base) A[(Fs * a.K + fl) * SG_TILE + r] = ok ? silu_value<MODE_F32>(xm) : 0.f;
-  }
-  __syncthreads();
-
-  // 4 x 4 outputs per thread: rows 4 ty.., columns 4 tx..
-  const int tx = tid & 15, ty = tid >> 4;
-  float acc[4][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-#pragma unroll 4
-  for (int k = 0; k < KS; ++k) {
-    const float4 av = *reinterpret_cast<const float4*>(A + k * SG_TILE + 4 * ty);
-    const float4 wv = *reinterpret_cast<const float4*>(Wt + k * SG_TILE + 4 * tx);
-    const float ar[4] = {av.x, av.y, av.z, av.w}, wr[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], wr[j], acc[i][j]);
-  }
-  __syncthreads();  // every thread is done with A before it holds the partial tile
-  float* P = A;     // [64][64] partial tile of this CTA
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    *reinterpret_cast<float4*>(P + (4 * ty + i) * SG_TILE + 4 * tx) =
-        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-  sg_cluster_sync();  // every partial tile of the cluster is published
-
-  // this CTA's rows of the tile: the S partials in rank order, bias, store
-  const int rb = SG_TILE / S;
-  float* Y = (float*)a.Y;
-  const float* bias = (const float*)a.bias;
-  for (int o = tid; o < rb * SG_TILE; o += SG_THREADS) {
-    const int r = (int)z * rb + o / SG_TILE, c = o % SG_TILE;
-    float v = 0.f;
-    for (int zz = 0; zz < S; ++zz) v += sg_ld_rank(P + r * SG_TILE + c, (uint32_t)zz);
-    const int row = row0 + r, col = col0 + c;
-    if (row < a.B && col < a.D_out) {
-      if (a.has_bias) v += bias[col];
-      Y[(size_t)row * a.D_out + col] = v;
-    }
-  }
-  sg_cluster_sync();  // no CTA leaves while another still reads its partial tile
-}
-
-// Cluster size and features per CTA of the split-K kernel, 0 when the layer is not for it: dense
-// fp32 weights, at least 256 rows (64-row tiles), a slice of at most SG_KMAX columns, and S as
-// large as fills about two CTAs per SM.
-static int splitk_plan(const LayerArgs& a, int* Fs_out) {
-  if (a.w.format != KAN_W_DENSE || (a.has_base && a.wb.format != KAN_W_DENSE)) return 0;
-  if (a.B < 256 || a.D_out < 32 || a.D_in < 1 || a.K < 1) return 0;
-  const int KT = a.K + (a.has_base ? 1 : 0);
-  const long long tiles =
-      (long long)((a.B + SG_TILE - 1) / SG_TILE) * ((a.D_out + SG_TILE - 1) / SG_TILE);
-  for (int S = SG_MAXS; S >= 1; S >>= 1) {
-    const int Fs = (a.D_in + S - 1) / S;
-    if (S > 1 && tiles * S > 2 * 148) continue;   // enough CTAs with fewer splits
-    if (S > 1 && (long long)(S / 2) * Fs >= a.D_in) continue;  // the last CTAs would be idle
-    if (Fs * KT > SG_KMAX) return 0;               // too long a slice even at this S
-    *Fs_out = Fs;
-    return S;
-  }
-  return 0;
-}
-
-int simt_splits(const LayerArgs& a, int act_dtype) {
-  int Fs = 0;
-  return act_dtype == KAN_F32 ? splitk_plan(a, &Fs) : 0;
-}
-
-template <int BASIS>
-static cudaError_t launch_splitk_basis(const LayerArgs& a, int S, int Fs, cudaStream_t s) {
-  const int KS = Fs * (a.K + (a.has_base ? 1 : 0));
-  const int smem = ((KS > SG_TILE ? KS : SG_TILE) + KS) * SG_TILE * (int)sizeof(float);
-  static std::atomic<unsigned long long> configured{0};
-  cudaError_t e = ensure_smem_attr(kan_simt_splitk_kernel<BASIS>,
-                                   2 * SG_KMAX * SG_TILE * (int)sizeof(float), configured);
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.D_out + SG_TILE - 1) / SG_TILE),
-                     (unsigned)((a.B + SG_TILE - 1) / SG_TILE), (unsigned)S);
-  cfg.blockDim = dim3(SG_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = (unsigned)S;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kan_simt_splitk_kernel<BASIS>, a, S, Fs);
-}
-
-static cudaError_t launch_splitk(const LayerArgs& a, int S, int Fs, cudaStream_t s) {
-  switch (BasisOf(a)) {
-    case KAN_CHEBY: return launch_splitk_basis<KAN_CHEBY>(a, S, Fs, s);
-    case KAN_RBF: return launch_splitk_basis<KAN_RBF>(a, S, Fs, s);
-    case KAN_BSPLINE: return launch_splitk_basis<KAN_BSPLINE>(a, S, Fs, s);
-    case KAN_WAVELET: return launch_splitk_basis<KAN_WAVELET>(a, S, Fs, s);
-    case KAN_RELU: return launch_splitk_basis<KAN_RELU>(a, S, Fs, s);
-    case KAN_FOURIER: return launch_splitk_basis<KAN_FOURIER>(a, S, Fs, s);
-    default: return launch_splitk_basis<KAN_JACOBI>(a, S, Fs, s);
-  }
-}
-
 // The streamed-panel kernel takes dense fp32 layers whose weight rows start on 16-byte
 // boundaries (D_in * K and D_in multiples of 4, aligned base pointers).
 static bool dense_f32_ok(const LayerArgs& a) {
@@ -630,9 +438,6 @@ static bool dense_f32_ok(const LayerArgs& a) {
 
 cudaError_t launch_simt(const LayerArgs& a, int act_dtype, cudaStream_t s) {
   note_launch();
-  int Fs = 0;
-  const int S = act_dtype == KAN_F32 ? splitk_plan(a, &Fs) : 0;
-  if (S > 0) return launch_splitk(a, S, Fs, s);
   if (act_dtype == KAN_F32 && dense_f32_ok(a)) {
     const long long wide = (long long)((a.D_out + 63) / 64) * ((a.B + DN_BM - 1) / DN_BM);
     return wide < 148 ? launch_dense_bn<32>(a, s) : launch_dense_bn<64>(a, s);
