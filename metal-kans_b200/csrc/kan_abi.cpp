@@ -93,7 +93,8 @@ struct DeviceState {
   std::vector<Scratch*> scratch;        // one per stream that ran the engine
   // kan_forward_host: copy streams (host->device, device->host) and per-chunk events
   cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t ev_in[2] = {}, ev_done[2] = {};
+  static constexpr int kMaxChunks = 4;  // kan_forward_host: copy/compute overlap chunks
+  cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
 };
 
 static DeviceState g_dev[MAX_DEVICES];
@@ -471,7 +472,7 @@ int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!d->h2d) {
       KAN_CUDA_TRY(cudaStreamCreateWithFlags(&d->d2h, cudaStreamNonBlocking));
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < DeviceState::kMaxChunks; ++c) {
         KAN_CUDA_TRY(cudaEventCreateWithFlags(&d->ev_in[c], cudaEventDisableTiming));
         KAN_CUDA_TRY(cudaEventCreateWithFlags(&d->ev_done[c], cudaEventDisableTiming));
       }
@@ -483,13 +484,17 @@ int kan_forward_host(const kan_layer* layer, const void* X, void* Y, int B) {
   void *dX, *dY;
   if ((rc = scratch_buf(d, d->stream, SC_HX, (size_t)B * xrow, false, &dX))) return rc;
   if ((rc = scratch_buf(d, d->stream, SC_HY, (size_t)B * yrow, false, &dY))) return rc;
-  // two chunks (at a 128-row boundary) once the copies are worth overlapping: the second
-  // chunk's input crosses the link while the first computes, the first chunk's result returns
-  // while the second computes
-  const int nc = (B >= 2048 && (size_t)B * (xrow + yrow) >= ((size_t)2 << 20)) ? 2 : 1;
-  const int rows0 = nc == 2 ? (B / 2 + 127) / 128 * 128 : B;
+  // chunks (at 128-row boundaries) once the copies are worth overlapping: chunk c + 1's input
+  // crosses the link while chunk c computes, and chunk c's result returns while chunk c + 1
+  // computes, so only the first input and the last result copy stay exposed.  Four chunks from
+  // 32768 rows (each still fills the GPU with row tiles), two from 2048 rows and 2 MB of copies.
+  const bool big = (size_t)B * (xrow + yrow) >= ((size_t)2 << 20);
+  const int nc = (big && B >= 32768) ? DeviceState::kMaxChunks : ((big && B >= 2048) ? 2 : 1);
+  const int per = (B / nc + 127) / 128 * 128;
   for (int c = 0; c < nc; ++c) {
-    const int r0 = c == 0 ? 0 : rows0, rows = c == 0 ? rows0 : B - rows0;
+    const int r0 = std::min(B, c * per);
+    const int rows = c == nc - 1 ? B - r0 : std::min(per, B - r0);
+    if (rows <= 0) break;
     const char* xs = (const char*)X + (size_t)r0 * xrow;
     char* xd = (char*)dX + (size_t)r0 * xrow;
     char* yd = (char*)dY + (size_t)r0 * yrow;
