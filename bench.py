@@ -60,7 +60,7 @@ TRAFFIC = {
     "c5:ternary:1": {"bytes": 52557312 + 40448,
                      "src": "profiles/kan_gemv_cc_kernel_c5_ternary_bf16_b1.md",
                      "note": "the main kernel; the pre-pass reads 40 KB"},
-    "c5:ternary:65536": {"bytes": 5865144576 + 527921408,
+    "c5:ternary:65536": {"bytes": 5892764672 + 527818752,
                          "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b65536.md"},
 }
 
