@@ -421,10 +421,29 @@ class Clocks:
                 "reasons": [n for n, bit in self.NAMES if self.reasons & bit]}
 
 
+def blas_on_all_cores():
+    """A context in which NumPy's BLAS uses every host core of this process (torchrun sets
+    OMP_NUM_THREADS=1 when it starts several processes), and that thread count."""
+    import contextlib
+
+    cores = len(os.sched_getaffinity(0))
+    try:
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=cores, user_api="blas"), cores
+    except Exception:
+        return contextlib.nullcontext(), int(os.environ.get("OMP_NUM_THREADS", cores))
+
+
 def cpu_sample(w, budget_s, min_calls=1):
     """Time the CPU restatement of the reference path on a bounded row sample of the workload
     (threads: NumPy's BLAS on every host core of this process)."""
-    cores = len(os.sched_getaffinity(0))
+    ctx, cores = blas_on_all_cores()
+    with ctx:
+        return _cpu_sample(w, budget_s, min_calls, cores)
+
+
+def _cpu_sample(w, budget_s, min_calls, cores):
     sample = min(w.B, 512)
     xs = w.rows(0, sample)
     w.cpu(xs)  # warm-up (also builds cached dequantised weights)
@@ -740,15 +759,16 @@ def reference_arm(args, rank, world):
     w = get_spec(args.config, args.rows)
     sample = min(w.B, 512)
     xs = w.rows(0, sample)
-    for _ in range(args.warmup):
-        w.cpu(xs)
-    steps, t0 = 0, time.perf_counter()
-    while steps < args.steps and (steps < 1 or time.perf_counter() - t0 < 120.0):
-        w.cpu(xs)
-        steps += 1
-    dt = time.perf_counter() - t0
+    ctx, cores = blas_on_all_cores()
+    with ctx:
+        for _ in range(args.warmup):
+            w.cpu(xs)
+        steps, t0 = 0, time.perf_counter()
+        while steps < args.steps and (steps < 1 or time.perf_counter() - t0 < 120.0):
+            w.cpu(xs)
+            steps += 1
+        dt = time.perf_counter() - t0
     value = steps * sample / dt
-    cores = len(os.sched_getaffinity(0))
     note = getattr(w, "cpu_note", "")
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / steps,
