@@ -231,3 +231,18 @@ def test_torch_module(mk, dtype):
     assert O.max_rel_err(y.detach().float().cpu().numpy(), ref.astype(np.float32)) <= TOL[mode]
     net = mk.TorchMetalKAN([4, 8, 2], basis="cheby", degree=3).cuda()
     assert net(torch.randn(10, 4)).shape == (10, 2)  # CPU input -> CPU output
+
+
+@pytest.mark.parametrize("B", [2500, 40000])
+def test_host_forward_chunks(mk, B):
+    """kan_forward_host (what layer(x) calls on host arrays) overlaps copies and kernels in two
+    chunks from 2048 rows and four from 32768 (ragged last chunk here): every row of the result is
+    the layer's, checked against the oracle on rows from each chunk."""
+    np.random.seed(B)
+    layer = mk.ChebyKAN(512, 256, degree=5).bfloat16()
+    x = np.random.default_rng(B).uniform(-1, 1, (B, 512)).astype(O.act_dtype("bf16"))
+    y = layer(x)
+    assert y.shape == (B, 256)
+    rows = np.unique(np.linspace(0, B - 1, 40).astype(int))
+    err = layer_err(y[rows], layer, x[rows], "bf16", "cheby")
+    assert err <= TOL["bf16"], f"max rel err {err:.3g}"
