@@ -51,6 +51,9 @@ TOL = {"f32": 1e-5, "f16": 2e-3, "bf16": 2e-3}
 TRAFFIC = {
     "c1": {"bytes": 451328, "src": "profiles/kan_simt_dense_kernel_c1_cheby_fp32_b1024.md"},
     "c2": {"bytes": 3386368, "src": "profiles/kan_tc_kernel_c2_fastkan_fp16_b4096.md"},
+    "c4": {"bytes": 2487623424 + 234930432,
+           "src": "profiles/kan_tc_kernel_c4_gated_int4_bf16_t16384.md",
+           "note": "both launches of a step: gate + up pair, then down"},
     "c3": {"bytes": 20276992, "src": "profiles/kan_tc_kernel_c3_bspline_fp16_b8192.md",
            "note": "first (largest) of the net's three launches"},
     "c5:ternary:4096": {"bytes": 470647552 + 23311616,
