@@ -44,7 +44,8 @@ METRIC = "fused KAN layer rows/sec at 1/2/4/8 B200; % tensor-pipe or HBM rooflin
 DEFAULT_CONFIG = "c5:ternary:65536"
 TOL = {"f32": 1e-5, "f16": 2e-3, "bf16": 2e-3}
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel, each
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per step, like roofline.achieved: the
+# step's one launch, or the sum of its launches for the nets (c3) and the GatedKAN block (c4); each
 # from an ncu capture summarised under profiles/ (file named per entry).  `scale` > 1: captured on
 # a smaller batch of the same layer and scaled by the rows processed (the summary says why that
 # holds); the line reports the scale.
@@ -54,8 +55,9 @@ TRAFFIC = {
     "c4": {"bytes": 2487623424 + 234930432,
            "src": "profiles/kan_tc_kernel_c4_gated_int4_bf16_t16384.md",
            "note": "both launches of a step: gate + up pair, then down"},
-    "c3": {"bytes": 20276992, "src": "profiles/kan_tc_kernel_c3_bspline_fp16_b8192.md",
-           "note": "first (largest) of the net's three launches"},
+    "c3": {"bytes": 20276992 + 768 + 13337344 + 6144 + 8579072,
+           "src": "profiles/kan_tc_kernel_c3_bspline_fp16_b8192.md",
+           "note": "the net's three launches of a step"},
     "c5:ternary:4096": {"bytes": 470647552 + 23311616,
                         "src": "profiles/kan_tc_kernel_c5_ternary_bf16_b4096.md"},
     "c5:ternary:16": {"bytes": 53773568 + 152064,
