@@ -151,19 +151,27 @@ template <int MODE>
 struct BsplineGen {
   float b0, b1, b2, b3;
   int span, k;
-  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+  // The four nonzero terms (before rounding to the operand dtype) and the span of a mapped input.
+  __device__ __forceinline__ static void terms(float xm, const LayerArgs& a, float& t0, float& t1,
+                                               float& t2, float& t3, int& s) {
     float pos = (xm - a.grid_min) * a.inv_h;
     float fl = floorf(pos);
-    int s = (int)fminf(fmaxf(fl, 0.0f), (float)(a.grid_size - 1));
+    s = (int)fminf(fmaxf(fl, 0.0f), (float)(a.grid_size - 1));
     float u = fminf(fmaxf(pos - (float)s, 0.0f), 1.0f);
     float om = 1.0f - u;
     const float inv6 = 1.0f / 6.0f;
     float u2 = u * u, u3 = u2 * u;
-    b0 = Act<MODE>::round(om * om * om * inv6);
-    b1 = Act<MODE>::round((3.0f * u3 - 6.0f * u2 + 4.0f) * inv6);
-    b2 = Act<MODE>::round((-3.0f * u3 + 3.0f * u2 + 3.0f * u + 1.0f) * inv6);
-    b3 = Act<MODE>::round(u3 * inv6);
-    span = s;
+    t0 = om * om * om * inv6;
+    t1 = (3.0f * u3 - 6.0f * u2 + 4.0f) * inv6;
+    t2 = (-3.0f * u3 + 3.0f * u2 + 3.0f * u + 1.0f) * inv6;
+    t3 = u3 * inv6;
+  }
+  __device__ __forceinline__ void init(float xm, int, const LayerArgs& a) {
+    terms(xm, a, b0, b1, b2, b3, span);
+    b0 = Act<MODE>::round(b0);
+    b1 = Act<MODE>::round(b1);
+    b2 = Act<MODE>::round(b2);
+    b3 = Act<MODE>::round(b3);
     k = 0;
   }
   __device__ __forceinline__ float next() {

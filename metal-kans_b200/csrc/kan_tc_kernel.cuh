@@ -539,6 +539,13 @@ struct RowProducer {
 #pragma unroll
       for (int f = 0; f < F; ++f) xm[f] = xs[f];
     }
+    if constexpr (BASIS == KAN_BSPLINE && K == 8) produce_bspline8(a_stage, r, xm, a);
+    else produce_terms(a_stage, r, xm, blk, a);
+  }
+
+  // Every basis: the row's 64 terms in fp32 registers, rounded and packed in pairs.
+  __device__ __forceinline__ void produce_terms(uint8_t* a_stage, int r, const float (&xm)[F],
+                                                int blk, const LayerArgs& a) {
     float v[64];
 #pragma unroll
     for (int f = 0; f < F; ++f) {
@@ -611,7 +618,63 @@ struct RowProducer {
       *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) = pk;
     }
   }
+
+  // Cubic B-splines, K = 8: only the four terms at the span are nonzero.  They are rounded to the
+  // operand dtype and packed as four 16-bit halves (the same values the generic path stores), moved
+  // to their span by one 64-bit shift -- the feature's eight terms as four 32-bit words -- and
+  // merged into the row's 32 words at the feature's column (odd columns by a 16-bit funnel shift).
+  // No per-term selects and no fp32 staging of the row.
+  __device__ __forceinline__ void produce_bspline8(uint8_t* a_stage, int r, const float (&xm)[F],
+                                                   const LayerArgs& a) {
+    uint32_t w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = 0u;
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const int p = f * KT;  // first column of the feature
+      float t0, t1, t2, t3;
+      int span;
+      BsplineGen<MODE>::terms(xm[f], a, t0, t1, t2, t3, span);
+      const unsigned long long v =
+          ((unsigned long long)pack2<MODE>(t2, t3) << 32) | (unsigned long long)pack2<MODE>(t0, t1);
+      const int sh = 16 * span;
+      unsigned long long lo = 0ull, hi = 0ull;
+      if (sh < 0) {
+        lo = sh > -64 ? v >> (-sh) : 0ull;
+      } else if (sh < 64) {
+        lo = v << sh;
+        hi = sh ? v >> (64 - sh) : 0ull;
+      } else if (sh < 128) {
+        hi = v << (sh - 64);
+      }
+      const uint32_t q0 = (uint32_t)lo, q1 = (uint32_t)(lo >> 32);
+      const uint32_t q2 = (uint32_t)hi, q3 = (uint32_t)(hi >> 32);
+      if ((p & 1) == 0) {
+        w[p / 2] |= q0;
+        w[p / 2 + 1] |= q1;
+        w[p / 2 + 2] |= q2;
+        w[p / 2 + 3] |= q3;
+      } else {
+        const int b = p / 2;
+        w[b] |= q0 << 16;
+        w[b + 1] |= __funnelshift_l(q0, q1, 16);
+        w[b + 2] |= __funnelshift_l(q1, q2, 16);
+        w[b + 3] |= __funnelshift_l(q2, q3, 16);
+        w[b + 4] |= q3 >> 16;
+      }
+      if (HB) {
+        const uint32_t hs = pack2<MODE>(silu_value<MODE>(xm[f]), 0.f) & 0xFFFFu;
+        const int ps = p + K;
+        w[ps / 2] |= (ps & 1) ? (hs << 16) : hs;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(a_stage + a_chunk_off(r, j)) =
+          make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  }
 };
+
 
 // Runtime K (any K + has_base <= 64): zero the row, then 2-byte stores of the computed terms.
 template <int BASIS, int MODE>
