@@ -675,7 +675,6 @@ struct RowProducer {
   }
 };
 
-
 // Runtime K (any K + has_base <= 64): zero the row, then 2-byte stores of the computed terms.
 template <int BASIS, int MODE>
 struct RowProducerAnyK {
