@@ -55,7 +55,7 @@ TRAFFIC = {
     "c4": {"bytes": 2487623424 + 234930432,
            "src": "profiles/kan_tc_kernel_c4_gated_int4_bf16_t16384.md",
            "note": "both launches of a step: gate + up pair, then down"},
-    "c3": {"bytes": 20276992 + 768 + 13337344 + 6144 + 8579072,
+    "c3": {"bytes": 20279296 + 512 + 13347328 + 16128 + 8580608,
            "src": "profiles/kan_tc_kernel_c3_bspline_fp16_b8192.md",
            "note": "the net's three launches of a step"},
     "c5:ternary:4096": {"bytes": 470647552 + 23311616,
